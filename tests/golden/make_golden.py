@@ -1,0 +1,269 @@
+#!/usr/bin/env python3
+"""Generate the golden fixtures in this directory by running the REFERENCE.
+
+This script imports HydraNet itself (read-only) and records what the
+reference computes on seeded synthetic inputs: its packer, its dequantiser,
+its two routers and its MoE layers in dequant mode.  The fixtures pin the
+numpy oracle under ``oracle/``; the GPU box never runs this script (the
+reference is not there), it only reads the committed ``.npz`` files.
+
+Usage (from the repository root)::
+
+    python tests/golden/make_golden.py --reference <path to the hydranet checkout>
+
+The reference checkout is exposed to Python as a package named ``hydranet``
+through a symlink in a temporary directory.
+
+Large weights are not stored: they are regenerated from their seed with
+numpy's PCG64 stream (``hydranet_b200/synth.py``) and pinned by the SHA-256 of
+the packed expert blobs the reference packer produced.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+
+from hydranet_b200 import synth  # noqa: E402
+
+
+def import_reference(ref: Path):
+    tmp = Path(tempfile.mkdtemp(prefix="hnref_"))
+    os.symlink(ref, tmp / "hydranet")
+    sys.path.insert(0, str(tmp))
+    import torch  # noqa: F401
+    import hydranet  # noqa: F401
+    return hydranet
+
+
+def sha(*arrays) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+# ---------------------------------------------------------------------------
+# 1. Packer / dequantiser known answers
+# ---------------------------------------------------------------------------
+
+def pack_cases(torch, ExpertWeightPacker, QuantConfig):
+    packer = ExpertWeightPacker(QuantConfig(group_size=128))
+    cases = {}
+
+    def add(name, w):
+        t = torch.from_numpy(w.copy())
+        p, s = packer.quantize_tensor(t)
+        d = packer.dequantize_tensor(p, s, w.shape[0], w.shape[1])
+        cases[name + "/w"] = w
+        cases[name + "/packed"] = p.numpy()
+        cases[name + "/scales"] = s.numpy()
+        cases[name + "/dequant"] = d.numpy()
+
+    add("rand_f32", synth.host_normal(11, (64, 256), 0.1))
+    add("rand_f16", synth.host_normal(12, (32, 512), 0.1).astype(np.float16))
+    add("wide_f32", synth.host_normal(13, (16, 1024), 0.02))
+    # Edge rows: an all-zero group, exact half-way values (ties round to even),
+    # a dominant outlier, very large and very small magnitudes, all-negative.
+    e = synth.host_normal(14, (8, 256), 1.0)
+    e[0, :128] = 0.0
+    e[1, :128] = np.float32(7.0) * (np.arange(128, dtype=np.float32) % 15 - 7) / np.float32(7.0)
+    e[1, 0] = 7.0  # absmax 7 -> scale 1: entries are integers; add exact halves below
+    e[1, 1:15] = np.array([0.5, 1.5, 2.5, -0.5, -1.5, -2.5, 3.5, -3.5, 4.5, -4.5, 5.5, -5.5, 6.5, -6.5],
+                          dtype=np.float32)
+    e[2, 128:] *= 1e-3
+    e[2, 130] = 50.0
+    e[3] *= 1e4
+    e[4] *= 1e-30
+    e[5] = -np.abs(e[5])
+    add("edge_f32", e.astype(np.float32))
+    return cases
+
+
+# ---------------------------------------------------------------------------
+# 2. MoE layers through the reference (dequant mode, float32)
+# ---------------------------------------------------------------------------
+
+def packed_experts(torch, packer, base_seed, shape):
+    """Pack every expert with the REFERENCE packer; return numpy tensors + blob hashes."""
+    out, hashes = [], []
+    for e in range(shape.experts):
+        g, u, d = synth.host_expert_weights(base_seed, shape, e)
+        pe = packer.pack_expert(0, e, {"gate_proj": torch.from_numpy(g), "up_proj": torch.from_numpy(u),
+                                       "down_proj": torch.from_numpy(d)})
+        t = [pe.gate_proj_packed.numpy(), pe.gate_proj_scales.numpy(), pe.up_proj_packed.numpy(),
+             pe.up_proj_scales.numpy(), pe.down_proj_packed.numpy(), pe.down_proj_scales.numpy()]
+        out.append(t)
+        hashes.append(sha(*t))
+    return out, hashes
+
+
+def dequant_weights(torch, packer, t, shape):
+    H, F = shape.hidden, shape.ffn
+    gp, gs, up, us, dp, ds = [torch.from_numpy(a) for a in t]
+    return {"gate_proj": packer.dequantize_tensor(gp, gs, F, H).float(),
+            "up_proj": packer.dequantize_tensor(up, us, F, H).float(),
+            "down_proj": packer.dequantize_tensor(dp, ds, H, F).float()}
+
+
+def mixtral_layer(ref, torch, base_seed, shape, tokens, affinity_cached=None):
+    from hydranet.config import MixtralConfig, ExpertCacheConfig
+    from hydranet.cache.expert_cache import ExpertCacheManager
+    from hydranet.model.mixtral import MixtralMoELayer
+    from hydranet.preprocess.pack_weights import ExpertWeightPacker, QuantConfig
+
+    cfg = MixtralConfig()
+    cfg.hidden_dim, cfg.intermediate_dim = shape.hidden, shape.ffn
+    cfg.num_experts, cfg.experts_per_token, cfg.num_layers = shape.experts, shape.top_k, 1
+    cc = ExpertCacheConfig(pinned_slots=shape.experts, hot_slots=0, probation_slots=0,
+                           enable_affinity_bonus=affinity_cached is not None)
+    mgr = ExpertCacheManager(cfg, cc, device=torch.device("cpu"), dtype=torch.float32)
+    packer = ExpertWeightPacker(QuantConfig(group_size=shape.group_size))
+    experts, hashes = packed_experts(torch, packer, base_seed, shape)
+    for e, t in enumerate(experts):
+        mgr.register_expert(0, e, dequant_weights(torch, packer, t, shape))
+    layer = MixtralMoELayer(cfg, cc, 0, mgr)
+    rw = synth.host_router_weight(base_seed, shape)
+    layer.router.gate.weight.data.copy_(torch.from_numpy(rw))
+    if affinity_cached is not None:
+        layer.router.set_cache_checker(lambda i: i in affinity_cached)
+    x = synth.host_activations(base_seed, tokens, shape.hidden)
+    with torch.no_grad():
+        h = torch.from_numpy(x).view(1, tokens, shape.hidden)
+        ro = layer.router(h, top_k_override=shape.top_k)
+        layer.router.reset_usage()
+        out = layer(h, top_k=shape.top_k)
+    mgr.shutdown()
+    return {
+        "x": x, "router_w": rw, "expert_sha256": np.array(hashes),
+        "idx": ro.expert_indices.view(tokens, -1).numpy(),
+        "weights": ro.expert_weights.view(tokens, -1).float().numpy(),
+        "logits": ro.router_logits.view(tokens, -1).numpy(),
+        "out": out.view(tokens, -1).numpy(),
+        "dims": np.array([shape.hidden, shape.ffn, shape.experts, shape.top_k, shape.group_size, tokens, base_seed]),
+        "affinity_cached": np.array(sorted(affinity_cached) if affinity_cached else [], dtype=np.int64),
+    }
+
+
+def glm_layer(ref, torch, base_seed, shape, tokens):
+    """Routed part of GLM4MoELayer (shared expert zeroed so the output is the routed sum)."""
+    from hydranet.config import GLM4AirConfig, ExpertCacheConfig
+    from hydranet.cache.expert_cache import ExpertCacheManager
+    from hydranet.model.glm4 import GLM4MoELayer
+    from hydranet.preprocess.pack_weights import ExpertWeightPacker, QuantConfig
+    from dataclasses import dataclass
+
+    cfg = GLM4AirConfig()
+    cfg.hidden_dim, cfg.moe_intermediate_dim = shape.hidden, shape.ffn
+    cfg.num_experts, cfg.experts_per_token = shape.experts, shape.top_k
+
+    @dataclass
+    class Adapter:
+        num_layers: int
+        num_experts: int
+        expert_size_bytes: int
+
+    cc = ExpertCacheConfig(pinned_slots=shape.experts, hot_slots=0, probation_slots=0)
+    mgr = ExpertCacheManager(Adapter(1, shape.experts, 3 * shape.hidden * shape.ffn * 2), cc,
+                             device=torch.device("cpu"), dtype=torch.float32)
+    packer = ExpertWeightPacker(QuantConfig(group_size=shape.group_size))
+    experts, hashes = packed_experts(torch, packer, base_seed, shape)
+    for e, t in enumerate(experts):
+        mgr.register_expert(0, e, dequant_weights(torch, packer, t, shape))
+    layer = GLM4MoELayer(cfg, 0, mgr)
+    rw = synth.host_router_weight(base_seed, shape)
+    with torch.no_grad():
+        layer.router.weight.copy_(torch.from_numpy(rw))
+        for p in layer.shared_expert.parameters():
+            p.zero_()
+    x = synth.host_activations(base_seed, tokens, shape.hidden)
+    with torch.no_grad():
+        h = torch.from_numpy(x).view(1, tokens, shape.hidden)
+        idx, w = layer.router(h)
+        out = layer(h)
+    mgr.shutdown()
+    return {
+        "x": x, "router_w": rw, "expert_sha256": np.array(hashes),
+        "idx": idx.numpy(), "weights": w.float().numpy(), "out": out.view(tokens, -1).numpy(),
+        "dims": np.array([shape.hidden, shape.ffn, shape.experts, shape.top_k, shape.group_size, tokens, base_seed]),
+    }
+
+
+# ---------------------------------------------------------------------------
+# 3. Routers at full model width, including bf16 activations
+# ---------------------------------------------------------------------------
+
+def mixtral_router_bf16(torch, base_seed, shape, tokens):
+    from hydranet.config import MixtralConfig, ExpertCacheConfig
+    from hydranet.model.router import TopKRouter
+    cfg = MixtralConfig()
+    cfg.hidden_dim, cfg.num_experts = shape.hidden, shape.experts
+    r = TopKRouter(cfg, ExpertCacheConfig(enable_affinity_bonus=False), 0).to(torch.bfloat16)
+    rw = synth.host_router_weight(base_seed, shape)
+    x = synth.host_activations(base_seed, tokens, shape.hidden)
+    with torch.no_grad():
+        r.gate.weight.copy_(torch.from_numpy(rw).to(torch.bfloat16))
+        o = r(torch.from_numpy(x).to(torch.bfloat16).view(1, tokens, -1), top_k_override=shape.top_k)
+    return {"idx": o.expert_indices.view(tokens, -1).numpy(),
+            "weights": o.expert_weights.view(tokens, -1).float().numpy(),
+            "logits": o.router_logits.view(tokens, -1).numpy(),
+            "dims": np.array([shape.hidden, shape.experts, shape.top_k, tokens, base_seed])}
+
+
+def glm_router(torch, base_seed, shape, tokens, dtype):
+    from hydranet.config import GLM4AirConfig
+    from hydranet.model.glm4 import GLM4SigmoidRouter
+    cfg = GLM4AirConfig()
+    cfg.hidden_dim, cfg.num_experts, cfg.experts_per_token = shape.hidden, shape.experts, shape.top_k
+    r = GLM4SigmoidRouter(cfg, 0)
+    rw = synth.host_router_weight(base_seed, shape)
+    x = synth.host_activations(base_seed, tokens, shape.hidden)
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16}[dtype]
+    with torch.no_grad():
+        r.weight.copy_(torch.from_numpy(rw))
+        idx, w = r(torch.from_numpy(x).to(tdt).view(1, tokens, -1))
+    return {"idx": idx.numpy(), "weights": w.float().numpy(),
+            "dims": np.array([shape.hidden, shape.experts, shape.top_k, tokens, base_seed])}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, type=Path)
+    args = ap.parse_args()
+    ref = import_reference(args.reference.resolve())
+    import torch
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    from hydranet.preprocess.pack_weights import ExpertWeightPacker, QuantConfig
+
+    np.savez_compressed(HERE / "pack_cases.npz", **pack_cases(torch, ExpertWeightPacker, QuantConfig))
+
+    c1 = synth.MoEShape(hidden=512, ffn=1024, experts=8, top_k=2)
+    np.savez_compressed(HERE / "c1_mixtral_layer.npz", **mixtral_layer(ref, torch, 0, c1, 4))
+    np.savez_compressed(HERE / "c1_mixtral_layer_affinity.npz",
+                        **mixtral_layer(ref, torch, 0, c1, 4, affinity_cached={0, 3, 5}))
+    c2s = synth.MoEShape(hidden=1024, ffn=2048, experts=8, top_k=2)
+    np.savez_compressed(HERE / "c2_small_mixtral_layer.npz", **mixtral_layer(ref, torch, 2, c2s, 16))
+    g = synth.MoEShape(hidden=512, ffn=256, experts=16, top_k=4)
+    np.savez_compressed(HERE / "glm_small_layer.npz", **glm_layer(ref, torch, 4, g, 8))
+
+    mix_full = synth.MoEShape(hidden=4096, ffn=14336, experts=8, top_k=2)
+    np.savez_compressed(HERE / "mixtral_router_bf16.npz", **mixtral_router_bf16(torch, 5, mix_full, 64))
+    glm_full = synth.MoEShape(hidden=4096, ffn=1408, experts=128, top_k=8)
+    np.savez_compressed(HERE / "glm_router_f32.npz", **glm_router(torch, 6, glm_full, 32, "f32"))
+    np.savez_compressed(HERE / "glm_router_bf16.npz", **glm_router(torch, 7, glm_full, 32, "bf16"))
+    for f in sorted(HERE.glob("*.npz")):
+        print(f"{f.name}: {f.stat().st_size} bytes")
+
+
+if __name__ == "__main__":
+    main()
