@@ -1,0 +1,206 @@
+// Shared helpers of the sm_100a INT4 MoE kernels: error plumbing, dtype
+// traits, and inline-PTX wrappers (cp.async, TMA bulk copies, mbarriers,
+// mma.sync).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <string>
+
+#include "../../include/hydranet_b200.h"
+
+namespace hn {
+
+// ----------------------------------------------------------------------------
+// Host-side error handling
+// ----------------------------------------------------------------------------
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int check_cuda(cudaError_t e, const char* what);
+int sm_count_current();
+
+#define HN_REQUIRE(cond, msg)                                  \
+  do {                                                         \
+    if (!(cond)) return ::hn::fail(HN_ERR_INVALID, (msg));     \
+  } while (0)
+#define HN_REQUIRE_SUPPORTED(cond, msg)                        \
+  do {                                                         \
+    if (!(cond)) return ::hn::fail(HN_ERR_UNSUPPORTED, (msg)); \
+  } while (0)
+#define HN_CUDA(call)                                          \
+  do {                                                         \
+    int _rc = ::hn::check_cuda((call), #call);                 \
+    if (_rc) return _rc;                                       \
+  } while (0)
+
+// Device error codes written into a workspace's error word.
+enum : int { DEV_ERR_NONE = 0, DEV_ERR_WAIT_TIMEOUT = 1, DEV_ERR_BAD_INDEX = 2 };
+
+// ----------------------------------------------------------------------------
+// Activation dtype traits.  Dequantisation uses the exponent-magic trick
+// (Kim et al., 2022, "Who Says Elephants Can't Run: Bringing Large Scale MoE
+// Models into Cloud Scale Production"; also FasterTransformer): OR-ing a
+// nibble n into the mantissa of a power of two gives the exact value 2^e + n.
+// ----------------------------------------------------------------------------
+struct BF16 {
+  using T = __nv_bfloat16;
+  using T2 = __nv_bfloat162;
+  // 0x4300 = 128.0: low nibble -> 128 + n; nibble at bits 3..6 -> 128 + 8n.
+  static constexpr uint32_t kMagic = 0x43004300u;
+  static constexpr float kOddScale = 0.125f;   // B operand of odd k is x/8
+  static constexpr float kCorrEven = 136.0f;   // (128 + n) - (n - 8)
+  static constexpr float kCorrOdd = 24.0f;     // (16 + n) - (n - 8)
+  static __device__ __forceinline__ float to_f(T v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ T from_f(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    T2 p = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&p);
+  }
+};
+
+struct F16 {
+  using T = __half;
+  using T2 = __half2;
+  // 0x6400 = 1024.0: low nibble -> 1024 + n; nibble at bits 4..7 -> 1024 + 16n.
+  static constexpr uint32_t kMagic = 0x64006400u;
+  static constexpr float kOddScale = 0.0625f;  // B operand of odd k is x/16
+  static constexpr float kCorrEven = 1032.0f;  // (1024 + n) - (n - 8)
+  static constexpr float kCorrOdd = 72.0f;     // (64 + n) - (n - 8)
+  static __device__ __forceinline__ float to_f(T v) { return __half2float(v); }
+  static __device__ __forceinline__ T from_f(float v) { return __float2half_rn(v); }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    T2 p = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&p);
+  }
+};
+
+// ----------------------------------------------------------------------------
+// PTX wrappers
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+template <uint32_t kMask>
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t c) {
+  // (a & kMask) | c  -- one LOP3
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(d) : "r"(a), "n"(kMask), "r"(c));
+  return d;
+}
+
+// cp.async 16 bytes global -> shared, L1 bypass, 256-byte L2 prefetch hint.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: gives up after kWaitLimitNs, records DEV_ERR_WAIT_TIMEOUT in
+// *err and returns false, so a kernel whose partner never arrives still ends.
+// Once any thread of the launch has recorded an error, every later wait of
+// every thread gives up at once (it polls *err), so a failing launch finishes
+// within about one wait limit instead of one limit per wait.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+__device__ __forceinline__ int ld_volatile_s32(const int* p) {
+  int v;
+  asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (err && ld_volatile_s32(err) != 0) return false;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (err && ld_volatile_s32(err) != 0) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);
+  return false;
+}
+
+// TMA bulk copy (non-tensor) global -> shared, completion on an mbarrier.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Named barrier among a subset of warps.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// D = A * B + C, m16n8k16, fp32 accumulate.
+template <typename Tr>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+
+template <>
+__device__ __forceinline__ void mma16816<BF16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<F16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float ld_cg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_cg_f32x4(const float4* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+
+}  // namespace hn

@@ -1,0 +1,1304 @@
+// INT4 mixture-of-experts decode path for sm_100a.
+//
+//   route_prep_kernel   one CTA per token: router logits / top-k / weights
+//                       (or caller-given routing), the token's activations
+//                       staged into MMA-fragment order, and -- in the last CTA
+//                       to finish -- the dispatch plan (per-expert token lists
+//                       cut into segments of at most 8*NT tokens).
+//   engine_kernel       persistent grouped INT4 GEMV/GEMM over (weight-row
+//                       tile x segment) tiles, k-split "stream-K" style so every
+//                       CTA streams the same number of 128-wide k-groups.
+//                       KIND_GATEUP: gate+up rows together, SiLU(gate)*up in
+//                       the epilogue, written as the next phase's operand.
+//                       KIND_DOWN: down projection; EPI_COMBINE scales by the
+//                       routing weight and sums the top-k choices per token,
+//                       EPI_STORE writes rows straight to the output.
+//
+// Weight tiles are streamed by per-thread cp.async into a per-warp ring; the
+// activation chunk of each k-group (shared by all warps) arrives by TMA bulk
+// copies issued by a producer warp and tracked by mbarriers.  The MMA is
+// mma.sync m16n8k16 with the WEIGHTS as the 16-row A operand and tokens as
+// the 8-column B operand.
+//
+// Dequantisation without subtraction: a nibble n OR-ed into the mantissa of
+// 2^e gives 2^e + n exactly (bf16: 128+n for a low nibble, 128+8n for a nibble
+// in bits 3..6; fp16: 1024+n / 1024+16n).  The B operand of odd k is
+// pre-divided by 8 (bf16) or 16 (fp16), so for every k the MMA computes
+// (n - 8 + c_k) * x_k with c_k = 136 / 24 (bf16) or 1032 / 72 (fp16).  The
+// constant part, C = sum_k c_k x_k per (token, group), is computed once when
+// the activations are staged and subtracted before the group scale is
+// applied: acc += scale[row, group] * (mma_partial - C).  Weights therefore
+// enter the MMA as the exact integers n - 8, and the scale multiplies in fp32.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace hn {
+
+constexpr int kChunk = 272;  // bytes per (token, k-group): 256 B fragments + fp32 C + 12 B pad
+constexpr int kNW = 8;       // consumer warps per engine CTA
+constexpr int kEngineThreads = (kNW + 1) * 32;
+constexpr int kMaxExperts = 1024;
+constexpr int kMaxTopK = 32;
+
+enum { KIND_GATEUP = 0, KIND_DOWN = 1 };
+enum { EPI_COMBINE = 0, EPI_STORE = 1 };
+enum { ROUTE_COMPUTE = 0, ROUTE_GIVEN = 1, ROUTE_IDENTITY = 2 };
+
+struct Plan {
+  int* err;
+  int* route_ctr;
+  int* counts;   // [E]
+  int* n_segs;   // [1]
+  int4* segs;    // [max_segs] {expert, first assignment, tokens, 0}
+  int* a_tok;    // [T*K] token of assignment p
+  float* a_w;    // [T*K] routing weight of assignment p
+  int* pos;      // [T*K] assignment index of (t, k)
+  int* idx;      // [T*K] top-k expert ids
+  float* wts;    // [T*K] top-k weights (rounded to the activation dtype)
+  uint8_t* xp;   // [K_in/128][T][kChunk]    staged activations
+  uint8_t* hp;   // [F/128][T*K][kChunk]     staged SiLU(gate)*up
+  float* part1;  // stream-K partial tiles, phase 1
+  float* part2;  // stream-K partial tiles, phase 2
+  float* R;      // [T*K][H] weighted expert outputs (EPI_COMBINE)
+  int* ctr1;     // per phase-1 tile arrival counters
+  int* ctr2;     // per phase-2 tile arrival counters
+  int* rtctr;    // per output row-tile segment counters
+};
+
+__host__ __device__ constexpr int seg_tokens(int nt) { return 8 * nt; }
+
+// ---------------------------------------------------------------------------
+// Activation staging.  For k-group g, token t, the chunk holds, for each tig
+// (= lane & 3 of the consuming thread) 64 bytes = 4 units of 16 bytes; unit
+// q of tig covers x[32*tig + 8*q + i], i = 0..7, packed as
+//   { (x0, x4), (x2, x6), (x1*s, x5*s), (x3*s, x7*s) }  (s = odd-k scale)
+// which is exactly the B fragment pair {b0, b1} of the two MMA k-steps that
+// consume word q of the thread's A data (see compute_iter).  Unit q of tig
+// is stored at slot q ^ (tig & 2) so that the 8 lanes of each quarter-warp
+// hit distinct shared-memory banks (the chunk stride, 272 B, is 17 granules).
+// ---------------------------------------------------------------------------
+template <typename Tr>
+__device__ __forceinline__ void pack_unit(const float (&v)[8], uint4& out, float& cpart) {
+  const float s = Tr::kOddScale;
+  uint4 u;
+  u.x = Tr::pack(v[0], v[4]);
+  u.y = Tr::pack(v[2], v[6]);
+  u.z = Tr::pack(v[1] * s, v[5] * s);
+  u.w = Tr::pack(v[3] * s, v[7] * s);
+  // effective odd values are what the MMA actually sees (times 1/s, exact)
+  const typename Tr::T2* oz = reinterpret_cast<const typename Tr::T2*>(&u.z);
+  const typename Tr::T2* ow = reinterpret_cast<const typename Tr::T2*>(&u.w);
+  float2 fz = make_float2(Tr::to_f(oz->x), Tr::to_f(oz->y));
+  float2 fw = make_float2(Tr::to_f(ow->x), Tr::to_f(ow->y));
+  const float inv = 1.0f / s;
+  cpart = Tr::kCorrEven * (((v[0] + v[2]) + v[4]) + v[6]) + Tr::kCorrOdd * inv * (((fz.x + fw.x) + fz.y) + fw.y);
+  out = u;
+}
+
+__device__ __forceinline__ int chunk_slot(int tig, int q) { return tig * 64 + ((q ^ (tig & 2)) << 4); }
+
+// ---------------------------------------------------------------------------
+// Router + staging + plan
+// ---------------------------------------------------------------------------
+struct RouteArgs {
+  const void* x;
+  int64_t ldx;
+  int T, H, E, K;
+  int mode;
+  int kind;
+  const void* rw;
+  int rw_dtype;
+  int logits_act;
+  const float* bonus;
+  float thr;
+  const float* bias;
+  int norm;
+  float scaling;
+  const int32_t* given_idx;
+  const float* given_w;
+  int32_t* out_idx;
+  float* out_w;
+  float* out_logits;
+  int seg;
+  Plan plan;
+};
+
+__device__ __forceinline__ float load_any(const void* p, int dtype, int64_t i) {
+  if (dtype == HN_DTYPE_F32) return reinterpret_cast<const float*>(p)[i];
+  if (dtype == HN_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+template <typename Tr>
+__global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
+  extern __shared__ __align__(16) float rsm[];
+  float* xs = rsm;                 // [H]
+  float* lg = xs + a.H;            // [E]
+  float* cpart = lg + a.E;         // [H/8]
+  __shared__ int s_last;
+  __shared__ int s_idx[kMaxTopK];
+  __shared__ float s_w[kMaxTopK];
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const typename Tr::T* xrow = reinterpret_cast<const typename Tr::T*>(a.x) + (int64_t)t * a.ldx;
+  for (int i = tid; i < a.H; i += 256) xs[i] = Tr::to_f(xrow[i]);
+  __syncthreads();
+
+  // 1. staged activations + per-group correction C
+  const int units = a.H / 8;
+  for (int u = tid; u < units; u += 256) {
+    const int g = u >> 4, tig = (u >> 2) & 3, q = u & 3;
+    const int k0 = g * 128 + tig * 32 + q * 8;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = xs[k0 + i];
+    uint4 packed;
+    float cp;
+    pack_unit<Tr>(v, packed, cp);
+    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk + chunk_slot(tig, q)) = packed;
+    cpart[u] = cp;
+  }
+  __syncthreads();
+  for (int g = tid; g < a.H / 128; g += 256) {
+    float c = 0.f;
+    for (int u = 0; u < 16; ++u) c += cpart[g * 16 + u];
+    *reinterpret_cast<float4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk + 256) = make_float4(c, 0.f, 0.f, 0.f);
+  }
+
+  // 2. routing for this token
+  if (a.mode == ROUTE_COMPUTE) {
+    for (int e = warp; e < a.E; e += 8) {
+      float acc = 0.f;
+      for (int i = lane; i < a.H; i += 32) acc += xs[i] * load_any(a.rw, a.rw_dtype, (int64_t)e * a.H + i);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) lg[e] = a.logits_act ? Tr::to_f(Tr::from_f(acc)) : acc;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // optional cache-affinity bonus (model/router.py:132-175)
+      if (a.kind == HN_ROUTER_SOFTMAX_TOPK && a.bonus) {
+        float mx = -INFINITY;
+        for (int e = lane; e < a.E; e += 32) mx = fmaxf(mx, lg[e]);
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float se = 0.f;
+        for (int e = lane; e < a.E; e += 32) se += expf(lg[e] - mx);
+        for (int o = 16; o; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+        float ent = 0.f;
+        for (int e = lane; e < a.E; e += 32) {
+          const float p = expf(lg[e] - mx) / se;
+          ent -= p * logf(p + 1e-10f);
+        }
+        for (int o = 16; o; o >>= 1) ent += __shfl_xor_sync(0xffffffffu, ent, o);
+        const bool on = ent / logf((float)a.E) > a.thr;
+        __syncwarp();
+        if (on)
+          for (int e = lane; e < a.E; e += 32) lg[e] += a.bonus[e];
+        __syncwarp();
+      }
+      if (a.out_logits)
+        for (int e = lane; e < a.E; e += 32) a.out_logits[(int64_t)t * a.E + e] = lg[e];
+      // selection scores; ties resolve to the lower expert index
+      float sc[kMaxExperts / 32];
+      const int per = (a.E + 31) / 32;
+      for (int j = 0; j < per; ++j) {
+        const int e = lane + 32 * j;
+        float v = -INFINITY;
+        if (e < a.E) {
+          v = lg[e];
+          if (a.kind == HN_ROUTER_SIGMOID_TOPK) {
+            v = 1.0f / (1.0f + expf(-v));
+            if (a.bias) v += a.bias[e];
+          }
+          if (v != v) v = -INFINITY;  // a NaN score never wins a slot
+        }
+        sc[j] = v;
+      }
+      for (int k = 0; k < a.K; ++k) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int j = 0; j < per; ++j) {
+          const int e = lane + 32 * j;
+          if (e < a.E && (sc[j] > bv || (sc[j] == bv && e < bi))) {
+            bv = sc[j];
+            bi = e;
+          }
+        }
+        for (int o = 16; o; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (bi >= a.E) bi = 0;  // unreachable for finite scores; keeps the index in range
+        if ((bi & 31) == lane) sc[bi >> 5] = -INFINITY;
+        if (lane == 0) s_idx[k] = bi;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        float w[kMaxTopK];
+        if (a.kind == HN_ROUTER_SOFTMAX_TOPK) {
+          // softmax over the selected logits (model/router.py:114), renormalised (:117)
+          float mx = -INFINITY;
+          for (int k = 0; k < a.K; ++k) mx = fmaxf(mx, lg[s_idx[k]]);
+          float s = 0.f;
+          for (int k = 0; k < a.K; ++k) {
+            w[k] = expf(lg[s_idx[k]] - mx);
+            s += w[k];
+          }
+          float s2 = 0.f;
+          for (int k = 0; k < a.K; ++k) {
+            w[k] = w[k] / s;
+            s2 += w[k];
+          }
+          for (int k = 0; k < a.K; ++k) w[k] = w[k] / s2;
+        } else {
+          // sigmoid scores of the selected experts, unbiased (model/glm4.py:300-307)
+          float s = 0.f;
+          for (int k = 0; k < a.K; ++k) {
+            w[k] = 1.0f / (1.0f + expf(-lg[s_idx[k]]));
+            s += w[k];
+          }
+          for (int k = 0; k < a.K; ++k) {
+            if (a.norm) w[k] = w[k] / (s + 1e-9f);
+            w[k] = w[k] * a.scaling;
+          }
+        }
+        for (int k = 0; k < a.K; ++k) s_w[k] = Tr::to_f(Tr::from_f(w[k]));  // cast to the activation dtype
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+  } else if (tid == 0) {
+    for (int k = 0; k < a.K; ++k) {
+      if (a.mode == ROUTE_GIVEN) {
+        int e = a.given_idx[(int64_t)t * a.K + k];
+        if (e < 0 || e >= a.E) {
+          atomicExch(a.plan.err, DEV_ERR_BAD_INDEX);
+          e = 0;
+        }
+        s_idx[k] = e;
+        s_w[k] = a.given_w[(int64_t)t * a.K + k];
+      } else {
+        s_idx[k] = 0;
+        s_w[k] = 1.0f;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < a.K) {
+    a.plan.idx[(int64_t)t * a.K + tid] = s_idx[tid];
+    a.plan.wts[(int64_t)t * a.K + tid] = s_w[tid];
+    if (a.out_idx) a.out_idx[(int64_t)t * a.K + tid] = s_idx[tid];
+    if (a.out_w) a.out_w[(int64_t)t * a.K + tid] = s_w[tid];
+  }
+
+  // 3. the last CTA to finish builds the plan
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(a.plan.route_ctr, 1) == a.T - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  int* cnt = reinterpret_cast<int*>(rsm);  // reuse (>= E ints available: H >= 128 floats)
+  int* off = cnt + a.E;
+  for (int e = tid; e < a.E; e += 256) cnt[e] = 0;
+  __syncthreads();
+  const int TK = a.T * a.K;
+  for (int i = tid; i < TK; i += 256) atomicAdd(&cnt[__ldcg(a.plan.idx + i)], 1);
+  __syncthreads();
+  if (tid == 0) {
+    int o = 0, ns = 0;
+    for (int e = 0; e < a.E; ++e) {
+      off[e] = o;
+      const int m = cnt[e];
+      for (int j = 0; j < m; j += a.seg) a.plan.segs[ns++] = make_int4(e, o + j, min(a.seg, m - j), 0);
+      o += m;
+      a.plan.counts[e] = m;
+    }
+    *a.plan.n_segs = ns;
+    *a.plan.route_ctr = 0;
+  }
+  __syncthreads();
+  // per-expert assignment order: by token, then by top-k slot (ballot over 32
+  // tokens at a time); a token listing the same expert twice gets two slots
+  for (int e = warp; e < a.E; e += 8) {
+    int base = 0;
+    for (int t0 = 0; t0 < a.T; t0 += 32) {
+      const int tt = t0 + lane;
+      for (int k = 0; k < a.K; ++k) {
+        const bool hit = tt < a.T && __ldcg(a.plan.idx + (int64_t)tt * a.K + k) == e;
+        const unsigned bal = __ballot_sync(0xffffffffu, hit);
+        if (hit) {
+          const int p = off[e] + base + __popc(bal & ((1u << lane) - 1u));
+          a.plan.pos[(int64_t)tt * a.K + k] = p;
+          a.plan.a_tok[p] = tt;
+          a.plan.a_w[p] = __ldcg(a.plan.wts + (int64_t)tt * a.K + k);
+        }
+        base += __popc(bal);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Grouped GEMV engine
+// ---------------------------------------------------------------------------
+struct EngineArgs {
+  int K;     // reduction length (multiple of 128)
+  int G;     // K / 128
+  int N;     // weight rows
+  int n_rt;  // row tiles
+  int T, topk;
+  const int4* segs;
+  const int* n_segs;
+  const int* a_tok;
+  const float* a_w;
+  const int* pos;
+  const hn_expert_ptrs* table;
+  hn_expert_ptrs single;
+  const uint8_t* bsrc;
+  int64_t b_gstride;
+  int b_use_tok;
+  uint8_t* hp;
+  int64_t hp_gstride;
+  float* R;
+  void* out;
+  int64_t ldo;
+  float* part;
+  int* tile_ctr;
+  int* rt_ctr;
+  int* err;
+  int P;
+};
+
+template <int NT, int SB, int DA>
+struct EngineSmem {
+  static constexpr int kSeg = seg_tokens(NT);
+  static constexpr int kHdr = 256;
+  static constexpr int kB = SB * kSeg * kChunk;
+  static constexpr int kA = kNW * DA * 2048;
+  static constexpr int kH = 128 * (kSeg + 1) * 4 + kSeg * 16 * 4;
+  static constexpr int kTotal = kHdr + kB + kA + kH;
+};
+
+template <int KIND>
+struct TileMap {
+  // GATEUP tiles are segment-major, DOWN tiles row-tile-major.
+  static __device__ __forceinline__ void split(int tile, int n_rt, int n_segs, int& seg, int& rt) {
+    if (KIND == KIND_GATEUP) {
+      seg = tile / n_rt;
+      rt = tile - seg * n_rt;
+    } else {
+      rt = tile / n_segs;
+      seg = tile - rt * n_segs;
+    }
+  }
+};
+
+template <typename Tr, int NT>
+__device__ __forceinline__ void compute_iter(const uint4 (&A)[4], const uint8_t* bstage, int nact, int g, int tig,
+                                             float (&P0)[NT][4], float (&P1)[NT][4]) {
+  const int swz = tig & 2;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t w0g = (&A[0].x)[q], w0h = (&A[1].x)[q], w1g = (&A[2].x)[q], w1h = (&A[3].x)[q];
+    uint4 bf[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      if (nt < nact)
+        bf[nt] = *reinterpret_cast<const uint4*>(bstage + (nt * 8 + g) * kChunk + tig * 64 + ((q ^ swz) << 4));
+    const uint32_t M = Tr::kMagic;
+    // k-step 1: nibbles (0,4) and (2,6)
+    {
+      uint32_t fa[4] = {lop3_and_or<0x000F000Fu>(w0g, M), lop3_and_or<0x000F000Fu>(w0h, M),
+                        lop3_and_or<0x000F000Fu>(w0g >> 8, M), lop3_and_or<0x000F000Fu>(w0h >> 8, M)};
+      uint32_t fb[4] = {lop3_and_or<0x000F000Fu>(w1g, M), lop3_and_or<0x000F000Fu>(w1h, M),
+                        lop3_and_or<0x000F000Fu>(w1g >> 8, M), lop3_and_or<0x000F000Fu>(w1h >> 8, M)};
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        if (nt < nact) {
+          mma16816<Tr>(P0[nt], fa, bf[nt].x, bf[nt].y);
+          mma16816<Tr>(P1[nt], fb, bf[nt].x, bf[nt].y);
+        }
+    }
+    // k-step 2: nibbles (1,5) and (3,7)
+    {
+      uint32_t fa[4], fb[4];
+      if constexpr (Tr::kMagic == BF16::kMagic) {
+        fa[0] = lop3_and_or<0x00780078u>(w0g >> 1, M);
+        fa[1] = lop3_and_or<0x00780078u>(w0h >> 1, M);
+        fa[2] = lop3_and_or<0x00780078u>(w0g >> 9, M);
+        fa[3] = lop3_and_or<0x00780078u>(w0h >> 9, M);
+        fb[0] = lop3_and_or<0x00780078u>(w1g >> 1, M);
+        fb[1] = lop3_and_or<0x00780078u>(w1h >> 1, M);
+        fb[2] = lop3_and_or<0x00780078u>(w1g >> 9, M);
+        fb[3] = lop3_and_or<0x00780078u>(w1h >> 9, M);
+      } else {
+        fa[0] = lop3_and_or<0x00F000F0u>(w0g, M);
+        fa[1] = lop3_and_or<0x00F000F0u>(w0h, M);
+        fa[2] = lop3_and_or<0x00F000F0u>(w0g >> 8, M);
+        fa[3] = lop3_and_or<0x00F000F0u>(w0h >> 8, M);
+        fb[0] = lop3_and_or<0x00F000F0u>(w1g, M);
+        fb[1] = lop3_and_or<0x00F000F0u>(w1h, M);
+        fb[2] = lop3_and_or<0x00F000F0u>(w1g >> 8, M);
+        fb[3] = lop3_and_or<0x00F000F0u>(w1h >> 8, M);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        if (nt < nact) {
+          mma16816<Tr>(P0[nt], fa, bf[nt].z, bf[nt].w);
+          mma16816<Tr>(P1[nt], fb, bf[nt].z, bf[nt].w);
+        }
+    }
+  }
+}
+
+// Per-warp view of one tile: segment, rows and pointers.
+struct TileView {
+  int seg, rt, m, p0;
+  const uint8_t* a[4];   // A0 row g, A0 row g+8, A1 row g, A1 row g+8 (+ tig*16)
+  const uint16_t* s[4];  // matching scale rows
+};
+
+template <int KIND>
+__device__ __forceinline__ void load_tile(const EngineArgs& a, int tile, int n_segs, int warp, int g, int tig,
+                                          TileView& v) {
+  TileMap<KIND>::split(tile, a.n_rt, n_segs, v.seg, v.rt);
+  const int4 sg = a.segs[v.seg];
+  v.m = sg.z;
+  v.p0 = sg.y;
+  const hn_expert_ptrs ep = a.table ? a.table[sg.x] : a.single;
+  const uint8_t* A0;
+  const uint8_t* A1;
+  const uint16_t* S0;
+  const uint16_t* S1;
+  int r[4];
+  if (KIND == KIND_GATEUP) {
+    A0 = ep.gate_packed;
+    S0 = ep.gate_scales;
+    A1 = ep.up_packed;
+    S1 = ep.up_scales;
+    const int rb = v.rt * 128 + warp * 16 + g;
+    r[0] = rb;
+    r[1] = rb + 8;
+    r[2] = rb;
+    r[3] = rb + 8;
+  } else {
+    A0 = A1 = ep.down_packed;
+    S0 = S1 = ep.down_scales;
+    const int rb = v.rt * 256 + warp * 32 + g;
+    r[0] = rb;
+    r[1] = rb + 8;
+    r[2] = rb + 16;
+    r[3] = rb + 24;
+  }
+  const int64_t rowb = a.K / 2;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int rr = min(r[i], a.N - 1);  // rows past N load row N-1 and are never stored
+    v.a[i] = (i < 2 ? A0 : A1) + (int64_t)rr * rowb + tig * 16;
+    v.s[i] = (i < 2 ? S0 : S1) + (int64_t)rr * a.G;
+  }
+}
+
+template <typename Tr, int NT, int KIND, int EPI, int SB, int DA, int MINB>
+__global__ void __launch_bounds__(kEngineThreads, MINB) engine_kernel(const __grid_constant__ EngineArgs a) {
+  using L = EngineSmem<NT, SB, DA>;
+  constexpr int SEG = L::kSeg;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + SB;
+  int* bcast = reinterpret_cast<int*>(empty + SB);
+  uint8_t* bst = smem + L::kHdr;
+  uint8_t* ast = bst + L::kB;
+  float* htile = reinterpret_cast<float*>(ast + L::kA);
+  float* cpart = htile + 128 * (SEG + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_segs = *a.n_segs;
+  const int n_tiles = a.n_rt * n_segs;
+  const int64_t NI = (int64_t)n_tiles * a.G;
+  if (NI <= 0) return;
+  const int64_t P = min((int64_t)a.P, NI);
+  const int64_t c = blockIdx.x;
+  if (c >= P) return;
+  const int64_t b0 = c * NI / P, b1 = (c + 1) * NI / P;
+  auto cta_of = [&](int64_t i) -> int64_t { return ((i + 1) * P - 1) / NI; };
+  auto begin_of = [&](int64_t cc) -> int64_t { return cc * NI / P; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SB; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), kNW);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kNW) {
+    // ------------------------------ producer ------------------------------
+    int tile = (int)(b0 / a.G), grp = (int)(b0 - (int64_t)tile * a.G);
+    int seg, rt;
+    TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+    int4 sg = a.segs[seg];
+    for (int64_t it = b0, k = 0; it < b1; ++it, ++k) {
+      const int stage = (int)(k % SB);
+      const uint32_t ph = (uint32_t)((k / SB) & 1);
+      if (k >= SB) mbar_wait(smem_u32(&empty[stage]), ph ^ 1u, a.err);
+      const int m = sg.z;
+      if (lane == 0) mbar_arrive_expect_tx(smem_u32(&full[stage]), (uint32_t)(m * kChunk));
+      __syncwarp();
+      if (lane < m) {
+        const int row = a.b_use_tok ? a.a_tok[sg.y + lane] : sg.y + lane;
+        const uint8_t* src = a.bsrc + (int64_t)grp * a.b_gstride + (int64_t)row * kChunk;
+        bulk_g2s(smem_u32(bst + (stage * SEG + lane) * kChunk), src, kChunk, smem_u32(&full[stage]));
+      }
+      if (++grp == a.G) {
+        grp = 0;
+        ++tile;
+        if (it + 1 < b1) {
+          TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+          sg = a.segs[seg];
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------- consumers --------------------------------
+  const int g = lane >> 2, tig = lane & 3;
+  constexpr int kConsumers = kNW * 32;
+  // prefetch cursor
+  int pf_tile = (int)(b0 / a.G), pf_grp = (int)(b0 - (int64_t)pf_tile * a.G);
+  int64_t pf_it = b0;
+  TileView pv;
+  load_tile<KIND>(a, pf_tile, n_segs, warp, g, tig, pv);
+  uint8_t* aw = ast + warp * DA * 2048;
+  auto issue_a = [&](int slot) {
+    if (pf_it < b1) {
+      const uint32_t dst = smem_u32(aw + slot * 2048 + lane * 16);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cp_async16(dst + j * 512, pv.a[j] + pf_grp * 64);
+    }
+    cp_async_commit();
+    if (pf_it < b1) {
+      ++pf_it;
+      if (++pf_grp == a.G) {
+        pf_grp = 0;
+        ++pf_tile;
+        if (pf_it < b1) load_tile<KIND>(a, pf_tile, n_segs, warp, g, tig, pv);
+      }
+    }
+  };
+#pragma unroll 1
+  for (int i = 0; i < DA; ++i) issue_a(i);
+
+  int tile = (int)(b0 / a.G), grp = (int)(b0 - (int64_t)tile * a.G);
+  TileView cv;
+  load_tile<KIND>(a, tile, n_segs, warp, g, tig, cv);
+  float acc0[NT][4], acc1[NT][4], P0[NT][4], P1[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc0[nt][j] = acc1[nt][j] = P0[nt][j] = P1[nt][j] = 0.f;
+
+#pragma unroll 1
+  for (int64_t it = b0, k = 0; it < b1; ++it, ++k) {
+    const int stage = (int)(k % SB);
+    const uint32_t ph = (uint32_t)((k / SB) & 1);
+    const int aslot = (int)(k % DA);
+    // group scales (fp16) of the four rows
+    float sc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sc[j] = __half2float(__ushort_as_half(__ldg(cv.s[j] + grp)));
+    cp_async_wait<DA - 1>();
+    uint4 A[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) A[j] = *reinterpret_cast<const uint4*>(aw + aslot * 2048 + j * 512 + lane * 16);
+    mbar_wait(smem_u32(&full[stage]), ph, a.err);
+    const uint8_t* bstage = bst + stage * SEG * kChunk;
+    const int nact = (cv.m + 7) >> 3;
+    float cl[NT], ch[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      cl[nt] = ch[nt] = 0.f;
+      if (nt < nact) {
+        cl[nt] = *reinterpret_cast<const float*>(bstage + (nt * 8 + 2 * tig) * kChunk + 256);
+        ch[nt] = *reinterpret_cast<const float*>(bstage + (nt * 8 + 2 * tig + 1) * kChunk + 256);
+      }
+    }
+    compute_iter<Tr, NT>(A, bstage, nact, g, tig, P0, P1);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
+    issue_a(aslot);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if (nt < nact) {
+        acc0[nt][0] += sc[0] * (P0[nt][0] - cl[nt]);
+        acc0[nt][1] += sc[0] * (P0[nt][1] - ch[nt]);
+        acc0[nt][2] += sc[1] * (P0[nt][2] - cl[nt]);
+        acc0[nt][3] += sc[1] * (P0[nt][3] - ch[nt]);
+        acc1[nt][0] += sc[2] * (P1[nt][0] - cl[nt]);
+        acc1[nt][1] += sc[2] * (P1[nt][1] - ch[nt]);
+        acc1[nt][2] += sc[3] * (P1[nt][2] - cl[nt]);
+        acc1[nt][3] += sc[3] * (P1[nt][3] - ch[nt]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) P0[nt][j] = P1[nt][j] = 0.f;
+    }
+
+    const bool tile_end = (grp == a.G - 1) || (it == b1 - 1);
+    if (tile_end) {
+      // ---------------- finish this CTA's piece of the tile ----------------
+      const int64_t ts = (int64_t)tile * a.G, te = ts + a.G;
+      bool own = true;
+      if (!(b0 <= ts && b1 >= te)) {
+        const int slot = (ts <= b0) ? 0 : 1;
+        float* dst = a.part + ((((int64_t)c * 2 + slot) * kNW + warp) * (8 * NT)) * 32 + lane;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            dst[((0 * NT + nt) * 4 + j) * 32] = acc0[nt][j];
+            dst[((1 * NT + nt) * 4 + j) * 32] = acc1[nt][j];
+          }
+        __threadfence();
+        named_bar_sync(1, kConsumers);
+        const int64_t c0 = cta_of(ts), c1 = cta_of(te - 1);
+        if (threadIdx.x == 0) bcast[0] = (atomicAdd(&a.tile_ctr[tile], 1) == (int)(c1 - c0));
+        named_bar_sync(1, kConsumers);
+        own = bcast[0] != 0;
+        if (own) {
+          __threadfence();
+          float s0[NT][4], s1[NT][4];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s0[nt][j] = s1[nt][j] = 0.f;
+          for (int64_t cc = c0; cc <= c1; ++cc) {
+            if (cc == c) {
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  s0[nt][j] += acc0[nt][j];
+                  s1[nt][j] += acc1[nt][j];
+                }
+            } else {
+              const int64_t bc = begin_of(cc);
+              const int sl = (bc >= ts && bc < te) ? 0 : 1;
+              const float* src = a.part + ((((int64_t)cc * 2 + sl) * kNW + warp) * (8 * NT)) * 32 + lane;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  s0[nt][j] += ld_cg_f32(src + ((0 * NT + nt) * 4 + j) * 32);
+                  s1[nt][j] += ld_cg_f32(src + ((1 * NT + nt) * 4 + j) * 32);
+                }
+            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              acc0[nt][j] = s0[nt][j];
+              acc1[nt][j] = s1[nt][j];
+            }
+          if (threadIdx.x == 0) a.tile_ctr[tile] = 0;
+        }
+      }
+      if (own) {
+        if (KIND == KIND_GATEUP) {
+          // SiLU(gate) * up for rows warp*16 + (g, g+8), tokens nt*8 + 2tig + (0, 1)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int row = warp * 16 + g + ((j >> 1) << 3);
+              const int tok = nt * 8 + 2 * tig + (j & 1);
+              const float h = silu_f(acc0[nt][j]) * acc1[nt][j];
+              htile[row * (SEG + 1) + tok] = Tr::to_f(Tr::from_f(h));
+            }
+          named_bar_sync(1, kConsumers);
+          const int m = cv.m;
+          uint8_t* dst = a.hp + (int64_t)cv.rt * a.hp_gstride;
+          for (int task = threadIdx.x; task < m * 16; task += kConsumers) {
+            const int tok = task >> 4, u = task & 15, tg = u >> 2, q = u & 3;
+            const int k0 = tg * 32 + q * 8;
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = htile[(k0 + i) * (SEG + 1) + tok];
+            uint4 pk;
+            float cp;
+            pack_unit<Tr>(v, pk, cp);
+            *reinterpret_cast<uint4*>(dst + (int64_t)(cv.p0 + tok) * kChunk + chunk_slot(tg, q)) = pk;
+            cpart[tok * 16 + u] = cp;
+          }
+          named_bar_sync(1, kConsumers);
+          if (threadIdx.x < m) {
+            float cs = 0.f;
+            for (int u = 0; u < 16; ++u) cs += cpart[threadIdx.x * 16 + u];
+            *reinterpret_cast<float4*>(dst + (int64_t)(cv.p0 + threadIdx.x) * kChunk + 256) =
+                make_float4(cs, 0.f, 0.f, 0.f);
+          }
+          named_bar_sync(1, kConsumers);
+        } else {
+          const int rb = cv.rt * 256 + warp * 32 + g;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int tok = nt * 8 + 2 * tig + (j & 1);
+              const int row = rb + ((j >> 2) << 4) + (((j >> 1) & 1) << 3);
+              const float v = (j < 4) ? acc0[nt][j] : acc1[nt][j - 4];
+              if (tok < cv.m && row < a.N) {
+                const int p = cv.p0 + tok;
+                if (EPI == EPI_STORE) {
+                  reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)a.a_tok[p] * a.ldo + row] = Tr::from_f(v);
+                } else {
+                  a.R[(int64_t)p * a.N + row] = v * a.a_w[p];
+                }
+              }
+            }
+          if (EPI == EPI_COMBINE) {
+            __threadfence();
+            named_bar_sync(1, kConsumers);
+            if (threadIdx.x == 0) bcast[1] = (atomicAdd(&a.rt_ctr[cv.rt], 1) == n_segs - 1);
+            named_bar_sync(1, kConsumers);
+            if (bcast[1]) {
+              __threadfence();
+              const int r0 = cv.rt * 256, nr = min(256, a.N - r0);
+              for (int task = threadIdx.x; task < a.T * nr; task += kConsumers) {
+                const int t = task / nr, row = r0 + task - t * nr;
+                float s = 0.f;
+                for (int kk = 0; kk < a.topk; ++kk) s += ld_cg_f32(a.R + (int64_t)a.pos[t * a.topk + kk] * a.N + row);
+                reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)t * a.ldo + row] = Tr::from_f(s);
+              }
+              if (threadIdx.x == 0) a.rt_ctr[cv.rt] = 0;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc0[nt][j] = acc1[nt][j] = 0.f;
+    }
+    if (++grp == a.G) {
+      grp = 0;
+      ++tile;
+      if (it + 1 < b1) load_tile<KIND>(a, tile, n_segs, warp, g, tig, cv);
+    }
+  }
+  cp_async_wait<0>();
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+template <int NT>
+struct Tune;
+template <>
+struct Tune<1> {
+  static constexpr int SB = 8, DA = 5, MINB = 2;
+};
+template <>
+struct Tune<2> {
+  static constexpr int SB = 6, DA = 4, MINB = 2;
+};
+template <>
+struct Tune<4> {
+  static constexpr int SB = 6, DA = 6, MINB = 1;
+};
+
+static int pick_nt(int64_t max_tokens_per_expert) {
+  if (max_tokens_per_expert <= 8) return 1;
+  if (max_tokens_per_expert <= 16) return 2;
+  return 4;
+}
+static int minb_of(int nt) { return nt == 1 ? Tune<1>::MINB : nt == 2 ? Tune<2>::MINB : Tune<4>::MINB; }
+
+template <typename Tr, int NT, int KIND, int EPI>
+static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
+  using TU = Tune<NT>;
+  using L = EngineSmem<NT, TU::SB, TU::DA>;
+  auto kern = engine_kernel<Tr, NT, KIND, EPI, TU::SB, TU::DA, TU::MINB>;
+  static bool attr_set[64] = {};  // per instantiation and device
+  int dev = 0;
+  HN_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    HN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  kern<<<a.P, kEngineThreads, L::kTotal, s>>>(a);
+  HN_CUDA(cudaGetLastError());
+  return HN_OK;
+}
+
+template <typename Tr, int KIND, int EPI>
+static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
+  switch (nt) {
+    case 1: return launch_engine_t<Tr, 1, KIND, EPI>(a, s);
+    case 2: return launch_engine_t<Tr, 2, KIND, EPI>(a, s);
+    default: return launch_engine_t<Tr, 4, KIND, EPI>(a, s);
+  }
+}
+
+// A workspace has a counter section at its FRONT (error word, arrival
+// counters; all zero between calls because every counter is reset by the
+// kernel that sees its final value) and a data section at its BACK.  Calls of
+// any shape can therefore share one zero-filled workspace: a counter section
+// [0, C) never overlaps another call's data section [size - D, size) as long
+// as each call's C + D fits.
+struct Layout {
+  size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
+  size_t counts, n_segs, segs, a_tok, a_w, pos, idx, wts, xp, hp, part1, part2, R, data;  // back (relative)
+  size_t total() const { return counters + data; }
+};
+
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// T tokens of width Kin, top-k over E experts; phase 1 rows F (0: no phase 1),
+// phase 2 rows N2.
+static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F, int64_t N2, int nt, int P,
+                          bool combine) {
+  Layout l{};
+  const int64_t TK = T * topk;
+  const int64_t seg = seg_tokens(nt);
+  const int64_t max_segs = std::min<int64_t>(E, TK) + (TK + seg - 1) / seg;
+  const int64_t n_rt2 = (N2 + 255) / 256;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o = align256(o + std::max<size_t>(bytes, 4));
+    return at;
+  };
+  l.err = take(4);
+  l.route_ctr = take(4);
+  l.ctr1 = take(F ? 4 * max_segs * (F / 128) : 0);
+  l.ctr2 = take(4 * max_segs * n_rt2);
+  l.rtctr = take(4 * n_rt2);
+  l.counters = o;
+  o = 0;
+  l.counts = take(4 * E);
+  l.n_segs = take(4);
+  l.segs = take(16 * max_segs);
+  l.a_tok = take(4 * TK);
+  l.a_w = take(4 * TK);
+  l.pos = take(4 * TK);
+  l.idx = take(4 * TK);
+  l.wts = take(4 * TK);
+  l.xp = take((size_t)(Kin / 128) * T * kChunk);
+  l.hp = take(F ? (size_t)(F / 128) * TK * kChunk : 0);
+  const size_t part = (size_t)P * 2 * kNW * 8 * nt * 32 * 4;
+  l.part1 = take(F ? part : 0);
+  l.part2 = take(part);
+  l.R = take(combine ? (size_t)TK * N2 * 4 : 0);
+  l.data = o;
+  return l;
+}
+
+static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  uint8_t* d = b + ((ws_bytes - l.data) & ~(size_t)255);  // data section, 256-byte aligned, at the back
+  Plan p;
+  p.err = reinterpret_cast<int*>(b + l.err);
+  p.route_ctr = reinterpret_cast<int*>(b + l.route_ctr);
+  p.ctr1 = reinterpret_cast<int*>(b + l.ctr1);
+  p.ctr2 = reinterpret_cast<int*>(b + l.ctr2);
+  p.rtctr = reinterpret_cast<int*>(b + l.rtctr);
+  p.counts = reinterpret_cast<int*>(d + l.counts);
+  p.n_segs = reinterpret_cast<int*>(d + l.n_segs);
+  p.segs = reinterpret_cast<int4*>(d + l.segs);
+  p.a_tok = reinterpret_cast<int*>(d + l.a_tok);
+  p.a_w = reinterpret_cast<float*>(d + l.a_w);
+  p.pos = reinterpret_cast<int*>(d + l.pos);
+  p.idx = reinterpret_cast<int*>(d + l.idx);
+  p.wts = reinterpret_cast<float*>(d + l.wts);
+  p.xp = d + l.xp;
+  p.hp = d + l.hp;
+  p.part1 = reinterpret_cast<float*>(d + l.part1);
+  p.part2 = reinterpret_cast<float*>(d + l.part2);
+  p.R = reinterpret_cast<float*>(d + l.R);
+  return p;
+}
+
+// The workspace must hold both sections with 256 bytes of slack for aligning
+// the data section; its base must be 256-byte aligned.
+static int check_ws(const void* ws, size_t bytes, const Layout& l) {
+  HN_REQUIRE(((uintptr_t)ws & 255) == 0, "workspace must be 256-byte aligned");
+  if (bytes < l.total() + 256) return fail(HN_ERR_WORKSPACE, "workspace too small");
+  return HN_OK;
+}
+
+static int grid_p(int nt) {
+  const int sms = sm_count_current();
+  return (sms > 0 ? sms : 148) * minb_of(nt);
+}
+
+template <typename Tr>
+static int launch_route(const RouteArgs& ra, cudaStream_t s) {
+  const size_t sm = (size_t)(ra.H + ra.E + ra.H / 8) * 4;
+  const size_t need = std::max(sm, (size_t)(2 * ra.E) * 4);
+  if (need > 48 * 1024) HN_CUDA(cudaFuncSetAttribute(route_prep_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    (int)need));
+  route_prep_kernel<Tr><<<ra.T, 256, need, s>>>(ra);
+  HN_CUDA(cudaGetLastError());
+  return HN_OK;
+}
+
+static int check_router(const hn_router_params* r, int64_t E) {
+  HN_REQUIRE(r, "router params are NULL");
+  HN_REQUIRE(r->kind == HN_ROUTER_SOFTMAX_TOPK || r->kind == HN_ROUTER_SIGMOID_TOPK, "unknown router kind");
+  HN_REQUIRE(r->weight, "router weight is NULL");
+  HN_REQUIRE(r->weight_dtype >= HN_DTYPE_F32 && r->weight_dtype <= HN_DTYPE_BF16, "bad router weight dtype");
+  HN_REQUIRE(r->top_k >= 1 && r->top_k <= E && r->top_k <= kMaxTopK, "top_k out of range");
+  return HN_OK;
+}
+
+struct MoECall {
+  const void* x;
+  int64_t ldx;
+  int dtype;
+  int64_t T, H, F, E;
+  int topk;
+  int route_mode;
+  const hn_router_params* router;
+  const int32_t* given_idx;
+  const float* given_w;
+  const hn_expert_ptrs* table;
+  hn_expert_ptrs single;
+  void* out;
+  int64_t ldo;
+  int32_t* out_idx;
+  float* out_w;
+  float* out_logits;
+  void* ws;
+  size_t ws_bytes;
+  cudaStream_t stream;
+  bool run_experts;
+};
+
+template <typename Tr>
+static int run_moe(const MoECall& m) {
+  const int64_t TK = m.T * m.topk;
+  const int nt = pick_nt(std::min<int64_t>(m.T, TK));
+  const int P = grid_p(nt);
+  // routed calls always scale by the routing weight and combine; the identity
+  // plan of a single expert MLP stores rows directly
+  const bool combine = m.route_mode != ROUTE_IDENTITY;
+  const Layout l = make_layout(m.T, m.H, m.E, m.topk, m.F, m.H, nt, P, combine);
+  int rc0 = check_ws(m.ws, m.ws_bytes, l);
+  if (rc0) return rc0;
+  const Plan plan = plan_at(m.ws, m.ws_bytes, l);
+
+  RouteArgs ra{};
+  ra.x = m.x;
+  ra.ldx = m.ldx;
+  ra.T = (int)m.T;
+  ra.H = (int)m.H;
+  ra.E = (int)m.E;
+  ra.K = m.topk;
+  ra.mode = m.route_mode;
+  if (m.router) {
+    ra.kind = m.router->kind;
+    ra.rw = m.router->weight;
+    ra.rw_dtype = m.router->weight_dtype;
+    ra.logits_act = m.router->logits_in_act_dtype;
+    ra.bonus = m.router->affinity_bonus;
+    ra.thr = m.router->entropy_threshold;
+    ra.bias = m.router->kind == HN_ROUTER_SIGMOID_TOPK ? m.router->correction_bias : nullptr;
+    ra.norm = m.router->norm_topk_prob;
+    ra.scaling = m.router->routed_scaling_factor;
+  }
+  ra.given_idx = m.given_idx;
+  ra.given_w = m.given_w;
+  ra.out_idx = m.out_idx;
+  ra.out_w = m.out_w;
+  ra.out_logits = m.out_logits;
+  ra.seg = seg_tokens(nt);
+  ra.plan = plan;
+  int rc = launch_route<Tr>(ra, m.stream);
+  if (rc || !m.run_experts) return rc;
+
+  EngineArgs e1{};
+  e1.K = (int)m.H;
+  e1.G = (int)(m.H / 128);
+  e1.N = (int)m.F;
+  e1.n_rt = (int)(m.F / 128);
+  e1.T = (int)m.T;
+  e1.topk = m.topk;
+  e1.segs = plan.segs;
+  e1.n_segs = plan.n_segs;
+  e1.a_tok = plan.a_tok;
+  e1.a_w = plan.a_w;
+  e1.pos = plan.pos;
+  e1.table = m.table;
+  e1.single = m.single;
+  e1.bsrc = plan.xp;
+  e1.b_gstride = m.T * kChunk;
+  e1.b_use_tok = 1;
+  e1.hp = plan.hp;
+  e1.hp_gstride = TK * kChunk;
+  e1.part = plan.part1;
+  e1.tile_ctr = plan.ctr1;
+  e1.err = plan.err;
+  e1.P = P;
+  rc = launch_engine<Tr, KIND_GATEUP, EPI_COMBINE>(nt, e1, m.stream);
+  if (rc) return rc;
+
+  EngineArgs e2 = e1;
+  e2.K = (int)m.F;
+  e2.G = (int)(m.F / 128);
+  e2.N = (int)m.H;
+  e2.n_rt = (int)((m.H + 255) / 256);
+  e2.bsrc = plan.hp;
+  e2.b_gstride = TK * kChunk;
+  e2.b_use_tok = 0;
+  e2.R = plan.R;
+  e2.out = m.out;
+  e2.ldo = m.ldo;
+  e2.part = plan.part2;
+  e2.tile_ctr = plan.ctr2;
+  e2.rt_ctr = plan.rtctr;
+  if (combine) return launch_engine<Tr, KIND_DOWN, EPI_COMBINE>(nt, e2, m.stream);
+  return launch_engine<Tr, KIND_DOWN, EPI_STORE>(nt, e2, m.stream);
+}
+
+static int dispatch_moe(const MoECall& m) {
+  if (m.dtype == HN_DTYPE_BF16) return run_moe<BF16>(m);
+  if (m.dtype == HN_DTYPE_F16) return run_moe<F16>(m);
+  return fail(HN_ERR_UNSUPPORTED, "activation dtype must be float16 or bfloat16");
+}
+
+static int check_dims(int64_t T, int64_t H, int64_t F, int64_t E) {
+  HN_REQUIRE(T >= 1, "need at least one token");
+  HN_REQUIRE(T <= (1 << 20), "too many tokens");
+  HN_REQUIRE(H >= 128 && H % 128 == 0, "hidden dim must be a positive multiple of 128");
+  HN_REQUIRE(F >= 128 && F % 128 == 0, "intermediate dim must be a positive multiple of 128");
+  HN_REQUIRE(E >= 1 && E <= kMaxExperts, "number of experts out of range");
+  HN_REQUIRE(H <= 32768 && F <= (1 << 18), "dims too large");
+  return HN_OK;
+}
+
+}  // namespace hn
+
+using namespace hn;
+
+extern "C" {
+
+size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int top_k) {
+  if (T < 1 || H < 128 || F < 128 || E < 1 || top_k < 1) return 0;
+  const int nt = pick_nt(std::min<int64_t>(T, T * top_k));
+  return make_layout(T, H, E, top_k, F, H, nt, grid_p(nt), true).total() + 256;
+}
+
+size_t hn_expert_mlp_workspace_size(int64_t T, int64_t H, int64_t F) {
+  if (T < 1 || H < 128 || F < 128) return 0;
+  const int nt = pick_nt(T);
+  return make_layout(T, H, 1, 1, F, H, nt, grid_p(nt), false).total() + 256;
+}
+
+size_t hn_int4_linear_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M < 1 || N < 1 || K < 128) return 0;
+  const int nt = pick_nt(M);
+  return make_layout(M, K, 1, 1, 0, N, nt, grid_p(nt), false).total() + 256;
+}
+
+int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
+                      const hn_router_params* router, const hn_expert_ptrs* experts, void* out, int32_t* topk_idx,
+                      float* topk_w, float* logits, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dims(T, H, F, E);
+  if (rc) return rc;
+  rc = check_router(router, E);
+  if (rc) return rc;
+  HN_REQUIRE(x && experts && out && workspace, "hn_moe_layer_int4: null pointer");
+  MoECall m{};
+  m.x = x;
+  m.ldx = H;
+  m.dtype = dtype;
+  m.T = T;
+  m.H = H;
+  m.F = F;
+  m.E = E;
+  m.topk = router->top_k;
+  m.route_mode = ROUTE_COMPUTE;
+  m.router = router;
+  m.table = experts;
+  m.out = out;
+  m.ldo = H;
+  m.out_idx = topk_idx;
+  m.out_w = topk_w;
+  m.out_logits = logits;
+  m.ws = workspace;
+  m.ws_bytes = workspace_bytes;
+  m.stream = (cudaStream_t)stream;
+  m.run_experts = true;
+  return dispatch_moe(m);
+}
+
+int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int top_k,
+                        const int32_t* topk_idx, const float* topk_w, const hn_expert_ptrs* experts, void* out,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dims(T, H, F, E);
+  if (rc) return rc;
+  HN_REQUIRE(top_k >= 1 && top_k <= E && top_k <= kMaxTopK, "top_k out of range");
+  HN_REQUIRE(x && topk_idx && topk_w && experts && out && workspace, "hn_moe_experts_int4: null pointer");
+  MoECall m{};
+  m.x = x;
+  m.ldx = H;
+  m.dtype = dtype;
+  m.T = T;
+  m.H = H;
+  m.F = F;
+  m.E = E;
+  m.topk = top_k;
+  m.route_mode = ROUTE_GIVEN;
+  m.given_idx = topk_idx;
+  m.given_w = topk_w;
+  m.table = experts;
+  m.out = out;
+  m.ldo = H;
+  m.ws = workspace;
+  m.ws_bytes = workspace_bytes;
+  m.stream = (cudaStream_t)stream;
+  m.run_experts = true;
+  return dispatch_moe(m);
+}
+
+int hn_moe_route(const void* x, int dtype, int64_t T, int64_t H, int64_t E, const hn_router_params* router,
+                 int32_t* topk_idx, float* topk_w, float* logits, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  int rc = check_dims(T, H, 128, E);
+  if (rc) return rc;
+  rc = check_router(router, E);
+  if (rc) return rc;
+  HN_REQUIRE(x && workspace, "hn_moe_route: null pointer");
+  MoECall m{};
+  m.x = x;
+  m.ldx = H;
+  m.dtype = dtype;
+  m.T = T;
+  m.H = H;
+  m.F = 128;
+  m.E = E;
+  m.topk = router->top_k;
+  m.route_mode = ROUTE_COMPUTE;
+  m.router = router;
+  m.out_idx = topk_idx;
+  m.out_w = topk_w;
+  m.out_logits = logits;
+  m.ws = workspace;
+  m.ws_bytes = workspace_bytes;
+  m.stream = (cudaStream_t)stream;
+  m.run_experts = false;
+  return dispatch_moe(m);
+}
+
+int hn_expert_mlp_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, const uint8_t* gate_packed,
+                       const uint16_t* gate_scales, const uint8_t* up_packed, const uint16_t* up_scales,
+                       const uint8_t* down_packed, const uint16_t* down_scales, int group_size, void* out,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  HN_REQUIRE_SUPPORTED(group_size == 128, "only group_size 128 is implemented");
+  int rc = check_dims(T, H, F, 1);
+  if (rc) return rc;
+  HN_REQUIRE(x && gate_packed && gate_scales && up_packed && up_scales && down_packed && down_scales && out &&
+                 workspace,
+             "hn_expert_mlp_int4: null pointer");
+  HN_REQUIRE((((uintptr_t)gate_packed | (uintptr_t)up_packed | (uintptr_t)down_packed) & 15) == 0,
+             "hn_expert_mlp_int4: packed weights must be 16-byte aligned");
+  MoECall m{};
+  m.x = x;
+  m.ldx = H;
+  m.dtype = dtype;
+  m.T = T;
+  m.H = H;
+  m.F = F;
+  m.E = 1;
+  m.topk = 1;
+  m.route_mode = ROUTE_IDENTITY;
+  m.single = hn_expert_ptrs{gate_packed, gate_scales, up_packed, up_scales, down_packed, down_scales};
+  m.out = out;
+  m.ldo = H;
+  m.ws = workspace;
+  m.ws_bytes = workspace_bytes;
+  m.stream = (cudaStream_t)stream;
+  m.run_experts = true;
+  return dispatch_moe(m);
+}
+
+int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, const uint8_t* w_packed,
+                   const uint16_t* w_scales, int64_t N, int group_size, void* out, int64_t ldo, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  HN_REQUIRE_SUPPORTED(group_size == 128, "only group_size 128 is implemented");
+  HN_REQUIRE(M >= 1 && N >= 1 && K >= 128 && K % 128 == 0, "int4_linear: need M, N >= 1 and K a multiple of 128");
+  HN_REQUIRE(M <= (1 << 20) && N <= (1 << 20) && K <= 32768, "int4_linear: dims too large");
+  HN_REQUIRE(((uintptr_t)w_packed & 15) == 0, "int4_linear: packed weights must be 16-byte aligned");
+  HN_REQUIRE(ldx >= K && ldo >= N, "int4_linear: bad row stride");
+  HN_REQUIRE(x && w_packed && w_scales && out && workspace, "int4_linear: null pointer");
+  const int nt = pick_nt(M);
+  const int P = grid_p(nt);
+  const Layout l = make_layout(M, K, 1, 1, 0, N, nt, P, false);
+  int rc0 = check_ws(workspace, workspace_bytes, l);
+  if (rc0) return rc0;
+  const Plan plan = plan_at(workspace, workspace_bytes, l);
+  cudaStream_t s = (cudaStream_t)stream;
+  RouteArgs ra{};
+  ra.x = x;
+  ra.ldx = ldx;
+  ra.T = (int)M;
+  ra.H = (int)K;
+  ra.E = 1;
+  ra.K = 1;
+  ra.mode = ROUTE_IDENTITY;
+  ra.seg = seg_tokens(nt);
+  ra.plan = plan;
+  EngineArgs e{};
+  e.K = (int)K;
+  e.G = (int)(K / 128);
+  e.N = (int)N;
+  e.n_rt = (int)((N + 255) / 256);
+  e.T = (int)M;
+  e.topk = 1;
+  e.segs = plan.segs;
+  e.n_segs = plan.n_segs;
+  e.a_tok = plan.a_tok;
+  e.a_w = plan.a_w;
+  e.pos = plan.pos;
+  e.table = nullptr;
+  e.single = hn_expert_ptrs{nullptr, nullptr, nullptr, nullptr, w_packed, w_scales};
+  e.bsrc = plan.xp;
+  e.b_gstride = M * kChunk;
+  e.b_use_tok = 1;
+  e.out = out;
+  e.ldo = ldo;
+  e.part = plan.part2;
+  e.tile_ctr = plan.ctr2;
+  e.rt_ctr = plan.rtctr;
+  e.err = plan.err;
+  e.P = P;
+  int rc;
+  if (dtype == HN_DTYPE_BF16) {
+    rc = launch_route<BF16>(ra, s);
+    if (!rc) rc = launch_engine<BF16, KIND_DOWN, EPI_STORE>(nt, e, s);
+  } else if (dtype == HN_DTYPE_F16) {
+    rc = launch_route<F16>(ra, s);
+    if (!rc) rc = launch_engine<F16, KIND_DOWN, EPI_STORE>(nt, e, s);
+  } else {
+    return fail(HN_ERR_UNSUPPORTED, "int4_linear: activation dtype must be float16 or bfloat16");
+  }
+  return rc;
+}
+
+int hn_workspace_error(const void* workspace, size_t workspace_bytes, int* error_code, void* stream) {
+  HN_REQUIRE(workspace && error_code && workspace_bytes >= 4, "hn_workspace_error: bad arguments");
+  HN_CUDA(cudaMemcpyAsync(error_code, workspace, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  HN_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  if (*error_code != 0) HN_CUDA(cudaMemsetAsync(const_cast<void*>(workspace), 0, 4, (cudaStream_t)stream));
+  return HN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+"""Grouped INT4 MoE layers: one router launch + two expert launches per layer.
+
+``MoELayerInt4`` replaces the host-synchronising per-expert loops of
+``MixtralMoELayer.forward`` (``model/mixtral.py:259-370``) and the routed part
+of ``GLM4MoELayer.forward`` (``model/glm4.py:365-473``): routing, per-expert
+token lists, the INT4 SwiGLU experts and the weighted top-k combine all run
+on the device with no host synchronisation, so a decode step can be captured
+in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from .packing import ExpertTable
+from .router import GLM4SigmoidRouter, RouterOutput, TopKRouter
+
+
+class MoELayerInt4(nn.Module):
+    """Router + INT4 experts + combine.
+
+    ``router`` is a ``TopKRouter`` (softmax, Mixtral) or ``GLM4SigmoidRouter``.
+    ``forward(hidden [B, S, H] or [T, H]) -> same shape``; with
+    ``return_routing=True`` it also returns (idx int64, weights, logits).
+    """
+
+    def __init__(self, router: nn.Module, experts: ExpertTable):
+        super().__init__()
+        self.router = router
+        self.experts = experts
+        self.num_experts = len(experts)
+        if router.num_experts != self.num_experts:
+            raise ValueError("router and expert table disagree on the number of experts")
+
+    def _params(self, x: torch.Tensor, top_k: Optional[int]):
+        if isinstance(self.router, TopKRouter):
+            k = top_k if top_k is not None else self.router.experts_per_token
+            bonus = self.router.bonus_vector(x.device)
+            return self.router.params(k, bonus), bonus
+        if isinstance(self.router, GLM4SigmoidRouter):
+            return self.router.params(), None
+        raise TypeError("unsupported router type")
+
+    def forward(self, hidden_states: torch.Tensor, top_k: Optional[int] = None, return_routing: bool = False):
+        shape = hidden_states.shape
+        x = hidden_states.reshape(-1, shape[-1]).contiguous()
+        params, bonus = self._params(x, top_k)
+        out, idx, w, logits = ops.moe_layer(x, params, self.experts.device_table, self.num_experts,
+                                            self.experts.intermediate_dim, want_routing=return_routing,
+                                            keep_refs=(bonus,))
+        out = out.view(shape)
+        if return_routing:
+            return out, RouterOutput(idx.long(), w.to(x.dtype), logits)
+        return out
+
+
+def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts: ExpertTable) -> torch.Tensor:
+    """Experts + weighted combine for externally routed tokens (x [T, H])."""
+    return ops.moe_experts(x, topk_idx, topk_w, experts.device_table, len(experts), experts.intermediate_dim)

@@ -60,3 +60,21 @@ def host_activations(base_seed: int, tokens: int, hidden: int) -> np.ndarray:
 
 def host_correction_bias(base_seed: int, experts: int, std: float = 0.1) -> np.ndarray:
     return host_normal(base_seed * 1_000_003 + 777_767, (experts,), std)
+
+
+def device_experts(seed: int, shape: MoEShape, device="cuda"):
+    """Experts generated on the GPU (seeded torch CUDA RNG, ~N(0, 0.02)) and packed
+    there by the CUDA packer.  Returns a list of ``packing.ExpertSlot``."""
+    import torch
+    from .packing import quantize_expert
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    H, F = shape.hidden, shape.ffn
+    slots = []
+    for _ in range(shape.experts):
+        g = torch.randn(F, H, generator=gen, device=device).mul_(WEIGHT_STD)
+        u = torch.randn(F, H, generator=gen, device=device).mul_(WEIGHT_STD)
+        d = torch.randn(H, F, generator=gen, device=device).mul_(WEIGHT_STD)
+        slots.append(quantize_expert(g, u, d, shape.group_size))
+        del g, u, d
+    return slots

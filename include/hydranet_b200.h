@@ -1,0 +1,180 @@
+/*
+ * hydranet_b200.h -- C ABI of the B200 (sm_100a) INT4 mixture-of-experts path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream, never
+ * synchronises and never allocates device memory.  Kernels that need scratch
+ * take a caller-owned workspace whose size comes from the matching
+ * *_workspace_size() query (query on the device that will run the call).
+ * A workspace must be 256-byte aligned and zero-filled once when it is first
+ * allocated.  The kernels leave it re-usable: its front holds arrival counters
+ * that each call resets to zero, its back holds per-call data, so one
+ * workspace may serve calls of any shape whose size query it satisfies.
+ * One workspace must not be used by two launches that may overlap on the
+ * device.
+ *
+ * Return value: HN_OK (0) or an HN_ERR_* code; hn_last_error() gives the
+ * message of the last failing call on the calling host thread.
+ *
+ * Tensor conventions follow the reference's packed format
+ * (preprocess/pack_weights.py:133-181, cache/packed_expert_store.py:77-108):
+ *   packed  uint8  [N, K/2]   two nibbles per byte, low nibble = even k
+ *   scales  fp16   [N, K/group_size]
+ *   weight  W[n, k] = (nibble - 8) * scale[n, k / group_size]
+ * Only group_size == 128 is implemented (HN_ERR_UNSUPPORTED otherwise).
+ * Activations are fp16 or bf16 (HN_DTYPE_*), row-major with unit inner stride.
+ */
+#ifndef HYDRANET_B200_H
+#define HYDRANET_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define HN_API __attribute__((visibility("default")))
+#else
+#define HN_API
+#endif
+
+enum hn_status {
+  HN_OK = 0,
+  HN_ERR_INVALID = 1,      /* bad pointer / shape / argument          */
+  HN_ERR_UNSUPPORTED = 2,  /* valid, but not implemented on this path */
+  HN_ERR_CUDA = 3,         /* a CUDA runtime call failed              */
+  HN_ERR_WORKSPACE = 4     /* workspace smaller than required         */
+};
+
+enum hn_dtype { HN_DTYPE_F32 = 0, HN_DTYPE_F16 = 1, HN_DTYPE_BF16 = 2 };
+
+/* Router kinds (see hn_moe_route). */
+enum hn_router_kind {
+  HN_ROUTER_SOFTMAX_TOPK = 0, /* Mixtral: model/router.py:73-130        */
+  HN_ROUTER_SIGMOID_TOPK = 1  /* GLM-4.5: model/glm4.py:261-309         */
+};
+
+/* Device-memory pointer table of one expert: the six tensors of a
+ * GpuExpertSlot (cache/packed_expert_store.py:136-162). */
+typedef struct hn_expert_ptrs {
+  const uint8_t* gate_packed;  /* [F, H/2] */
+  const uint16_t* gate_scales; /* [F, H/128] fp16 */
+  const uint8_t* up_packed;    /* [F, H/2] */
+  const uint16_t* up_scales;   /* [F, H/128] fp16 */
+  const uint8_t* down_packed;  /* [H, F/2] */
+  const uint16_t* down_scales; /* [H, F/128] fp16 */
+} hn_expert_ptrs;
+
+HN_API int hn_abi_version(void);
+HN_API const char* hn_last_error(void);
+
+/* Number of SMs the library sizes its persistent grids for (device 'device'). */
+HN_API int hn_device_sm_count(int device);
+
+/* ---------------------------------------------------------------------------
+ * Packing (replaces ExpertWeightPacker.quantize_tensor / dequantize_tensor,
+ * preprocess/pack_weights.py:133-181 and :230-268).
+ * ------------------------------------------------------------------------- */
+
+/* w [rows, cols] (fp32 or fp16, w_dtype) -> packed [rows, cols/2], scales
+ * [rows, cols/group] fp16.  Bit-identical to the reference packer. */
+HN_API int hn_quantize_int4(const void* w, int w_dtype, int64_t rows, int64_t cols, int group_size,
+                     uint8_t* packed, uint16_t* scales, void* stream);
+
+/* Raw nibbles 0..15 as uint8 [rows, cols] (debug/parity helper). */
+HN_API int hn_unpack_int4(const uint8_t* packed, int64_t rows, int64_t cols, uint8_t* out, void* stream);
+
+/* fp16 dequantisation (nibble - 8) * scale, as GpuExpertSlot._dequant_tensor
+ * (cache/packed_expert_store.py:287-315).  out: fp16 [rows, cols]. */
+HN_API int hn_dequant_int4(const uint8_t* packed, const uint16_t* scales, int64_t rows, int64_t cols,
+                    int group_size, uint16_t* out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Drop-in kernels (kernels/int4_gemm.py, kernels/int4_expert_mlp.py)
+ * ------------------------------------------------------------------------- */
+
+/* silu(gate) * up, elementwise, fp32 math, output in dtype
+ * (replaces fused_silu_mul, kernels/int4_gemm.py:196-208, and silu_mul,
+ * kernels/int4_expert_mlp.py:189-210). */
+HN_API int hn_silu_mul(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream);
+
+/* out[M, N] = x[M, K] @ W^T with W given packed (replaces int4_linear,
+ * kernels/int4_gemm.py:124-172 and kernels/int4_expert_mlp.py:99-156).
+ * ldx / ldo are row strides in elements. */
+HN_API size_t hn_int4_linear_workspace_size(int64_t M, int64_t N, int64_t K);
+HN_API int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K,
+                   const uint8_t* w_packed, const uint16_t* w_scales, int64_t N, int group_size,
+                   void* out, int64_t ldo, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[T, H] = down(silu(gate(x)) * up(x)) in one fused two-phase pass
+ * (replaces expert_mlp_int4_fused, kernels/int4_gemm.py:211-254, and
+ * expert_mlp_int4 / expert_mlp_int4_from_slot, kernels/int4_expert_mlp.py:213-272). */
+HN_API size_t hn_expert_mlp_workspace_size(int64_t T, int64_t H, int64_t F);
+HN_API int hn_expert_mlp_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F,
+                       const uint8_t* gate_packed, const uint16_t* gate_scales,
+                       const uint8_t* up_packed, const uint16_t* up_scales,
+                       const uint8_t* down_packed, const uint16_t* down_scales, int group_size,
+                       void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Grouped MoE layer: router + dispatch + expert MLPs + weighted top-k combine
+ * (replaces TopKRouter.forward / GLM4SigmoidRouter.forward and the per-expert
+ * loops of MixtralMoELayer.forward, model/mixtral.py:259-370, and
+ * GLM4MoELayer.forward, model/glm4.py:365-473, routed part).
+ * ------------------------------------------------------------------------- */
+
+typedef struct hn_router_params {
+  int kind;                 /* hn_router_kind                                    */
+  int top_k;
+  const void* weight;       /* [E, H] router weight                              */
+  int weight_dtype;         /* hn_dtype of weight                                */
+  int logits_in_act_dtype;  /* 1: round logits to the activation dtype before use
+                               (Mixtral gate Linear runs in the model dtype,
+                               model/router.py:102); 0: float32 logits            */
+  const float* affinity_bonus; /* [E] or NULL: cache-affinity bonus per expert,
+                               applied when the normalised entropy exceeds
+                               entropy_threshold (model/router.py:132-175)         */
+  float entropy_threshold;
+  const float* correction_bias; /* [E] or NULL (sigmoid only): added to the scores
+                               for selection only                                  */
+  int norm_topk_prob;       /* sigmoid only (model/glm4.py:302-304)              */
+  float routed_scaling_factor; /* sigmoid only (model/glm4.py:307)                */
+} hn_router_params;
+
+HN_API size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int top_k);
+
+/* x [T, H] -> out [T, H] = sum_k w[t,k] * MLP_{idx[t,k]}(x[t]).
+ * experts: DEVICE pointer to E hn_expert_ptrs.  Optional outputs (may be NULL):
+ * topk_idx int32 [T, k], topk_w float32 [T, k] (already rounded to the
+ * activation dtype, as model/router.py:120 and model/glm4.py:309 cast them),
+ * logits float32 [T, E]. */
+HN_API int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
+                      const hn_router_params* router, const hn_expert_ptrs* experts,
+                      void* out, int32_t* topk_idx, float* topk_w, float* logits,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same as hn_moe_layer_int4 but with routing supplied by the caller
+ * (topk_idx int32 [T, k], topk_w float32 [T, k]); used for expert-parallel
+ * shards and for callers that route on their own. */
+HN_API int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
+                        int top_k, const int32_t* topk_idx, const float* topk_w,
+                        const hn_expert_ptrs* experts, void* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Router only: writes topk_idx/topk_w (and logits if non-NULL). */
+HN_API int hn_moe_route(const void* x, int dtype, int64_t T, int64_t H, int64_t E,
+                 const hn_router_params* router, int32_t* topk_idx, float* topk_w, float* logits,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Device-side error word of a workspace (bounded waits that timed out set it).
+ * Copies 4 bytes device->host on 'stream' and synchronises that stream. */
+HN_API int hn_workspace_error(const void* workspace, size_t workspace_bytes, int* error_code, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HYDRANET_B200_H */

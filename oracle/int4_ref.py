@@ -84,10 +84,12 @@ def dequantize_tensor(packed: np.ndarray, scales: np.ndarray, group_size: int = 
     (``preprocess/pack_weights.py:230-268``) and
     ``GpuExpertSlot._dequant_tensor`` (``cache/packed_expert_store.py:287-315``).
     """
-    q = unpack_int4(packed).astype(np.int16) - 8
+    q = unpack_int4(packed).astype(np.float32) - np.float32(8)
     out_f, in_f = q.shape
-    qg = q.reshape(out_f, in_f // group_size, group_size).astype(np.float16)
-    return (qg * scales.astype(np.float16)[:, :, None]).astype(np.float16).reshape(out_f, in_f)
+    qg = q.reshape(out_f, in_f // group_size, group_size)
+    # (n - 8) * scale is exact in float32 (a 4-bit integer times an fp16), so
+    # rounding the float32 product to fp16 equals the reference's fp16 multiply
+    return (qg * scales.astype(np.float32)[:, :, None]).astype(np.float16).reshape(out_f, in_f)
 
 
 @dataclass

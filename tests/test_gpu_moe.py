@@ -1,0 +1,191 @@
+"""GPU parity of the grouped MoE layer (router + dispatch + experts + combine).
+
+Routing indices must match the oracle exactly; a mismatch is tolerated only
+where the oracle's own top-k boundary is a near-tie (gap within one ulp of
+the logit dtype), which the test reports.  Outputs: rel-L2 <= 1e-2 (north
+star) and a tighter precision bound.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from hydranet_b200 import _lib, ops, synth
+from hydranet_b200.moe import MoELayerInt4, moe_experts
+from hydranet_b200.router import GLM4SigmoidRouter, TopKRouter
+from oracle import int4_ref as R
+from tests.gpu_util import act, device_moe, host_moe, oracle_experts, rel_l2, to_np32
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+TIGHT = 6e-3
+
+
+def check_indices(idx, ref_idx, ref_scores, k, ulp_rel):
+    mism = np.nonzero(np.any(np.sort(idx, 1) != np.sort(ref_idx, 1), axis=1))[0]
+    for t in mism:
+        s = np.sort(ref_scores[t])[::-1]
+        gap = s[k - 1] - s[k]
+        assert gap <= 2 * ulp_rel * abs(s[k - 1]) + 1e-30, f"token {t}: index mismatch with logit gap {gap}"
+    return len(mism)
+
+
+def mixtral_layer(table, rw, k, bonus=None):
+    r = TopKRouter(hidden_dim=table.hidden_dim, num_experts=len(table), experts_per_token=k).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        r.gate.weight.copy_(rw)
+    if bonus is not None:
+        r.enable_affinity_bonus = True
+        r.set_cache_checker(lambda e: bool(bonus[e] > 0))
+    return MoELayerInt4(r, table)
+
+
+def test_c1_golden_layer(lib, golden_dir):
+    """Config 1 (H=512, F=1024, E=8, top-2) on the fixture's inputs."""
+    g = dict(np.load(golden_dir / "c1_mixtral_layer.npz"))
+    shape = synth.MoEShape(512, 1024, 8, 2)
+    table, packed = host_moe(shape, 0)
+    x = act(g["x"], "bf16")
+    rw = torch.from_numpy(g["router_w"]).cuda().to(torch.bfloat16)
+    layer = mixtral_layer(table, rw, 2)
+    out, ro = layer(x.view(1, 4, 512), return_routing=True)
+    xi, wi = to_np32(x), to_np32(rw)
+    idx, w, logits = R.softmax_topk_router_ref(xi, wi, 2, "bf16")
+    check_indices(ro.expert_indices.view(4, 2).cpu().numpy(), idx, logits, 2, 2 ** -8)
+    ref = R.moe_combine_ref(xi, idx, w, oracle_experts(packed))
+    err = rel_l2(to_np32(out.view(4, 512)), ref)
+    assert err <= TOL and err <= TIGHT, err
+
+
+@pytest.mark.parametrize("T", [1, 8, 32, 64])
+def test_mixtral_shape_layer(lib, T):
+    """Config 2: Mixtral-8x7B MoE layer decode (H=4096, F=14336, E=8, top-2), bf16."""
+    shape = synth.MoEShape(4096, 14336, 8, 2)
+    table, packed = _mixtral_full()
+    x = torch.randn(T, 4096, generator=torch.Generator("cuda").manual_seed(T), device="cuda").to(torch.bfloat16)
+    rw = (torch.randn(8, 4096, generator=torch.Generator("cuda").manual_seed(99), device="cuda") * 0.02)
+    rw = rw.to(torch.bfloat16)
+    layer = mixtral_layer(table, rw, 2)
+    out, ro = layer(x, return_routing=True)
+    xi, wi = to_np32(x), to_np32(rw)
+    idx, w, logits = R.softmax_topk_router_ref(xi, wi, 2, "bf16")
+    n_tie = check_indices(ro.expert_indices.cpu().numpy(), idx, logits, 2, 2 ** -8)
+    use_idx = ro.expert_indices.cpu().numpy() if n_tie else idx
+    use_w = to_np32(ro.expert_weights) if n_tie else w
+    np.testing.assert_allclose(to_np32(ro.expert_weights), use_w, rtol=2 ** -7, atol=1e-6)
+    ref = R.moe_combine_ref(xi, use_idx, use_w, _mixtral_oracle())
+    err = rel_l2(to_np32(out), ref)
+    assert err <= TOL and err <= TIGHT, err
+
+
+_FULL = {}
+
+
+def _mixtral_full():
+    if "m" not in _FULL:
+        _FULL["m"] = device_moe(synth.MoEShape(4096, 14336, 8, 2), 1234)
+    return _FULL["m"]
+
+
+def _mixtral_oracle():
+    if "mo" not in _FULL:
+        _FULL["mo"] = oracle_experts(_mixtral_full()[1])
+    return _FULL["mo"]
+
+
+@pytest.mark.parametrize("bias", [False, True])
+def test_glm_shape_layer(lib, bias):
+    """Config 4 layer: GLM-4.5-Air shape (H=4096, F=1408, E=128, sigmoid top-8), T=32 bf16."""
+    shape = synth.MoEShape(4096, 1408, 128, 8)
+    if "g" not in _FULL:
+        _FULL["g"] = device_moe(shape, 4321)
+    table, packed = _FULL["g"]
+    T = 32
+    x = torch.randn(T, 4096, generator=torch.Generator("cuda").manual_seed(5), device="cuda").to(torch.bfloat16)
+    r = GLM4SigmoidRouter(hidden_dim=4096, num_experts=128, experts_per_token=8).cuda()
+    cb = None
+    if bias:
+        cb = torch.from_numpy(synth.host_correction_bias(3, 128)).cuda()
+        r.set_correction_bias(cb)
+    layer = MoELayerInt4(r, table)
+    out, ro = layer(x, return_routing=True)
+    xi, wi = to_np32(x), to_np32(r.weight)
+    idx, w, logits = R.sigmoid_topk_router_ref(xi, wi, 8, "bf16", correction_bias=None if cb is None else to_np32(cb))
+    sel = 1 / (1 + np.exp(-logits)) + (0 if cb is None else to_np32(cb)[None, :])
+    n_tie = check_indices(ro.expert_indices.cpu().numpy(), idx, sel, 8, 2 ** -22)
+    assert n_tie == 0
+    ref = R.moe_combine_ref(xi, idx, w, oracle_experts(packed, idx.ravel()))
+    err = rel_l2(to_np32(out), ref)
+    assert err <= TOL and err <= TIGHT, err
+    # module interface of the router alone matches the layer's routing
+    i2, w2 = r(x.view(1, T, 4096))
+    assert torch.equal(i2, ro.expert_indices) and torch.equal(w2, ro.expert_weights)
+
+
+@pytest.mark.parametrize("k", [1, 2, 3])
+def test_given_routing_with_duplicates(lib, k):
+    """Caller-supplied routing (expert-parallel shards use this); duplicate picks count twice,
+    as the reference loop does (``model/mixtral.py:329-368``)."""
+    shape = synth.MoEShape(512, 256, 6, k)
+    table, packed = host_moe(shape, 11)
+    T = 37
+    rng = np.random.default_rng(0)
+    idx = rng.integers(0, 6, size=(T, k)).astype(np.int32)
+    w = rng.random((T, k)).astype(np.float32)
+    x = act(rng.standard_normal((T, 512), dtype=np.float32), "bf16")
+    out = moe_experts(x, torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), table)
+    ref = R.moe_combine_ref(to_np32(x), idx.astype(np.int64), w, oracle_experts(packed))
+    assert rel_l2(to_np32(out), ref) <= TIGHT
+
+
+def test_affinity_bonus_routing(lib):
+    """Cache-affinity bonus (``model/router.py:132-175``) on a near-uniform router."""
+    shape = synth.MoEShape(512, 256, 8, 2)
+    table, packed = host_moe(shape, 21)
+    bonus = np.zeros(8, np.float32)
+    bonus[[0, 3, 5]] = 0.1
+    x = act(np.random.default_rng(1).standard_normal((16, 512), dtype=np.float32), "bf16")
+    rw = torch.from_numpy(synth.host_normal(2, (8, 512), 0.002)).cuda().to(torch.bfloat16)
+    layer = mixtral_layer(table, rw, 2, bonus=bonus)
+    out, ro = layer(x, return_routing=True)
+    idx, w, logits = R.softmax_topk_router_ref(to_np32(x), to_np32(rw), 2, "bf16", affinity_bonus=bonus)
+    check_indices(ro.expert_indices.cpu().numpy(), idx, logits, 2, 2 ** -8)
+    assert np.isin(ro.expert_indices.cpu().numpy(), [0, 3, 5]).mean() > 0.5
+    ref = R.moe_combine_ref(to_np32(x), idx, w, oracle_experts(packed))
+    assert rel_l2(to_np32(out), ref) <= TIGHT
+
+
+def test_layer_repeatable_and_error_word_clean(lib):
+    shape = synth.MoEShape(1024, 512, 16, 4)
+    table, _ = host_moe(shape, 31)
+    r = GLM4SigmoidRouter(hidden_dim=1024, num_experts=16, experts_per_token=4).cuda()
+    layer = MoELayerInt4(r, table)
+    x = torch.randn(50, 1024, device="cuda", dtype=torch.bfloat16)
+    outs = [layer(x) for _ in range(3)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    for ws in _lib.workspaces.all():
+        assert _lib.workspace_error(ws) == 0
+
+
+def test_cuda_graph_capture(lib):
+    """A decode layer has no host sync, so it can be captured and replayed."""
+    shape = synth.MoEShape(1024, 512, 8, 2)
+    table, _ = host_moe(shape, 41)
+    rw = torch.randn(8, 1024, device="cuda", dtype=torch.bfloat16) * 0.02
+    layer = mixtral_layer(table, rw, 2)
+    x = torch.randn(8, 1024, device="cuda", dtype=torch.bfloat16)
+    ref = layer(x)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        layer(x)  # allocate this stream's workspace outside capture
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            y = layer(x)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)
