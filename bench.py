@@ -121,29 +121,48 @@ class ClockSampler:
 # CPU oracle timing (the reference's dequant-then-matmul path, restated)
 # ---------------------------------------------------------------------------
 
-def cpu_oracle_time(T: int, budget_s: float = 20.0):
+class OracleLayer:
+    """The oracle's MoE layer at config 2 (the reference's dequant-then-matmul
+    path, restated in numpy float32).  Expert weights are dequantised INT4 values
+    (random nibbles times fp16 group scales), built once outside any timing,
+    as the reference's dequant mode registers float weights at load time."""
+
+    def __init__(self, T: int):
+        from concurrent.futures import ThreadPoolExecutor
+        from oracle import int4_ref as R
+        from hydranet_b200 import synth
+        self.R = R
+
+        def make(e):
+            rng = np.random.default_rng(1000 + e)
+            mats = []
+            for n, k in ((F, H), (F, H), (H, F)):
+                packed = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+                scales = (rng.random((n, k // 128), dtype=np.float32) * np.float32(0.005)).astype(np.float16)
+                mats += [packed, scales]
+            return R.DequantExpert.from_packed(*mats)
+
+        with ThreadPoolExecutor(max_workers=min(8, cpu_threads())) as ex:
+            self.experts = dict(enumerate(ex.map(make, range(E))))
+        self.rw = synth.host_normal(99, (E, H), 0.02)
+        self.x = R.round_to_bf16(np.random.default_rng(0).standard_normal((T, H), dtype=np.float32))
+        self.T = T
+
+    def step(self):
+        idx, w, _ = self.R.softmax_topk_router_ref(self.x, self.rw, TOPK, "bf16")
+        return self.R.moe_combine_ref(self.x, idx, w, self.experts)
+
+
+def cpu_oracle_time(T: int, budget_s: float = 15.0, max_steps: int = 50):
     """tok/s of the oracle MoE layer on the host cores over a bounded sample."""
-    from oracle import int4_ref as R
-    from hydranet_b200 import synth
-    rng = np.random.default_rng(0)
-    shape = synth.MoEShape(H, F, E, TOPK)
-    experts = {}
-    for e in range(E):
-        # dequantised float32 experts, prepared outside the timed region (the
-        # reference registers dequantised weights at load time in dequant mode)
-        g, u, d = (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)
-                   for s in ((F, H), (F, H), (H, F)))
-        experts[e] = R.DequantExpert.from_packed(*R.quantize_tensor(g), *R.quantize_tensor(u), *R.quantize_tensor(d))
-        del g, u, d
-    rw = synth.host_normal(99, (E, H), 0.02)
-    x = R.round_to_bf16(rng.standard_normal((T, H), dtype=np.float32))
+    layer = OracleLayer(T)
+    layer.step()  # warm-up
     steps, t0 = 0, time.perf_counter()
     while True:
-        idx, w, _ = R.softmax_topk_router_ref(x, rw, TOPK, "bf16")
-        R.moe_combine_ref(x, idx, w, experts)
+        layer.step()
         steps += 1
         el = time.perf_counter() - t0
-        if el > budget_s or steps >= 50:
+        if el > budget_s or steps >= max_steps:
             break
     return T * steps / el, steps, el
 
@@ -160,21 +179,22 @@ def run_reference(args):
     if rank != 0:
         return
     T = args.tokens
-    vals = []
+    layer = OracleLayer(T)
     for _ in range(args.warmup):
-        cpu_oracle_time(T, budget_s=0.0)
+        layer.step()
+    t0 = time.perf_counter()
     for _ in range(args.steps):
-        v, n, el = cpu_oracle_time(T, budget_s=args.ref_budget)
-        vals.append(v)
-    v = statistics.median(vals)
+        layer.step()
+    el = time.perf_counter() - t0
+    v = T * args.steps / el
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / v, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "tokens": T, "hidden": H, "ffn": F, "experts": E, "top_k": TOPK,
                        "group_size": 128},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
-                             "sample": f"{args.steps} samples x up to {args.ref_budget:.0f}s of oracle layer steps "
-                                       f"(numpy float32, dequant-then-matmul) at T={T}"},
+                             "sample": f"{args.steps} oracle layer steps at T={T} (numpy float32 "
+                                       f"dequant-then-matmul, weights dequantised before timing)"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -192,6 +212,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=HEADLINE_T)
     ap.add_argument("--ref-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", type=str, default=",".join(map(str, SWEEP)),
+                    help="comma-separated token batches to time (default 1,8,32,64)")
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="distinct layers rotated per step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -216,8 +239,10 @@ def main():
     _lib.load()
 
     shape = synth.MoEShape(H, F, E, TOPK)
+    sweep = tuple(int(t) for t in args.sweep.split(","))
+    n_layers = max(1, args.layers)
     layers = []
-    for li in range(N_LAYERS):
+    for li in range(n_layers):
         table = ExpertTable(synth.device_experts(1000 * rank + li, shape, dev))
         r = TopKRouter(hidden_dim=H, num_experts=E, experts_per_token=TOPK).to(dev, torch.bfloat16)
         with torch.no_grad():
@@ -239,9 +264,9 @@ def main():
         return float(t.item())
 
     results = {}
-    for T in SWEEP:
+    for T in sweep:
         xs = [torch.randn(T, H, generator=torch.Generator(dev).manual_seed(T * 10 + i), device=dev)
-              .to(torch.bfloat16) for i in range(N_LAYERS)]
+              .to(torch.bfloat16) for i in range(n_layers)]
         # routing of each layer's input (fixed per layer) -> touched experts -> algorithmic bytes
         touched = []
         with torch.no_grad():
@@ -264,7 +289,7 @@ def main():
                 graphs.append(g)
         torch.cuda.current_stream(dev).wait_stream(s)
         for i in range(args.warmup):
-            graphs[i % N_LAYERS].replay()
+            graphs[i % n_layers].replay()
         torch.cuda.synchronize(dev)
         barrier()
         torch.cuda.synchronize(dev)
@@ -272,7 +297,7 @@ def main():
         with ClockSampler(local) as clk:
             ev0.record()
             for i in range(args.steps):
-                graphs[i % N_LAYERS].replay()
+                graphs[i % n_layers].replay()
             ev1.record()
             torch.cuda.synchronize(dev)
         ms = ev0.elapsed_time(ev1) / args.steps
@@ -286,22 +311,22 @@ def main():
         torch.cuda.synchronize(dev)
 
     # end-to-end through the public API: pinned host input -> device -> layer -> host
-    T = args.tokens if args.tokens in results else HEADLINE_T
+    T = args.tokens if args.tokens in results else max(results)
     x_host = [torch.randn(T, H, generator=torch.Generator().manual_seed(5 + i)).to(torch.bfloat16).pin_memory()
-              for i in range(N_LAYERS)]
+              for i in range(n_layers)]
     x_dev = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
     out_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
     with torch.no_grad():
         for i in range(args.warmup):
-            x_dev.copy_(x_host[i % N_LAYERS], non_blocking=True)
-            out_host.copy_(layers[i % N_LAYERS](x_dev), non_blocking=True)
+            x_dev.copy_(x_host[i % n_layers], non_blocking=True)
+            out_host.copy_(layers[i % n_layers](x_dev), non_blocking=True)
         torch.cuda.synchronize(dev)
         barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()
         for i in range(args.steps):
-            x_dev.copy_(x_host[i % N_LAYERS], non_blocking=True)
-            out_host.copy_(layers[i % N_LAYERS](x_dev), non_blocking=True)
+            x_dev.copy_(x_host[i % n_layers], non_blocking=True)
+            out_host.copy_(layers[i % n_layers](x_dev), non_blocking=True)
         ev1.record()
         torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
@@ -321,8 +346,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": hr["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, weights ~N(0,0.02) INT4 g128)",
             "config": {"workload": WORKLOAD, "tokens": T, "hidden": H, "ffn": F, "experts": E, "top_k": TOPK,
-                       "group_size": 128, "layers_rotated": N_LAYERS, "l2": "weights per step > L2 (126 MB), "
-                       "4 distinct layers rotated", "cuda_graph": True,
+                       "group_size": 128, "layers_rotated": n_layers, "l2": "weights per step > L2 (126 MB), "
+                       f"{n_layers} distinct layers rotated", "cuda_graph": True,
                        "parallelism": "replicas" if world > 1 else "single"},
             "roofline": {"bound": "hbm", "achieved": hr["gbs"], "peak": hbm_peak, "unit": "GB/s",
                          "frac": hr["frac"], "traffic": None, "kernel": "moe layer pass (route+gateup+down)",

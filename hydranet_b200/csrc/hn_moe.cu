@@ -69,14 +69,13 @@ struct Plan {
 __host__ __device__ constexpr int seg_tokens(int nt) { return 8 * nt; }
 
 // ---------------------------------------------------------------------------
-// Activation staging.  For k-group g, token t, the chunk holds, for each tig
-// (= lane & 3 of the consuming thread) 64 bytes = 4 units of 16 bytes; unit
-// q of tig covers x[32*tig + 8*q + i], i = 0..7, packed as
-//   { (x0, x4), (x2, x6), (x1*s, x5*s), (x3*s, x7*s) }  (s = odd-k scale)
-// which is exactly the B fragment pair {b0, b1} of the two MMA k-steps that
-// consume word q of the thread's A data (see compute_iter).  Unit q of tig
-// is stored at slot q ^ (tig & 2) so that the 8 lanes of each quarter-warp
-// hit distinct shared-memory banks (the chunk stride, 272 B, is 17 granules).
+// Activation staging.  For k-group g and token t a 272-byte chunk holds 16
+// units of 16 bytes followed by the fp32 correction C (and 12 bytes of pad).
+// Unit c covers x[128*g + 8*c + i], i = 0..7, packed as bf16/f16 pairs
+//   { (x0, x4), (x2, x6), (x1*s, x5*s), (x3*s, x7*s) }   (s = odd-k scale)
+// i.e. logical k 8c..8c+7 of the MMA, matching the TMEM columns the weight
+// dequantiser writes for the same 8 nibbles (dequant_word).  A unit is one
+// 16-byte row of a K-major core matrix of the tensor-core B operand.
 // ---------------------------------------------------------------------------
 template <typename Tr>
 __device__ __forceinline__ void pack_unit(const float (&v)[8], uint4& out, float& cpart) {
@@ -96,7 +95,6 @@ __device__ __forceinline__ void pack_unit(const float (&v)[8], uint4& out, float
   out = u;
 }
 
-__device__ __forceinline__ int chunk_slot(int tig, int q) { return tig * 64 + ((q ^ (tig & 2)) << 4); }
 
 // ---------------------------------------------------------------------------
 // Router + staging + plan
@@ -147,15 +145,15 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   // 1. staged activations + per-group correction C
   const int units = a.H / 8;
   for (int u = tid; u < units; u += 256) {
-    const int g = u >> 4, tig = (u >> 2) & 3, q = u & 3;
-    const int k0 = g * 128 + tig * 32 + q * 8;
+    const int g = u >> 4, ch = u & 15;
+    const int k0 = g * 128 + ch * 8;
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = xs[k0 + i];
     uint4 packed;
     float cp;
     pack_unit<Tr>(v, packed, cp);
-    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk + chunk_slot(tig, q)) = packed;
+    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk + ch * 16) = packed;
     cpart[u] = cp;
   }
   __syncthreads();
@@ -374,16 +372,6 @@ struct EngineArgs {
   int P;
 };
 
-template <int NT, int SB, int DA>
-struct EngineSmem {
-  static constexpr int kSeg = seg_tokens(NT);
-  static constexpr int kHdr = 256;
-  static constexpr int kB = SB * kSeg * kChunk;
-  static constexpr int kA = kNW * DA * 2048;
-  static constexpr int kH = 128 * (kSeg + 1) * 4 + kSeg * 16 * 4;
-  static constexpr int kTotal = kHdr + kB + kA + kH;
-};
-
 template <int KIND>
 struct TileMap {
   // GATEUP tiles are segment-major, DOWN tiles row-tile-major.
@@ -398,124 +386,96 @@ struct TileMap {
   }
 };
 
-template <typename Tr, int NT>
-__device__ __forceinline__ void compute_iter(const uint4 (&A)[4], const uint8_t* bstage, int nact, int g, int tig,
-                                             float (&P0)[NT][4], float (&P1)[NT][4]) {
-  const int swz = tig & 2;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t w0g = (&A[0].x)[q], w0h = (&A[1].x)[q], w1g = (&A[2].x)[q], w1h = (&A[3].x)[q];
-    uint4 bf[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-      if (nt < nact)
-        bf[nt] = *reinterpret_cast<const uint4*>(bstage + (nt * 8 + g) * kChunk + tig * 64 + ((q ^ swz) << 4));
-    const uint32_t M = Tr::kMagic;
-    // k-step 1: nibbles (0,4) and (2,6)
-    {
-      uint32_t fa[4] = {lop3_and_or<0x000F000Fu>(w0g, M), lop3_and_or<0x000F000Fu>(w0h, M),
-                        lop3_and_or<0x000F000Fu>(w0g >> 8, M), lop3_and_or<0x000F000Fu>(w0h >> 8, M)};
-      uint32_t fb[4] = {lop3_and_or<0x000F000Fu>(w1g, M), lop3_and_or<0x000F000Fu>(w1h, M),
-                        lop3_and_or<0x000F000Fu>(w1g >> 8, M), lop3_and_or<0x000F000Fu>(w1h >> 8, M)};
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        if (nt < nact) {
-          mma16816<Tr>(P0[nt], fa, bf[nt].x, bf[nt].y);
-          mma16816<Tr>(P1[nt], fb, bf[nt].x, bf[nt].y);
-        }
-    }
-    // k-step 2: nibbles (1,5) and (3,7)
-    {
-      uint32_t fa[4], fb[4];
-      if constexpr (Tr::kMagic == BF16::kMagic) {
-        fa[0] = lop3_and_or<0x00780078u>(w0g >> 1, M);
-        fa[1] = lop3_and_or<0x00780078u>(w0h >> 1, M);
-        fa[2] = lop3_and_or<0x00780078u>(w0g >> 9, M);
-        fa[3] = lop3_and_or<0x00780078u>(w0h >> 9, M);
-        fb[0] = lop3_and_or<0x00780078u>(w1g >> 1, M);
-        fb[1] = lop3_and_or<0x00780078u>(w1h >> 1, M);
-        fb[2] = lop3_and_or<0x00780078u>(w1g >> 9, M);
-        fb[3] = lop3_and_or<0x00780078u>(w1h >> 9, M);
-      } else {
-        fa[0] = lop3_and_or<0x00F000F0u>(w0g, M);
-        fa[1] = lop3_and_or<0x00F000F0u>(w0h, M);
-        fa[2] = lop3_and_or<0x00F000F0u>(w0g >> 8, M);
-        fa[3] = lop3_and_or<0x00F000F0u>(w0h >> 8, M);
-        fb[0] = lop3_and_or<0x00F000F0u>(w1g, M);
-        fb[1] = lop3_and_or<0x00F000F0u>(w1h, M);
-        fb[2] = lop3_and_or<0x00F000F0u>(w1g >> 8, M);
-        fb[3] = lop3_and_or<0x00F000F0u>(w1h >> 8, M);
-      }
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        if (nt < nact) {
-          mma16816<Tr>(P0[nt], fa, bf[nt].z, bf[nt].w);
-          mma16816<Tr>(P1[nt], fb, bf[nt].z, bf[nt].w);
-        }
-    }
-  }
-}
+// Shared-memory plan of the tcgen05 engine.
+//   token operand ring: SB stages of [17 chunks][N tokens][16 B]; chunk c < 16
+//     holds logical k [8c, 8c+8) of each token, chunk 16 its correction C.
+//     For MMA k-step s the K-major core matrices are chunks 2s and 2s+1:
+//     LBO (K direction) = 16*N bytes, SBO (8-token blocks) = 128 bytes.
+//   weight ring: per row thread DA slots of 64 B (one 128-wide k-group).
+//   htile / cpart: epilogue staging.
+template <int N, int SB, int DA>
+struct TcSmem {
+  static constexpr int kHdr = 512;
+  static constexpr int kBStage = 17 * N * 16;
+  static constexpr int kB = SB * kBStage;
+  static constexpr int kA = kNW * DA * 2048;
+  static constexpr int kH = 128 * (N + 1) * 4 + N * 16 * 4;
+  static constexpr int kTotal = kHdr + kB + kA + kH;
+};
 
-// Per-warp view of one tile: segment, rows and pointers.
-struct TileView {
+// TMEM columns: A stages [0, 256) = 2 stages x {A0, A1} x 64 columns (128 k of
+// bf16 pairs); D stages [256, 256 + 4N) = 2 stages x {A0, A1} x N fp32 columns.
+constexpr int kTmemCols = 512;
+constexpr int kTcThreads = (kNW + 2) * 32;  // 8 row warps, 1 producer warp, 1 MMA warp
+
+// Per-thread view of the tile rows: thread (matrix j, row r) of a tile.
+struct RowView {
   int seg, rt, m, p0;
-  const uint8_t* a[4];   // A0 row g, A0 row g+8, A1 row g, A1 row g+8 (+ tig*16)
-  const uint16_t* s[4];  // matching scale rows
+  const uint8_t* a;   // this thread's weight row (+ group * 64)
+  const uint16_t* s;  // this thread's scale row (+ group)
 };
 
 template <int KIND>
-__device__ __forceinline__ void load_tile(const EngineArgs& a, int tile, int n_segs, int warp, int g, int tig,
-                                          TileView& v) {
+__device__ __forceinline__ void load_rowview(const EngineArgs& a, int tile, int n_segs, int j, int r, RowView& v) {
   TileMap<KIND>::split(tile, a.n_rt, n_segs, v.seg, v.rt);
   const int4 sg = a.segs[v.seg];
   v.m = sg.z;
   v.p0 = sg.y;
   const hn_expert_ptrs ep = a.table ? a.table[sg.x] : a.single;
-  const uint8_t* A0;
-  const uint8_t* A1;
-  const uint16_t* S0;
-  const uint16_t* S1;
-  int r[4];
+  const uint8_t* A;
+  const uint16_t* S;
+  int row;
   if (KIND == KIND_GATEUP) {
-    A0 = ep.gate_packed;
-    S0 = ep.gate_scales;
-    A1 = ep.up_packed;
-    S1 = ep.up_scales;
-    const int rb = v.rt * 128 + warp * 16 + g;
-    r[0] = rb;
-    r[1] = rb + 8;
-    r[2] = rb;
-    r[3] = rb + 8;
+    A = j ? ep.up_packed : ep.gate_packed;
+    S = j ? ep.up_scales : ep.gate_scales;
+    row = v.rt * 128 + r;
   } else {
-    A0 = A1 = ep.down_packed;
-    S0 = S1 = ep.down_scales;
-    const int rb = v.rt * 256 + warp * 32 + g;
-    r[0] = rb;
-    r[1] = rb + 8;
-    r[2] = rb + 16;
-    r[3] = rb + 24;
+    A = ep.down_packed;
+    S = ep.down_scales;
+    row = v.rt * 256 + j * 128 + r;
   }
-  const int64_t rowb = a.K / 2;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int rr = min(r[i], a.N - 1);  // rows past N load row N-1 and are never stored
-    v.a[i] = (i < 2 ? A0 : A1) + (int64_t)rr * rowb + tig * 16;
-    v.s[i] = (i < 2 ? S0 : S1) + (int64_t)rr * a.G;
+  row = min(row, a.N - 1);  // rows past N load row N-1 and are never stored
+  v.a = A + (int64_t)row * (a.K / 2);
+  v.s = S + (int64_t)row * a.G;
+}
+
+// Dequantise one 32-bit word (8 nibbles of k = 8w..8w+7) into 4 TMEM columns of
+// bf16/f16 pairs: (n0,n4) (n2,n6) as 2^e+n, (n1,n5) (n3,n7) as 2^e+8n (bf16) or
+// 2^e+16n (f16).
+template <typename Tr>
+__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t* o) {
+  const uint32_t M = Tr::kMagic;
+  o[0] = lop3_and_or<0x000F000Fu>(w, M);
+  o[1] = lop3_and_or<0x000F000Fu>(w >> 8, M);
+  if constexpr (Tr::kMagic == BF16::kMagic) {
+    o[2] = lop3_and_or<0x00780078u>(w >> 1, M);
+    o[3] = lop3_and_or<0x00780078u>(w >> 9, M);
+  } else {
+    o[2] = lop3_and_or<0x00F000F0u>(w, M);
+    o[3] = lop3_and_or<0x00F000F0u>(w >> 8, M);
   }
 }
 
-template <typename Tr, int NT, int KIND, int EPI, int SB, int DA, int MINB>
-__global__ void __launch_bounds__(kEngineThreads, MINB) engine_kernel(const __grid_constant__ EngineArgs a) {
-  using L = EngineSmem<NT, SB, DA>;
-  constexpr int SEG = L::kSeg;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + SB;
-  int* bcast = reinterpret_cast<int*>(empty + SB);
+template <typename Tr, int N, int KIND, int EPI, int SB, int DA>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_constant__ EngineArgs a) {
+  using L = TcSmem<N, SB, DA>;
+  constexpr int SA = 2, SD = 2, LOOK = 2;
+  static_assert(LOOK <= SB - 1, "producer look-ahead must leave a free stage");
+  constexpr uint32_t IDESC = umma_idesc<Tr, 128, N>();
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* a_full = bars;       // [SA] row threads -> MMA
+  uint64_t* a_empty = bars + 2;  // [SA] MMA commit -> row threads
+  uint64_t* d_full = bars + 4;   // [SD] MMA commit -> row threads
+  uint64_t* d_empty = bars + 6;  // [SD] row threads -> MMA
+  uint64_t* b_full = bars + 8;   // [SB] producer -> MMA
+  uint64_t* b_empty = bars + 24; // [SB] row threads -> producer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
+  int* bcast = reinterpret_cast<int*>(bars + 41);
   uint8_t* bst = smem + L::kHdr;
   uint8_t* ast = bst + L::kB;
   float* htile = reinterpret_cast<float*>(ast + L::kA);
-  float* cpart = htile + 128 * (SEG + 1);
+  float* cpart = htile + 128 * (N + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_segs = *a.n_segs;
@@ -530,31 +490,52 @@ __global__ void __launch_bounds__(kEngineThreads, MINB) engine_kernel(const __gr
   auto begin_of = [&](int64_t cc) -> int64_t { return cc * NI / P; };
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(smem_u32(&a_full[s]), kNW * 32);
+      mbar_init(smem_u32(&a_empty[s]), 1);
+    }
+    for (int s = 0; s < SD; ++s) {
+      mbar_init(smem_u32(&d_full[s]), 1);
+      mbar_init(smem_u32(&d_empty[s]), kNW * 32);
+    }
     for (int s = 0; s < SB; ++s) {
-      mbar_init(smem_u32(&full[s]), 1);
-      mbar_init(smem_u32(&empty[s]), kNW);
+      mbar_init(smem_u32(&b_full[s]), 32);
+      mbar_init(smem_u32(&b_empty[s]), kNW * 32);
     }
     fence_barrier_init();
   }
+  if (warp == kNW + 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
 
   if (warp == kNW) {
-    // ------------------------------ producer ------------------------------
+    // ------------------------- producer: token operand -------------------------
     int tile = (int)(b0 / a.G), grp = (int)(b0 - (int64_t)tile * a.G);
     int seg, rt;
     TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
     int4 sg = a.segs[seg];
-    for (int64_t it = b0, k = 0; it < b1; ++it, ++k) {
+    int64_t k = 0;
+    for (int64_t it = b0; it < b1; ++it, ++k) {
       const int stage = (int)(k % SB);
-      const uint32_t ph = (uint32_t)((k / SB) & 1);
-      if (k >= SB) mbar_wait(smem_u32(&empty[stage]), ph ^ 1u, a.err);
+      if (k >= SB) mbar_wait(smem_u32(&b_empty[stage]), (uint32_t)(((k / SB) - 1) & 1), a.err);
       const int m = sg.z;
-      if (lane == 0) mbar_arrive_expect_tx(smem_u32(&full[stage]), (uint32_t)(m * kChunk));
-      __syncwarp();
-      if (lane < m) {
-        const int row = a.b_use_tok ? a.a_tok[sg.y + lane] : sg.y + lane;
-        const uint8_t* src = a.bsrc + (int64_t)grp * a.b_gstride + (int64_t)row * kChunk;
-        bulk_g2s(smem_u32(bst + (stage * SEG + lane) * kChunk), src, kChunk, smem_u32(&full[stage]));
+      uint8_t* dst = bst + stage * L::kBStage;
+      for (int t = lane; t < m * 17; t += 32) {
+        const int tok = t / 17, ch = t - tok * 17;
+        const int row = a.b_use_tok ? a.a_tok[sg.y + tok] : sg.y + tok;
+        cp_async16(smem_u32(dst + 16 * (N * ch + tok)),
+                   a.bsrc + (int64_t)grp * a.b_gstride + (int64_t)row * kChunk + ch * 16);
+      }
+      cp_async_commit();
+      if (k >= LOOK) {
+        cp_async_wait<LOOK>();
+        fence_proxy_async_smem();  // generic-proxy writes -> read by the tensor core (async proxy)
+        mbar_arrive(smem_u32(&b_full[(k - LOOK) % SB]));
       }
       if (++grp == a.G) {
         grp = 0;
@@ -565,267 +546,275 @@ __global__ void __launch_bounds__(kEngineThreads, MINB) engine_kernel(const __gr
         }
       }
     }
-    return;
-  }
-
-  // -------------------------------- consumers --------------------------------
-  const int g = lane >> 2, tig = lane & 3;
-  constexpr int kConsumers = kNW * 32;
-  // prefetch cursor
-  int pf_tile = (int)(b0 / a.G), pf_grp = (int)(b0 - (int64_t)pf_tile * a.G);
-  int64_t pf_it = b0;
-  TileView pv;
-  load_tile<KIND>(a, pf_tile, n_segs, warp, g, tig, pv);
-  uint8_t* aw = ast + warp * DA * 2048;
-  auto issue_a = [&](int slot) {
-    if (pf_it < b1) {
-      const uint32_t dst = smem_u32(aw + slot * 2048 + lane * 16);
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    for (int64_t kk = (k > LOOK ? k - LOOK : 0); kk < k; ++kk) mbar_arrive(smem_u32(&b_full[kk % SB]));
+  } else if (warp == kNW + 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      int64_t k = 0;
+      for (int64_t it = b0; it < b1; ++it, ++k) {
+        const int sa = (int)(k % SA), sd = (int)(k % SD), sb = (int)(k % SB);
+        mbar_wait(smem_u32(&a_full[sa]), (uint32_t)((k / SA) & 1), a.err);
+        mbar_wait(smem_u32(&b_full[sb]), (uint32_t)((k / SB) & 1), a.err);
+        if (k >= SD) mbar_wait(smem_u32(&d_empty[sd]), (uint32_t)(((k / SD) - 1) & 1), a.err);
+        tc_fence_after();
+        const uint32_t bbase = smem_u32(bst + sb * L::kBStage);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) cp_async16(dst + j * 512, pv.a[j] + pf_grp * 64);
-    }
-    cp_async_commit();
-    if (pf_it < b1) {
-      ++pf_it;
-      if (++pf_grp == a.G) {
-        pf_grp = 0;
-        ++pf_tile;
-        if (pf_it < b1) load_tile<KIND>(a, pf_tile, n_segs, warp, g, tig, pv);
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int s = 0; s < 8; ++s) {
+            const uint64_t bdesc = umma_sdesc_noswizzle(bbase + s * 32 * N, 16 * N, 128);
+            umma_ts(tbase + 256 + sd * 2 * N + j * N, tbase + sa * 128 + j * 64 + s * 8, bdesc, IDESC,
+                    s > 0 ? 1u : 0u);
+          }
+        umma_commit(smem_u32(&a_empty[sa]));
+        umma_commit(smem_u32(&d_full[sd]));
       }
     }
-  };
-#pragma unroll 1
-  for (int i = 0; i < DA; ++i) issue_a(i);
-
-  int tile = (int)(b0 / a.G), grp = (int)(b0 - (int64_t)tile * a.G);
-  TileView cv;
-  load_tile<KIND>(a, tile, n_segs, warp, g, tig, cv);
-  float acc0[NT][4], acc1[NT][4], P0[NT][4], P1[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc0[nt][j] = acc1[nt][j] = P0[nt][j] = P1[nt][j] = 0.f;
-
-#pragma unroll 1
-  for (int64_t it = b0, k = 0; it < b1; ++it, ++k) {
-    const int stage = (int)(k % SB);
-    const uint32_t ph = (uint32_t)((k / SB) & 1);
-    const int aslot = (int)(k % DA);
-    // group scales (fp16) of the four rows
-    float sc[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) sc[j] = __half2float(__ushort_as_half(__ldg(cv.s[j] + grp)));
-    cp_async_wait<DA - 1>();
-    uint4 A[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) A[j] = *reinterpret_cast<const uint4*>(aw + aslot * 2048 + j * 512 + lane * 16);
-    mbar_wait(smem_u32(&full[stage]), ph, a.err);
-    const uint8_t* bstage = bst + stage * SEG * kChunk;
-    const int nact = (cv.m + 7) >> 3;
-    float cl[NT], ch[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      cl[nt] = ch[nt] = 0.f;
-      if (nt < nact) {
-        cl[nt] = *reinterpret_cast<const float*>(bstage + (nt * 8 + 2 * tig) * kChunk + 256);
-        ch[nt] = *reinterpret_cast<const float*>(bstage + (nt * 8 + 2 * tig + 1) * kChunk + 256);
-      }
-    }
-    compute_iter<Tr, NT>(A, bstage, nact, g, tig, P0, P1);
     __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
-    issue_a(aslot);
+  } else {
+    // ------------------------------- row threads -------------------------------
+    const int j = warp >> 2, q = warp & 3, r = q * 32 + lane;
+    const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
+    constexpr int kRows = kNW * 32;
+    uint8_t* aw = ast + warp * DA * 2048 + lane * 16;
+    // prefetch cursor
+    int pf_tile = (int)(b0 / a.G), pf_grp = (int)(b0 - (int64_t)pf_tile * a.G);
+    int64_t pf_it = b0;
+    RowView pv;
+    load_rowview<KIND>(a, pf_tile, n_segs, j, r, pv);
+    auto issue_a = [&](int slot) {
+      if (pf_it < b1) {
+        const uint32_t dst = smem_u32(aw + slot * 2048);
+        const uint8_t* src = pv.a + pf_grp * 64;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      if (nt < nact) {
-        acc0[nt][0] += sc[0] * (P0[nt][0] - cl[nt]);
-        acc0[nt][1] += sc[0] * (P0[nt][1] - ch[nt]);
-        acc0[nt][2] += sc[1] * (P0[nt][2] - cl[nt]);
-        acc0[nt][3] += sc[1] * (P0[nt][3] - ch[nt]);
-        acc1[nt][0] += sc[2] * (P1[nt][0] - cl[nt]);
-        acc1[nt][1] += sc[2] * (P1[nt][1] - ch[nt]);
-        acc1[nt][2] += sc[3] * (P1[nt][2] - cl[nt]);
-        acc1[nt][3] += sc[3] * (P1[nt][3] - ch[nt]);
+        for (int i = 0; i < 4; ++i) cp_async16(dst + i * 512, src + i * 16);
       }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) P0[nt][j] = P1[nt][j] = 0.f;
-    }
+      cp_async_commit();
+      if (pf_it < b1) {
+        ++pf_it;
+        if (++pf_grp == a.G) {
+          pf_grp = 0;
+          ++pf_tile;
+          if (pf_it < b1) load_rowview<KIND>(a, pf_tile, n_segs, j, r, pv);
+        }
+      }
+    };
+#pragma unroll 1
+    for (int i = 0; i < DA; ++i) issue_a(i);
 
-    const bool tile_end = (grp == a.G - 1) || (it == b1 - 1);
-    if (tile_end) {
-      // ---------------- finish this CTA's piece of the tile ----------------
-      const int64_t ts = (int64_t)tile * a.G, te = ts + a.G;
-      bool own = true;
-      if (!(b0 <= ts && b1 >= te)) {
-        const int slot = (ts <= b0) ? 0 : 1;
-        float* dst = a.part + ((((int64_t)c * 2 + slot) * kNW + warp) * (8 * NT)) * 32 + lane;
+    int tile = (int)(b0 / a.G), grp = (int)(b0 - (int64_t)tile * a.G);
+    RowView cv;
+    load_rowview<KIND>(a, tile, n_segs, j, r, cv);
+    float acc[N];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
+    for (int n = 0; n < N; ++n) acc[n] = 0.f;
+
+    // flush of k-group kk: acc += scale * (D - C) for the active 8-token blocks
+    auto flush = [&](int64_t kk, float scale, int m) {
+      const int sd = (int)(kk % SD), sb = (int)(kk % SB);
+      mbar_wait(smem_u32(&d_full[sd]), (uint32_t)((kk / SD) & 1), a.err);
+      tc_fence_after();
+      float d[N];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            dst[((0 * NT + nt) * 4 + j) * 32] = acc0[nt][j];
-            dst[((1 * NT + nt) * 4 + j) * 32] = acc1[nt][j];
-          }
-        __threadfence();
-        named_bar_sync(1, kConsumers);
-        const int64_t c0 = cta_of(ts), c1 = cta_of(te - 1);
-        if (threadIdx.x == 0) bcast[0] = (atomicAdd(&a.tile_ctr[tile], 1) == (int)(c1 - c0));
-        named_bar_sync(1, kConsumers);
-        own = bcast[0] != 0;
-        if (own) {
+      for (int blk = 0; blk < N / 8; ++blk) {
+        float t8[8];
+        if (blk * 8 < m) tmem_ld8(tlane + 256 + sd * 2 * N + j * N + blk * 8, t8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d[blk * 8 + i] = t8[i];
+      }
+      tc_wait_ld();
+      const float* cst = reinterpret_cast<const float*>(bst + sb * L::kBStage + 16 * N * 16);
+#pragma unroll
+      for (int blk = 0; blk < N / 8; ++blk)
+        if (blk * 8 < m) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[blk * 8 + i] += scale * (d[blk * 8 + i] - cst[4 * (blk * 8 + i)]);
+        }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&d_empty[sd]));
+      mbar_arrive(smem_u32(&b_empty[sb]));
+    };
+
+    bool pending = false;
+    float pend_scale = 0.f;
+#pragma unroll 1
+    for (int64_t it = b0, k = 0; it < b1; ++it, ++k) {
+      const int sa = (int)(k % SA);
+      const float scale = __half2float(__ushort_as_half(__ldg(cv.s + grp)));
+      cp_async_wait<DA - 1>();
+      uint4 W[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(aw + (k % DA) * 2048 + i * 512);
+      if (k >= SA) {
+        mbar_wait(smem_u32(&a_empty[sa]), (uint32_t)(((k / SA) - 1) & 1), a.err);
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t o[16];
+        dequant_word<Tr>(W[i].x, o + 0);
+        dequant_word<Tr>(W[i].y, o + 4);
+        dequant_word<Tr>(W[i].z, o + 8);
+        dequant_word<Tr>(W[i].w, o + 12);
+        tmem_st16(tlane + sa * 128 + j * 64 + i * 16, o);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&a_full[sa]));
+      issue_a((int)(k % DA));
+      if (pending) flush(k - 1, pend_scale, cv.m);
+      const bool tile_end = (grp == a.G - 1) || (it == b1 - 1);
+      if (!tile_end) {
+        pending = true;
+        pend_scale = scale;
+      } else {
+        pending = false;
+        flush(k, scale, cv.m);
+        // ---------------- finish this CTA's piece of the tile ----------------
+        const int64_t ts = (int64_t)tile * a.G, te = ts + a.G;
+        bool own = true;
+        if (!(b0 <= ts && b1 >= te)) {
+          const int slot = (ts <= b0) ? 0 : 1;
+          float* dst = a.part + ((((int64_t)c * 2 + slot) * kNW + warp) * N) * 32 + lane;
+#pragma unroll
+          for (int n = 0; n < N; ++n) dst[n * 32] = acc[n];
           __threadfence();
-          float s0[NT][4], s1[NT][4];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) s0[nt][j] = s1[nt][j] = 0.f;
-          for (int64_t cc = c0; cc <= c1; ++cc) {
-            if (cc == c) {
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  s0[nt][j] += acc0[nt][j];
-                  s1[nt][j] += acc1[nt][j];
-                }
-            } else {
-              const int64_t bc = begin_of(cc);
-              const int sl = (bc >= ts && bc < te) ? 0 : 1;
-              const float* src = a.part + ((((int64_t)cc * 2 + sl) * kNW + warp) * (8 * NT)) * 32 + lane;
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  s0[nt][j] += ld_cg_f32(src + ((0 * NT + nt) * 4 + j) * 32);
-                  s1[nt][j] += ld_cg_f32(src + ((1 * NT + nt) * 4 + j) * 32);
-                }
-            }
-          }
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              acc0[nt][j] = s0[nt][j];
-              acc1[nt][j] = s1[nt][j];
-            }
-          if (threadIdx.x == 0) a.tile_ctr[tile] = 0;
-        }
-      }
-      if (own) {
-        if (KIND == KIND_GATEUP) {
-          // SiLU(gate) * up for rows warp*16 + (g, g+8), tokens nt*8 + 2tig + (0, 1)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int row = warp * 16 + g + ((j >> 1) << 3);
-              const int tok = nt * 8 + 2 * tig + (j & 1);
-              const float h = silu_f(acc0[nt][j]) * acc1[nt][j];
-              htile[row * (SEG + 1) + tok] = Tr::to_f(Tr::from_f(h));
-            }
-          named_bar_sync(1, kConsumers);
-          const int m = cv.m;
-          uint8_t* dst = a.hp + (int64_t)cv.rt * a.hp_gstride;
-          for (int task = threadIdx.x; task < m * 16; task += kConsumers) {
-            const int tok = task >> 4, u = task & 15, tg = u >> 2, q = u & 3;
-            const int k0 = tg * 32 + q * 8;
-            float v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = htile[(k0 + i) * (SEG + 1) + tok];
-            uint4 pk;
-            float cp;
-            pack_unit<Tr>(v, pk, cp);
-            *reinterpret_cast<uint4*>(dst + (int64_t)(cv.p0 + tok) * kChunk + chunk_slot(tg, q)) = pk;
-            cpart[tok * 16 + u] = cp;
-          }
-          named_bar_sync(1, kConsumers);
-          if (threadIdx.x < m) {
-            float cs = 0.f;
-            for (int u = 0; u < 16; ++u) cs += cpart[threadIdx.x * 16 + u];
-            *reinterpret_cast<float4*>(dst + (int64_t)(cv.p0 + threadIdx.x) * kChunk + 256) =
-                make_float4(cs, 0.f, 0.f, 0.f);
-          }
-          named_bar_sync(1, kConsumers);
-        } else {
-          const int rb = cv.rt * 256 + warp * 32 + g;
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int tok = nt * 8 + 2 * tig + (j & 1);
-              const int row = rb + ((j >> 2) << 4) + (((j >> 1) & 1) << 3);
-              const float v = (j < 4) ? acc0[nt][j] : acc1[nt][j - 4];
-              if (tok < cv.m && row < a.N) {
-                const int p = cv.p0 + tok;
-                if (EPI == EPI_STORE) {
-                  reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)a.a_tok[p] * a.ldo + row] = Tr::from_f(v);
-                } else {
-                  a.R[(int64_t)p * a.N + row] = v * a.a_w[p];
-                }
-              }
-            }
-          if (EPI == EPI_COMBINE) {
+          named_bar_sync(1, kRows);
+          const int64_t c0 = cta_of(ts), c1 = cta_of(te - 1);
+          if (threadIdx.x == 0) bcast[0] = (atomicAdd(&a.tile_ctr[tile], 1) == (int)(c1 - c0));
+          named_bar_sync(1, kRows);
+          own = bcast[0] != 0;
+          if (own) {
             __threadfence();
-            named_bar_sync(1, kConsumers);
-            if (threadIdx.x == 0) bcast[1] = (atomicAdd(&a.rt_ctr[cv.rt], 1) == n_segs - 1);
-            named_bar_sync(1, kConsumers);
-            if (bcast[1]) {
-              __threadfence();
-              const int r0 = cv.rt * 256, nr = min(256, a.N - r0);
-              for (int task = threadIdx.x; task < a.T * nr; task += kConsumers) {
-                const int t = task / nr, row = r0 + task - t * nr;
-                float s = 0.f;
-                for (int kk = 0; kk < a.topk; ++kk) s += ld_cg_f32(a.R + (int64_t)a.pos[t * a.topk + kk] * a.N + row);
-                reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)t * a.ldo + row] = Tr::from_f(s);
+            float sum[N];
+#pragma unroll
+            for (int n = 0; n < N; ++n) sum[n] = 0.f;
+            for (int64_t cc = c0; cc <= c1; ++cc) {
+              if (cc == c) {
+#pragma unroll
+                for (int n = 0; n < N; ++n) sum[n] += acc[n];
+              } else {
+                const int64_t bc = begin_of(cc);
+                const int sl = (bc >= ts && bc < te) ? 0 : 1;
+                const float* src = a.part + ((((int64_t)cc * 2 + sl) * kNW + warp) * N) * 32 + lane;
+#pragma unroll
+                for (int n = 0; n < N; ++n) sum[n] += ld_cg_f32(src + n * 32);
               }
-              if (threadIdx.x == 0) a.rt_ctr[cv.rt] = 0;
+            }
+#pragma unroll
+            for (int n = 0; n < N; ++n) acc[n] = sum[n];
+            if (threadIdx.x == 0) a.tile_ctr[tile] = 0;
+          }
+        }
+        if (own) {
+          const int m = cv.m;
+          if (KIND == KIND_GATEUP) {
+            if (j == 1) {
+#pragma unroll
+              for (int n = 0; n < N; ++n) htile[r * (N + 1) + n] = acc[n];
+            }
+            named_bar_sync(1, kRows);
+            if (j == 0) {
+#pragma unroll
+              for (int n = 0; n < N; ++n) {
+                const float h = silu_f(acc[n]) * htile[r * (N + 1) + n];
+                htile[r * (N + 1) + n] = Tr::to_f(Tr::from_f(h));
+              }
+            }
+            named_bar_sync(1, kRows);
+            uint8_t* dstp = a.hp + (int64_t)cv.rt * a.hp_gstride;
+            for (int task = threadIdx.x; task < m * 16; task += kRows) {
+              const int tok = task >> 4, ch = task & 15;
+              float v[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[i] = htile[(ch * 8 + i) * (N + 1) + tok];
+              uint4 pk;
+              float cp;
+              pack_unit<Tr>(v, pk, cp);
+              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + tok) * kChunk + ch * 16) = pk;
+              cpart[tok * 16 + ch] = cp;
+            }
+            named_bar_sync(1, kRows);
+            if (threadIdx.x < m) {
+              float cs = 0.f;
+              for (int u = 0; u < 16; ++u) cs += cpart[threadIdx.x * 16 + u];
+              *reinterpret_cast<float4*>(dstp + (int64_t)(cv.p0 + threadIdx.x) * kChunk + 256) =
+                  make_float4(cs, 0.f, 0.f, 0.f);
+            }
+            named_bar_sync(1, kRows);
+          } else {
+            const int row = cv.rt * 256 + j * 128 + r;
+            if (row < a.N) {
+#pragma unroll
+              for (int n = 0; n < N; ++n) {
+                if (n < m) {
+                  const int p = cv.p0 + n;
+                  if (EPI == EPI_STORE)
+                    reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)a.a_tok[p] * a.ldo + row] = Tr::from_f(acc[n]);
+                  else
+                    a.R[(int64_t)p * a.N + row] = acc[n] * a.a_w[p];
+                }
+              }
+            }
+            if (EPI == EPI_COMBINE) {
+              __threadfence();
+              named_bar_sync(1, kRows);
+              if (threadIdx.x == 0) bcast[1] = (atomicAdd(&a.rt_ctr[cv.rt], 1) == n_segs - 1);
+              named_bar_sync(1, kRows);
+              if (bcast[1]) {
+                __threadfence();
+                const int r0 = cv.rt * 256, nr = min(256, a.N - r0);
+                for (int task = threadIdx.x; task < a.T * nr; task += kRows) {
+                  const int t = task / nr, rr = r0 + task - t * nr;
+                  float sacc = 0.f;
+                  for (int kk = 0; kk < a.topk; ++kk)
+                    sacc += ld_cg_f32(a.R + (int64_t)a.pos[t * a.topk + kk] * a.N + rr);
+                  reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)t * a.ldo + rr] = Tr::from_f(sacc);
+                }
+                if (threadIdx.x == 0) a.rt_ctr[cv.rt] = 0;
+              }
             }
           }
         }
+#pragma unroll
+        for (int n = 0; n < N; ++n) acc[n] = 0.f;
       }
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc0[nt][j] = acc1[nt][j] = 0.f;
+      if (++grp == a.G) {
+        grp = 0;
+        ++tile;
+        if (it + 1 < b1) load_rowview<KIND>(a, tile, n_segs, j, r, cv);
+      }
     }
-    if (++grp == a.G) {
-      grp = 0;
-      ++tile;
-      if (it + 1 < b1) load_tile<KIND>(a, tile, n_segs, warp, g, tig, cv);
-    }
+    cp_async_wait<0>();
   }
-  cp_async_wait<0>();
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kNW + 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
 }
 
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-template <int NT>
-struct Tune;
-template <>
-struct Tune<1> {
-  static constexpr int SB = 8, DA = 5, MINB = 2;
-};
-template <>
-struct Tune<2> {
-  static constexpr int SB = 6, DA = 4, MINB = 2;
-};
-template <>
-struct Tune<4> {
-  static constexpr int SB = 6, DA = 6, MINB = 1;
+// Tokens per segment = N of the MMA (16 or 32); 8*nt with nt in {2, 4}.
+static int pick_nt(int64_t max_tokens_per_expert) { return max_tokens_per_expert <= 16 ? 2 : 4; }
+
+template <int N>
+struct TcTune {
+  static constexpr int SB = 4, DA = 6;
 };
 
-static int pick_nt(int64_t max_tokens_per_expert) {
-  if (max_tokens_per_expert <= 8) return 1;
-  if (max_tokens_per_expert <= 16) return 2;
-  return 4;
-}
-static int minb_of(int nt) { return nt == 1 ? Tune<1>::MINB : nt == 2 ? Tune<2>::MINB : Tune<4>::MINB; }
-
-template <typename Tr, int NT, int KIND, int EPI>
+template <typename Tr, int N, int KIND, int EPI>
 static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
-  using TU = Tune<NT>;
-  using L = EngineSmem<NT, TU::SB, TU::DA>;
-  auto kern = engine_kernel<Tr, NT, KIND, EPI, TU::SB, TU::DA, TU::MINB>;
+  using TU = TcTune<N>;
+  using L = TcSmem<N, TU::SB, TU::DA>;
+  static_assert(2 * L::kTotal > 228 * 1024, "one engine CTA per SM: it allocates all 512 TMEM columns");
+  auto kern = tc_engine_kernel<Tr, N, KIND, EPI, TU::SB, TU::DA>;
   static bool attr_set[64] = {};  // per instantiation and device
   int dev = 0;
   HN_CUDA(cudaGetDevice(&dev));
@@ -833,18 +822,15 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
     HN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  kern<<<a.P, kEngineThreads, L::kTotal, s>>>(a);
+  kern<<<a.P, kTcThreads, L::kTotal, s>>>(a);
   HN_CUDA(cudaGetLastError());
   return HN_OK;
 }
 
 template <typename Tr, int KIND, int EPI>
 static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
-  switch (nt) {
-    case 1: return launch_engine_t<Tr, 1, KIND, EPI>(a, s);
-    case 2: return launch_engine_t<Tr, 2, KIND, EPI>(a, s);
-    default: return launch_engine_t<Tr, 4, KIND, EPI>(a, s);
-  }
+  if (nt <= 2) return launch_engine_t<Tr, 16, KIND, EPI>(a, s);
+  return launch_engine_t<Tr, 32, KIND, EPI>(a, s);
 }
 
 // A workspace has a counter section at its FRONT (error word, arrival
@@ -935,8 +921,9 @@ static int check_ws(const void* ws, size_t bytes, const Layout& l) {
 }
 
 static int grid_p(int nt) {
+  (void)nt;
   const int sms = sm_count_current();
-  return (sms > 0 ? sms : 148) * minb_of(nt);
+  return sms > 0 ? sms : 148;  // one persistent engine CTA per SM
 }
 
 template <typename Tr>
