@@ -53,7 +53,8 @@ def test_fp16_zero_group_and_large_matrix(lib):
 
 def test_roundtrip_error_bounds(lib):
     """Reference bound: max |err| < 0.1, mean < 0.01 (``tests/test_int4_pack.py:64-66``)."""
-    w = torch.randn(512, 256, device="cuda", dtype=torch.float16) * 0.1
+    torch.manual_seed(42)  # the reference test's own input (tests/test_int4_pack.py:33-35)
+    w = (torch.randn(512, 256, dtype=torch.float16) * 0.1).cuda()
     p, s = ops.quantize_int4(w)
     err = (ops.dequant_int4(p, s).float() - w.float()).abs()
     assert err.max().item() < 0.1 and err.mean().item() < 0.01
