@@ -403,10 +403,18 @@ struct TcSmem {
   static constexpr int kTotal = kHdr + kB + kA + kH;
 };
 
-// TMEM columns: A stages [0, 256) = 2 stages x {A0, A1} x 64 columns (128 k of
-// bf16 pairs); D stages [256, 256 + 4N) = 2 stages x {A0, A1} x N fp32 columns.
+// TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as bf16/f16
+// pairs) from column 0, then SD accumulator stages of {A0, A1} x N fp32 columns.
+// N = 16: SA = 3, SD = 4 (384 + 128 columns); N = 32: SA = 2, SD = 4 (256 + 256).
 constexpr int kTmemCols = 512;
 constexpr int kTcThreads = (kNW + 2) * 32;  // 8 row warps, 1 producer warp, 1 MMA warp
+template <int N>
+struct TmemPlan {
+  static constexpr int SA = (N == 16) ? 3 : 2;
+  static constexpr int SD = 4;
+  static constexpr int kD0 = SA * 128;
+  static_assert(kD0 + SD * 2 * N <= kTmemCols, "TMEM plan exceeds 512 columns");
+};
 
 // Per-thread view of the tile rows: thread (matrix j, row r) of a tile.
 struct RowView {
@@ -459,19 +467,21 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t* o) {
 template <typename Tr, int N, int KIND, int EPI, int SB, int DA>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_constant__ EngineArgs a) {
   using L = TcSmem<N, SB, DA>;
-  constexpr int SA = 2, SD = 2, LOOK = 2;
-  static_assert(LOOK <= SB - 1, "producer look-ahead must leave a free stage");
+  constexpr int SA = TmemPlan<N>::SA, SD = TmemPlan<N>::SD, D0 = TmemPlan<N>::kD0;
+  constexpr int LAG = SD - 1;   // a k-group's accumulator is flushed LAG iterations after its dequant
+  constexpr int LOOK = SB - 2;  // producer signals a token stage LOOK stages after issuing it
+  static_assert(LOOK >= 1 && SA <= 4 && SD <= 4 && SB <= 16, "stage counts");
   constexpr uint32_t IDESC = umma_idesc<Tr, 128, N>();
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* a_full = bars;       // [SA] row threads -> MMA
-  uint64_t* a_empty = bars + 2;  // [SA] MMA commit -> row threads
-  uint64_t* d_full = bars + 4;   // [SD] MMA commit -> row threads
-  uint64_t* d_empty = bars + 6;  // [SD] row threads -> MMA
-  uint64_t* b_full = bars + 8;   // [SB] producer -> MMA
-  uint64_t* b_empty = bars + 24; // [SB] row threads -> producer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
-  int* bcast = reinterpret_cast<int*>(bars + 41);
+  uint64_t* a_full = bars;        // [SA] row threads -> MMA
+  uint64_t* a_empty = bars + 4;   // [SA] MMA commit -> row threads
+  uint64_t* d_full = bars + 8;    // [SD] MMA commit -> row threads
+  uint64_t* d_empty = bars + 12;  // [SD] row threads -> MMA
+  uint64_t* b_full = bars + 16;   // [SB] producer -> MMA
+  uint64_t* b_empty = bars + 32;  // [SB] row threads -> producer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 48);
+  int* bcast = reinterpret_cast<int*>(bars + 49);
   uint8_t* bst = smem + L::kHdr;
   uint8_t* ast = bst + L::kB;
   float* htile = reinterpret_cast<float*>(ast + L::kA);
@@ -515,21 +525,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 
   if (warp == kNW) {
     // ------------------------- producer: token operand -------------------------
+    // Lane l copies the 17 chunks of token l of the segment; a stage is
+    // signalled (after its copies landed and a proxy fence) LOOK stages later.
     int tile = (int)(b0 / a.G), grp = (int)(b0 - (int64_t)tile * a.G);
     int seg, rt;
     TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
     int4 sg = a.segs[seg];
+    const uint8_t* src_tok = nullptr;
+    auto set_token = [&]() {
+      src_tok = nullptr;
+      if (lane < sg.z) {
+        const int row = a.b_use_tok ? a.a_tok[sg.y + lane] : sg.y + lane;
+        src_tok = a.bsrc + (int64_t)row * kChunk;
+      }
+    };
+    set_token();
     int64_t k = 0;
     for (int64_t it = b0; it < b1; ++it, ++k) {
       const int stage = (int)(k % SB);
       if (k >= SB) mbar_wait(smem_u32(&b_empty[stage]), (uint32_t)(((k / SB) - 1) & 1), a.err);
-      const int m = sg.z;
-      uint8_t* dst = bst + stage * L::kBStage;
-      for (int t = lane; t < m * 17; t += 32) {
-        const int tok = t / 17, ch = t - tok * 17;
-        const int row = a.b_use_tok ? a.a_tok[sg.y + tok] : sg.y + tok;
-        cp_async16(smem_u32(dst + 16 * (N * ch + tok)),
-                   a.bsrc + (int64_t)grp * a.b_gstride + (int64_t)row * kChunk + ch * 16);
+      if (src_tok) {
+        const uint32_t dst = smem_u32(bst + stage * L::kBStage + 16 * lane);
+        const uint8_t* src = src_tok + (int64_t)grp * a.b_gstride;
+#pragma unroll
+        for (int ch = 0; ch < 17; ++ch) cp_async16(dst + 16 * N * ch, src + ch * 16);
       }
       cp_async_commit();
       if (k >= LOOK) {
@@ -543,6 +562,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         if (it + 1 < b1) {
           TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
           sg = a.segs[seg];
+          set_token();
         }
       }
     }
@@ -565,7 +585,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 #pragma unroll
           for (int s = 0; s < 8; ++s) {
             const uint64_t bdesc = umma_sdesc_noswizzle(bbase + s * 32 * N, 16 * N, 128);
-            umma_ts(tbase + 256 + sd * 2 * N + j * N, tbase + sa * 128 + j * 64 + s * 8, bdesc, IDESC,
+            umma_ts(tbase + D0 + sd * 2 * N + j * N, tbase + sa * 128 + j * 64 + s * 8, bdesc, IDESC,
                     s > 0 ? 1u : 0u);
           }
         umma_commit(smem_u32(&a_empty[sa]));
@@ -620,7 +640,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 #pragma unroll
       for (int blk = 0; blk < N / 8; ++blk) {
         float t8[8];
-        if (blk * 8 < m) tmem_ld8(tlane + 256 + sd * 2 * N + j * N + blk * 8, t8);
+        if (blk * 8 < m) tmem_ld8(tlane + D0 + sd * 2 * N + j * N + blk * 8, t8);
 #pragma unroll
         for (int i = 0; i < 8; ++i) d[blk * 8 + i] = t8[i];
       }
@@ -637,12 +657,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       mbar_arrive(smem_u32(&b_empty[sb]));
     };
 
-    bool pending = false;
-    float pend_scale = 0.f;
+    // Accumulators of the last `npend` k-groups (their scales in sw[0..npend-1],
+    // oldest first) are still in TMEM; a group is flushed LAG iterations after
+    // its dequant, or at the end of its tile.
+    int npend = 0;
+    float sw[LAG + 1];
+#pragma unroll
+    for (int i = 0; i <= LAG; ++i) sw[i] = 0.f;
+    float scale_next = __half2float(__ushort_as_half(__ldg(cv.s + grp)));
 #pragma unroll 1
     for (int64_t it = b0, k = 0; it < b1; ++it, ++k) {
       const int sa = (int)(k % SA);
-      const float scale = __half2float(__ushort_as_half(__ldg(cv.s + grp)));
+      const bool tile_end = (grp == a.G - 1) || (it == b1 - 1);
+      const float scale = scale_next;
+      if (!tile_end) scale_next = __half2float(__ushort_as_half(__ldg(cv.s + grp + 1)));
       cp_async_wait<DA - 1>();
       uint4 W[4];
 #pragma unroll
@@ -664,14 +692,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       tc_fence_before();
       mbar_arrive(smem_u32(&a_full[sa]));
       issue_a((int)(k % DA));
-      if (pending) flush(k - 1, pend_scale, cv.m);
-      const bool tile_end = (grp == a.G - 1) || (it == b1 - 1);
+      // append this group's scale to the pending window
+#pragma unroll
+      for (int i = 0; i <= LAG; ++i)
+        if (i == npend) sw[i] = scale;
+      ++npend;
       if (!tile_end) {
-        pending = true;
-        pend_scale = scale;
+        if (npend > LAG) {
+          flush(k - LAG, sw[0], cv.m);
+#pragma unroll
+          for (int i = 0; i < LAG; ++i) sw[i] = sw[i + 1];
+          --npend;
+        }
       } else {
-        pending = false;
-        flush(k, scale, cv.m);
+#pragma unroll
+        for (int i = 0; i <= LAG; ++i)
+          if (i < npend) flush(k - npend + 1 + i, sw[i], cv.m);
+        npend = 0;
         // ---------------- finish this CTA's piece of the tile ----------------
         const int64_t ts = (int64_t)tile * a.G, te = ts + a.G;
         bool own = true;
@@ -784,7 +821,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       if (++grp == a.G) {
         grp = 0;
         ++tile;
-        if (it + 1 < b1) load_rowview<KIND>(a, tile, n_segs, j, r, cv);
+        if (it + 1 < b1) {
+          load_rowview<KIND>(a, tile, n_segs, j, r, cv);
+          scale_next = __half2float(__ushort_as_half(__ldg(cv.s)));
+        }
       }
     }
     cp_async_wait<0>();
@@ -806,7 +846,7 @@ static int pick_nt(int64_t max_tokens_per_expert) { return max_tokens_per_expert
 
 template <int N>
 struct TcTune {
-  static constexpr int SB = 4, DA = 6;
+  static constexpr int SB = 8, DA = 6;
 };
 
 template <typename Tr, int N, int KIND, int EPI>
