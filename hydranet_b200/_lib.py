@@ -51,10 +51,13 @@ SIGNATURES = {
     "hn_expert_mlp_int4": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hn_moe_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int]),
+    "hn_expert_maps_bytes": (c_size_t, []),
+    "hn_expert_maps_encode": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p]),
     "hn_moe_layer_int4": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, ctypes.POINTER(RouterParams),
-                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                  c_void_p]),
     "hn_moe_experts_int4": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p,
-                                    c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+                                    c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hn_moe_route": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, ctypes.POINTER(RouterParams), c_void_p,
                              c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hn_workspace_error": (c_int, [c_void_p, c_size_t, ctypes.POINTER(c_int), c_void_p]),
@@ -87,7 +90,7 @@ def load():
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
-            if lib.hn_abi_version() != 1:
+            if lib.hn_abi_version() != 2:
                 raise RuntimeError("libhydranet_b200.so ABI version mismatch")
             _lib = lib
     return _lib

@@ -279,4 +279,21 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Dequantise one 32-bit word (8 nibbles of k = 8w..8w+7) into 4 TMEM columns of
+// bf16/f16 pairs: (n0,n4) (n2,n6) as 2^e+n, (n1,n5) (n3,n7) as 2^e+8n (bf16) or
+// 2^e+16n (f16).
+template <typename Tr>
+__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t* o) {
+  const uint32_t M = Tr::kMagic;
+  o[0] = lop3_and_or<0x000F000Fu>(w, M);
+  o[1] = lop3_and_or<0x000F000Fu>(w >> 8, M);
+  if constexpr (Tr::kMagic == BF16::kMagic) {
+    o[2] = lop3_and_or<0x00780078u>(w >> 1, M);
+    o[3] = lop3_and_or<0x00780078u>(w >> 9, M);
+  } else {
+    o[2] = lop3_and_or<0x00F000F0u>(w, M);
+    o[3] = lop3_and_or<0x00F000F0u>(w >> 8, M);
+  }
+}
+
 }  // namespace hn

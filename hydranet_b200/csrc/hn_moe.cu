@@ -30,6 +30,9 @@
 // applied: acc += scale[row, group] * (mma_partial - C).  Weights therefore
 // enter the MMA as the exact integers n - 8, and the scale multiplies in fp32.
 #include <algorithm>
+#include <cstring>
+#include <string>
+#include <cuda.h>
 
 #include "common.cuh"
 
@@ -344,6 +347,13 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
 // ---------------------------------------------------------------------------
 // Grouped GEMV engine
 // ---------------------------------------------------------------------------
+// 2-D TMA descriptors of one expert's packed matrices (uint8, [rows, K/2]):
+// gate/up boxes are 128 B x 128 rows, down boxes 128 B x 256 rows; 128B swizzle.
+struct ExpertMaps {
+  CUtensorMap gate, up, down;
+};
+static_assert(sizeof(ExpertMaps) == 384, "ExpertMaps layout");
+
 struct EngineArgs {
   int K;     // reduction length (multiple of 128)
   int G;     // K / 128
@@ -357,6 +367,8 @@ struct EngineArgs {
   const int* pos;
   const hn_expert_ptrs* table;
   hn_expert_ptrs single;
+  const ExpertMaps* maps;  // device array [E] of tensor maps, or NULL: use single_maps
+  ExpertMaps single_maps;
   const uint8_t* bsrc;
   int64_t b_gstride;
   int b_use_tok;
@@ -386,28 +398,30 @@ struct TileMap {
   }
 };
 
-// Shared-memory plan of the tcgen05 engine.
-//   token operand ring: SB stages of [17 chunks][N tokens][16 B]; chunk c < 16
-//     holds logical k [8c, 8c+8) of each token, chunk 16 its correction C.
-//     For MMA k-step s the K-major core matrices are chunks 2s and 2s+1:
-//     LBO (K direction) = 16*N bytes, SBO (8-token blocks) = 128 bytes.
-//   weight ring: per row thread DA slots of 64 B (one 128-wide k-group).
+// Shared-memory plan of the tcgen05 engine (base rounded up to 1024 B).
+//   weight ring: ST stages of 32 KB = one 2-D TMA box pair (A0 rows, A1 rows)
+//     x 128 B (two 128-wide k-groups), 128B-swizzled: the 16-byte chunk c of
+//     row r sits at chunk c ^ (r & 7) of the row.
+//   token ring: SB stages of [17 chunks][N tokens][16 B]; chunk c < 16 holds
+//     logical k [8c, 8c+8) of each token, chunk 16 its correction C.  For MMA
+//     k-step s the K-major core matrices are chunks 2s and 2s+1: LBO (K
+//     direction) = 16*N bytes, SBO (8-token blocks) = 128 bytes.
 //   htile / cpart: epilogue staging.
-template <int N, int SB, int DA>
+template <int N, int ST, int SB>
 struct TcSmem {
-  static constexpr int kHdr = 512;
+  static constexpr int kHdr = 1024;
+  static constexpr int kWStage = 32768;
+  static constexpr int kW = ST * kWStage;
   static constexpr int kBStage = 17 * N * 16;
   static constexpr int kB = SB * kBStage;
-  static constexpr int kA = kNW * DA * 2048;
   static constexpr int kH = 128 * (N + 1) * 4 + N * 16 * 4;
-  static constexpr int kTotal = kHdr + kB + kA + kH;
+  static constexpr int kTotal = 1024 /* alignment slack */ + kHdr + kW + kB + kH;
 };
 
 // TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as bf16/f16
 // pairs) from column 0, then SD accumulator stages of {A0, A1} x N fp32 columns.
-// N = 16: SA = 3, SD = 4 (384 + 128 columns); N = 32: SA = 2, SD = 4 (256 + 256).
 constexpr int kTmemCols = 512;
-constexpr int kTcThreads = (kNW + 2) * 32;  // 8 row warps, 1 producer warp, 1 MMA warp
+constexpr int kTcThreads = (kNW + 3) * 32;  // 8 row warps, token producer, MMA issuer, weight producer
 template <int N>
 struct TmemPlan {
   static constexpr int SA = (N == 16) ? 3 : 2;
@@ -416,10 +430,9 @@ struct TmemPlan {
   static_assert(kD0 + SD * 2 * N <= kTmemCols, "TMEM plan exceeds 512 columns");
 };
 
-// Per-thread view of the tile rows: thread (matrix j, row r) of a tile.
+// Per-thread view of the tile: thread (matrix j, row r).
 struct RowView {
-  int seg, rt, m, p0;
-  const uint8_t* a;   // this thread's weight row (+ group * 64)
+  int seg, rt, m, p0, e;
   const uint16_t* s;  // this thread's scale row (+ group)
 };
 
@@ -429,68 +442,60 @@ __device__ __forceinline__ void load_rowview(const EngineArgs& a, int tile, int 
   const int4 sg = a.segs[v.seg];
   v.m = sg.z;
   v.p0 = sg.y;
+  v.e = sg.x;
   const hn_expert_ptrs ep = a.table ? a.table[sg.x] : a.single;
-  const uint8_t* A;
   const uint16_t* S;
   int row;
   if (KIND == KIND_GATEUP) {
-    A = j ? ep.up_packed : ep.gate_packed;
     S = j ? ep.up_scales : ep.gate_scales;
     row = v.rt * 128 + r;
   } else {
-    A = ep.down_packed;
     S = ep.down_scales;
     row = v.rt * 256 + j * 128 + r;
   }
-  row = min(row, a.N - 1);  // rows past N load row N-1 and are never stored
-  v.a = A + (int64_t)row * (a.K / 2);
+  row = min(row, a.N - 1);  // rows past N read row N-1's scales and are never stored
   v.s = S + (int64_t)row * a.G;
 }
 
-// Dequantise one 32-bit word (8 nibbles of k = 8w..8w+7) into 4 TMEM columns of
-// bf16/f16 pairs: (n0,n4) (n2,n6) as 2^e+n, (n1,n5) (n3,n7) as 2^e+8n (bf16) or
-// 2^e+16n (f16).
-template <typename Tr>
-__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t* o) {
-  const uint32_t M = Tr::kMagic;
-  o[0] = lop3_and_or<0x000F000Fu>(w, M);
-  o[1] = lop3_and_or<0x000F000Fu>(w >> 8, M);
-  if constexpr (Tr::kMagic == BF16::kMagic) {
-    o[2] = lop3_and_or<0x00780078u>(w >> 1, M);
-    o[3] = lop3_and_or<0x00780078u>(w >> 9, M);
-  } else {
-    o[2] = lop3_and_or<0x00F000F0u>(w, M);
-    o[3] = lop3_and_or<0x00F000F0u>(w >> 8, M);
-  }
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
 
-template <typename Tr, int N, int KIND, int EPI, int SB, int DA>
+template <typename Tr, int N, int KIND, int EPI, int ST, int SB>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_constant__ EngineArgs a) {
-  using L = TcSmem<N, SB, DA>;
+  using L = TcSmem<N, ST, SB>;
   constexpr int SA = TmemPlan<N>::SA, SD = TmemPlan<N>::SD, D0 = TmemPlan<N>::kD0;
-  constexpr int LAG = SD - 1;   // a k-group's accumulator is flushed LAG iterations after its dequant
-  constexpr int LOOK = SB - 2;  // producer signals a token stage LOOK stages after issuing it
-  static_assert(LOOK >= 1 && SA <= 4 && SD <= 4 && SB <= 16, "stage counts");
+  constexpr int LAG = SD - 1;   // a k-group's accumulator is flushed LAG groups after its dequant
+  constexpr int LOOK = SB - 2;  // token producer signals a stage LOOK stages after issuing it
+  static_assert(LOOK >= 1 && SA <= 4 && SD <= 4 && SB <= 16 && ST <= 8, "stage counts");
   constexpr uint32_t IDESC = umma_idesc<Tr, 128, N>();
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   uint64_t* a_full = bars;        // [SA] row threads -> MMA
   uint64_t* a_empty = bars + 4;   // [SA] MMA commit -> row threads
   uint64_t* d_full = bars + 8;    // [SD] MMA commit -> row threads
   uint64_t* d_empty = bars + 12;  // [SD] row threads -> MMA
-  uint64_t* b_full = bars + 16;   // [SB] producer -> MMA
-  uint64_t* b_empty = bars + 32;  // [SB] row threads -> producer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 48);
-  int* bcast = reinterpret_cast<int*>(bars + 49);
-  uint8_t* bst = smem + L::kHdr;
-  uint8_t* ast = bst + L::kB;
-  float* htile = reinterpret_cast<float*>(ast + L::kA);
+  uint64_t* b_full = bars + 16;   // [SB] token producer -> MMA
+  uint64_t* b_empty = bars + 32;  // [SB] row threads -> token producer
+  uint64_t* w_full = bars + 48;   // [ST] weight TMA -> row threads
+  uint64_t* w_empty = bars + 56;  // [ST] row threads -> weight producer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 64);
+  int* bcast = reinterpret_cast<int*>(bars + 65);
+  uint8_t* wst = smem + L::kHdr;
+  uint8_t* bst = wst + L::kW;
+  float* htile = reinterpret_cast<float*>(bst + L::kB);
   float* cpart = htile + 128 * (N + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_segs = *a.n_segs;
   const int n_tiles = a.n_rt * n_segs;
-  const int64_t NI = (int64_t)n_tiles * a.G;
+  const int GP = (a.G + 1) >> 1;  // k-group pairs per tile
+  const int64_t NI = (int64_t)n_tiles * GP;
   if (NI <= 0) return;
   const int64_t P = min((int64_t)a.P, NI);
   const int64_t c = blockIdx.x;
@@ -512,6 +517,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       mbar_init(smem_u32(&b_full[s]), 32);
       mbar_init(smem_u32(&b_empty[s]), kNW * 32);
     }
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(smem_u32(&w_full[s]), 1);
+      mbar_init(smem_u32(&w_empty[s]), kNW * 32);
+    }
     fence_barrier_init();
   }
   if (warp == kNW + 1) {
@@ -523,46 +532,61 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == kNW) {
-    // ------------------------- producer: token operand -------------------------
+  if (warp == kNW + 2) {
+    // ------------------------- weight producer (2-D TMA) -------------------------
+    if (lane == 0) {
+      int64_t ks = 0;
+      for (int64_t it = b0; it < b1; ++it, ++ks) {
+        const int tile = (int)(it / GP), gp = (int)(it - (int64_t)tile * GP);
+        int seg, rt;
+        TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+        const int e = a.segs[seg].x;
+        const ExpertMaps* em = a.maps ? a.maps + e : &a.single_maps;
+        const int s = (int)(ks % ST);
+        if (ks >= ST) mbar_wait(smem_u32(&w_empty[s]), (uint32_t)(((ks / ST) - 1) & 1), a.err);
+        const uint32_t bar = smem_u32(&w_full[s]);
+        mbar_arrive_expect_tx(bar, L::kWStage);
+        const uint32_t dst = smem_u32(wst + s * L::kWStage);
+        if (KIND == KIND_GATEUP) {
+          tma_load_2d(dst, &em->gate, gp * 128, rt * 128, bar);
+          tma_load_2d(dst + 16384, &em->up, gp * 128, rt * 128, bar);
+        } else {
+          tma_load_2d(dst, &em->down, gp * 128, rt * 256, bar);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kNW) {
+    // ------------------------- token producer -------------------------
     // Lane l copies the 17 chunks of token l of the segment; a stage is
     // signalled (after its copies landed and a proxy fence) LOOK stages later.
-    int tile = (int)(b0 / a.G), grp = (int)(b0 - (int64_t)tile * a.G);
-    int seg, rt;
-    TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
-    int4 sg = a.segs[seg];
-    const uint8_t* src_tok = nullptr;
-    auto set_token = [&]() {
-      src_tok = nullptr;
+    int64_t k = 0;
+    for (int64_t it = b0; it < b1; ++it) {
+      const int tile = (int)(it / GP), gp = (int)(it - (int64_t)tile * GP);
+      int seg, rt;
+      TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+      const int4 sg = a.segs[seg];
+      const uint8_t* src_tok = nullptr;
       if (lane < sg.z) {
         const int row = a.b_use_tok ? a.a_tok[sg.y + lane] : sg.y + lane;
         src_tok = a.bsrc + (int64_t)row * kChunk;
       }
-    };
-    set_token();
-    int64_t k = 0;
-    for (int64_t it = b0; it < b1; ++it, ++k) {
-      const int stage = (int)(k % SB);
-      if (k >= SB) mbar_wait(smem_u32(&b_empty[stage]), (uint32_t)(((k / SB) - 1) & 1), a.err);
-      if (src_tok) {
-        const uint32_t dst = smem_u32(bst + stage * L::kBStage + 16 * lane);
-        const uint8_t* src = src_tok + (int64_t)grp * a.b_gstride;
+      const int ng = min(2, a.G - 2 * gp);
+      for (int gi = 0; gi < ng; ++gi, ++k) {
+        const int grp = 2 * gp + gi;
+        const int stage = (int)(k % SB);
+        if (k >= SB) mbar_wait(smem_u32(&b_empty[stage]), (uint32_t)(((k / SB) - 1) & 1), a.err);
+        if (src_tok) {
+          const uint32_t dst = smem_u32(bst + stage * L::kBStage + 16 * lane);
+          const uint8_t* src = src_tok + (int64_t)grp * a.b_gstride;
 #pragma unroll
-        for (int ch = 0; ch < 17; ++ch) cp_async16(dst + 16 * N * ch, src + ch * 16);
-      }
-      cp_async_commit();
-      if (k >= LOOK) {
-        cp_async_wait<LOOK>();
-        fence_proxy_async_smem();  // generic-proxy writes -> read by the tensor core (async proxy)
-        mbar_arrive(smem_u32(&b_full[(k - LOOK) % SB]));
-      }
-      if (++grp == a.G) {
-        grp = 0;
-        ++tile;
-        if (it + 1 < b1) {
-          TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
-          sg = a.segs[seg];
-          set_token();
+          for (int ch = 0; ch < 17; ++ch) cp_async16(dst + 16 * N * ch, src + ch * 16);
+        }
+        cp_async_commit();
+        if (k >= LOOK) {
+          cp_async_wait<LOOK>();
+          fence_proxy_async_smem();  // generic-proxy writes -> read by the tensor core (async proxy)
+          mbar_arrive(smem_u32(&b_full[(k - LOOK) % SB]));
         }
       }
     }
@@ -573,23 +597,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       int64_t k = 0;
-      for (int64_t it = b0; it < b1; ++it, ++k) {
-        const int sa = (int)(k % SA), sd = (int)(k % SD), sb = (int)(k % SB);
-        mbar_wait(smem_u32(&a_full[sa]), (uint32_t)((k / SA) & 1), a.err);
-        mbar_wait(smem_u32(&b_full[sb]), (uint32_t)((k / SB) & 1), a.err);
-        if (k >= SD) mbar_wait(smem_u32(&d_empty[sd]), (uint32_t)(((k / SD) - 1) & 1), a.err);
-        tc_fence_after();
-        const uint32_t bbase = smem_u32(bst + sb * L::kBStage);
+      for (int64_t it = b0; it < b1; ++it) {
+        const int gp = (int)(it % GP);
+        const int ng = min(2, a.G - 2 * gp);
+        for (int gi = 0; gi < ng; ++gi, ++k) {
+          const int sa = (int)(k % SA), sd = (int)(k % SD), sb = (int)(k % SB);
+          mbar_wait(smem_u32(&a_full[sa]), (uint32_t)((k / SA) & 1), a.err);
+          mbar_wait(smem_u32(&b_full[sb]), (uint32_t)((k / SB) & 1), a.err);
+          if (k >= SD) mbar_wait(smem_u32(&d_empty[sd]), (uint32_t)(((k / SD) - 1) & 1), a.err);
+          tc_fence_after();
+          const uint32_t bbase = smem_u32(bst + sb * L::kBStage);
 #pragma unroll
-        for (int j = 0; j < 2; ++j)
+          for (int j = 0; j < 2; ++j)
 #pragma unroll
-          for (int s = 0; s < 8; ++s) {
-            const uint64_t bdesc = umma_sdesc_noswizzle(bbase + s * 32 * N, 16 * N, 128);
-            umma_ts(tbase + D0 + sd * 2 * N + j * N, tbase + sa * 128 + j * 64 + s * 8, bdesc, IDESC,
-                    s > 0 ? 1u : 0u);
-          }
-        umma_commit(smem_u32(&a_empty[sa]));
-        umma_commit(smem_u32(&d_full[sd]));
+            for (int s = 0; s < 8; ++s) {
+              const uint64_t bdesc = umma_sdesc_noswizzle(bbase + s * 32 * N, 16 * N, 128);
+              umma_ts(tbase + D0 + sd * 2 * N + j * N, tbase + sa * 128 + j * 64 + s * 8, bdesc, IDESC,
+                      s > 0 ? 1u : 0u);
+            }
+          umma_commit(smem_u32(&a_empty[sa]));
+          umma_commit(smem_u32(&d_full[sd]));
+        }
       }
     }
     __syncwarp();
@@ -598,40 +626,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     const int j = warp >> 2, q = warp & 3, r = q * 32 + lane;
     const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
     constexpr int kRows = kNW * 32;
-    uint8_t* aw = ast + warp * DA * 2048 + lane * 16;
-    // prefetch cursor
-    int pf_tile = (int)(b0 / a.G), pf_grp = (int)(b0 - (int64_t)pf_tile * a.G);
-    int64_t pf_it = b0;
-    RowView pv;
-    load_rowview<KIND>(a, pf_tile, n_segs, j, r, pv);
-    auto issue_a = [&](int slot) {
-      if (pf_it < b1) {
-        const uint32_t dst = smem_u32(aw + slot * 2048);
-        const uint8_t* src = pv.a + pf_grp * 64;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) cp_async16(dst + i * 512, src + i * 16);
-      }
-      cp_async_commit();
-      if (pf_it < b1) {
-        ++pf_it;
-        if (++pf_grp == a.G) {
-          pf_grp = 0;
-          ++pf_tile;
-          if (pf_it < b1) load_rowview<KIND>(a, pf_tile, n_segs, j, r, pv);
-        }
-      }
-    };
-#pragma unroll 1
-    for (int i = 0; i < DA; ++i) issue_a(i);
+    const int wrow = (j * 128 + r) * 128;  // this thread's row inside a weight stage
+    const int swz = r & 7;
 
-    int tile = (int)(b0 / a.G), grp = (int)(b0 - (int64_t)tile * a.G);
+    int tile = (int)(b0 / GP);
     RowView cv;
     load_rowview<KIND>(a, tile, n_segs, j, r, cv);
     float acc[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) acc[n] = 0.f;
 
-    // flush of k-group kk: acc += scale * (D - C) for the active 8-token blocks
+    // flush of group counter kk: acc += scale * (D - C) for the active 8-token blocks
     auto flush = [&](int64_t kk, float scale, int m) {
       const int sd = (int)(kk % SD), sb = (int)(kk % SB);
       mbar_wait(smem_u32(&d_full[sd]), (uint32_t)((kk / SD) & 1), a.err);
@@ -640,6 +645,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 #pragma unroll
       for (int blk = 0; blk < N / 8; ++blk) {
         float t8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t8[i] = 0.f;
         if (blk * 8 < m) tmem_ld8(tlane + D0 + sd * 2 * N + j * N + blk * 8, t8);
 #pragma unroll
         for (int i = 0; i < 8; ++i) d[blk * 8 + i] = t8[i];
@@ -658,59 +665,66 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     };
 
     // Accumulators of the last `npend` k-groups (their scales in sw[0..npend-1],
-    // oldest first) are still in TMEM; a group is flushed LAG iterations after
-    // its dequant, or at the end of its tile.
+    // oldest first) are still in TMEM; a group is flushed LAG groups after its
+    // dequant, or at the end of its tile.
     int npend = 0;
     float sw[LAG + 1];
 #pragma unroll
     for (int i = 0; i <= LAG; ++i) sw[i] = 0.f;
-    float scale_next = __half2float(__ushort_as_half(__ldg(cv.s + grp)));
+    int64_t k = 0;  // group counter (same sequence as the MMA issuer and the token producer)
+    int64_t ks = 0; // weight stage counter
 #pragma unroll 1
-    for (int64_t it = b0, k = 0; it < b1; ++it, ++k) {
-      const int sa = (int)(k % SA);
-      const bool tile_end = (grp == a.G - 1) || (it == b1 - 1);
-      const float scale = scale_next;
-      if (!tile_end) scale_next = __half2float(__ushort_as_half(__ldg(cv.s + grp + 1)));
-      cp_async_wait<DA - 1>();
-      uint4 W[4];
+    for (int64_t it = b0; it < b1; ++it, ++ks) {
+      const int gp = (int)(it - (int64_t)tile * GP);
+      const int ng = min(2, a.G - 2 * gp);
+      const int ws = (int)(ks % ST);
+      mbar_wait(smem_u32(&w_full[ws]), (uint32_t)((ks / ST) & 1), a.err);
+      const uint8_t* wrow_p = wst + ws * L::kWStage + wrow;
+#pragma unroll 1
+      for (int gi = 0; gi < ng; ++gi, ++k) {
+        const int grp = 2 * gp + gi;
+        const int sa = (int)(k % SA);
+        const bool tile_end = (grp == a.G - 1) || (it == b1 - 1 && gi == ng - 1);
+        const float scale = __half2float(__ushort_as_half(__ldg(cv.s + grp)));
+        uint4 W[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(aw + (k % DA) * 2048 + i * 512);
-      if (k >= SA) {
-        mbar_wait(smem_u32(&a_empty[sa]), (uint32_t)(((k / SA) - 1) & 1), a.err);
-        tc_fence_after();
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint32_t o[16];
-        dequant_word<Tr>(W[i].x, o + 0);
-        dequant_word<Tr>(W[i].y, o + 4);
-        dequant_word<Tr>(W[i].z, o + 8);
-        dequant_word<Tr>(W[i].w, o + 12);
-        tmem_st16(tlane + sa * 128 + j * 64 + i * 16, o);
-      }
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(smem_u32(&a_full[sa]));
-      issue_a((int)(k % DA));
-      // append this group's scale to the pending window
-#pragma unroll
-      for (int i = 0; i <= LAG; ++i)
-        if (i == npend) sw[i] = scale;
-      ++npend;
-      if (!tile_end) {
-        if (npend > LAG) {
-          flush(k - LAG, sw[0], cv.m);
-#pragma unroll
-          for (int i = 0; i < LAG; ++i) sw[i] = sw[i + 1];
-          --npend;
+        for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + i) ^ swz) << 4));
+        if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));  // stage data is in registers now
+        if (k >= SA) {
+          mbar_wait(smem_u32(&a_empty[sa]), (uint32_t)(((k / SA) - 1) & 1), a.err);
+          tc_fence_after();
         }
-      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint32_t o[16];
+          dequant_word<Tr>(W[i].x, o + 0);
+          dequant_word<Tr>(W[i].y, o + 4);
+          dequant_word<Tr>(W[i].z, o + 8);
+          dequant_word<Tr>(W[i].w, o + 12);
+          tmem_st16(tlane + sa * 128 + j * 64 + i * 16, o);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(smem_u32(&a_full[sa]));
+#pragma unroll
+        for (int i = 0; i <= LAG; ++i)
+          if (i == npend) sw[i] = scale;
+        ++npend;
+        if (!tile_end) {
+          if (npend > LAG) {
+            flush(k - LAG, sw[0], cv.m);
+#pragma unroll
+            for (int i = 0; i < LAG; ++i) sw[i] = sw[i + 1];
+            --npend;
+          }
+          continue;
+        }
 #pragma unroll
         for (int i = 0; i <= LAG; ++i)
           if (i < npend) flush(k - npend + 1 + i, sw[i], cv.m);
         npend = 0;
         // ---------------- finish this CTA's piece of the tile ----------------
-        const int64_t ts = (int64_t)tile * a.G, te = ts + a.G;
+        const int64_t ts = (int64_t)tile * GP, te = ts + GP;
         bool own = true;
         if (!(b0 <= ts && b1 >= te)) {
           const int slot = (ts <= b0) ? 0 : 1;
@@ -818,16 +832,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 #pragma unroll
         for (int n = 0; n < N; ++n) acc[n] = 0.f;
       }
-      if (++grp == a.G) {
-        grp = 0;
+      if (gp == GP - 1 && it + 1 < b1) {
         ++tile;
-        if (it + 1 < b1) {
-          load_rowview<KIND>(a, tile, n_segs, j, r, cv);
-          scale_next = __half2float(__ushort_as_half(__ldg(cv.s)));
-        }
+        load_rowview<KIND>(a, tile, n_segs, j, r, cv);
       }
     }
-    cp_async_wait<0>();
   }
 
   tc_fence_before();
@@ -846,15 +855,16 @@ static int pick_nt(int64_t max_tokens_per_expert) { return max_tokens_per_expert
 
 template <int N>
 struct TcTune {
-  static constexpr int SB = 8, DA = 6;
+  static constexpr int ST = 4, SB = 6;
 };
 
 template <typename Tr, int N, int KIND, int EPI>
 static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
   using TU = TcTune<N>;
-  using L = TcSmem<N, TU::SB, TU::DA>;
+  using L = TcSmem<N, TU::ST, TU::SB>;
   static_assert(2 * L::kTotal > 228 * 1024, "one engine CTA per SM: it allocates all 512 TMEM columns");
-  auto kern = tc_engine_kernel<Tr, N, KIND, EPI, TU::SB, TU::DA>;
+  static_assert(L::kTotal <= 227 * 1024, "engine shared memory exceeds the per-CTA limit");
+  auto kern = tc_engine_kernel<Tr, N, KIND, EPI, TU::ST, TU::SB>;
   static bool attr_set[64] = {};  // per instantiation and device
   int dev = 0;
   HN_CUDA(cudaGetDevice(&dev));
@@ -986,6 +996,56 @@ static int check_router(const hn_router_params* r, int64_t E) {
   return HN_OK;
 }
 
+// ---------------------------------------------------------------------------
+// 2-D TMA descriptors.  cuTensorMapEncodeTiled is fetched from the driver at
+// run time (cudaGetDriverEntryPoint) so the library needs no -lcuda.
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// uint8 matrix [rows, row_bytes] read as boxes of 128 bytes x box_rows, 128B swizzle.
+static int encode_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64_t row_bytes, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(HN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (no CUDA driver)");
+  HN_REQUIRE(base && ((uintptr_t)base & 15) == 0, "packed weights must be non-null and 16-byte aligned");
+  HN_REQUIRE(row_bytes % 16 == 0 && rows >= 1, "bad packed weight shape");
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1u, 1u};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HN_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return HN_OK;
+}
+
+static int encode_expert_maps(ExpertMaps* out, const hn_expert_ptrs& p, int64_t H, int64_t F) {
+  memset(out, 0, sizeof(*out));
+  int rc = HN_OK;
+  if (p.gate_packed && (rc = encode_rows_map(&out->gate, p.gate_packed, F, H / 2, 128))) return rc;
+  if (p.up_packed && (rc = encode_rows_map(&out->up, p.up_packed, F, H / 2, 128))) return rc;
+  if (p.down_packed && (rc = encode_rows_map(&out->down, p.down_packed, H, F / 2, 256))) return rc;
+  return HN_OK;
+}
+
 struct MoECall {
   const void* x;
   int64_t ldx;
@@ -998,6 +1058,8 @@ struct MoECall {
   const float* given_w;
   const hn_expert_ptrs* table;
   hn_expert_ptrs single;
+  const ExpertMaps* maps;  // device array [E] of tensor maps, or NULL: use single_maps
+  ExpertMaps single_maps;
   void* out;
   int64_t ldo;
   int32_t* out_idx;
@@ -1065,6 +1127,11 @@ static int run_moe(const MoECall& m) {
   e1.pos = plan.pos;
   e1.table = m.table;
   e1.single = m.single;
+  e1.maps = static_cast<const ExpertMaps*>(m.maps);
+  if (!m.table) {
+    rc = encode_expert_maps(&e1.single_maps, m.single, m.H, m.F);
+    if (rc) return rc;
+  }
   e1.bsrc = plan.xp;
   e1.b_gstride = m.T * kChunk;
   e1.b_use_tok = 1;
@@ -1136,13 +1203,15 @@ size_t hn_int4_linear_workspace_size(int64_t M, int64_t N, int64_t K) {
 }
 
 int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
-                      const hn_router_params* router, const hn_expert_ptrs* experts, void* out, int32_t* topk_idx,
+                      const hn_router_params* router, const hn_expert_ptrs* experts, const void* expert_maps,
+                      void* out, int32_t* topk_idx,
                       float* topk_w, float* logits, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_dims(T, H, F, E);
   if (rc) return rc;
   rc = check_router(router, E);
   if (rc) return rc;
-  HN_REQUIRE(x && experts && out && workspace, "hn_moe_layer_int4: null pointer");
+  HN_REQUIRE(x && experts && expert_maps && out && workspace, "hn_moe_layer_int4: null pointer");
+  HN_REQUIRE(((uintptr_t)expert_maps & 63) == 0, "expert_maps must be 64-byte aligned");
   MoECall m{};
   m.x = x;
   m.ldx = H;
@@ -1155,6 +1224,7 @@ int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F,
   m.route_mode = ROUTE_COMPUTE;
   m.router = router;
   m.table = experts;
+  m.maps = static_cast<const ExpertMaps*>(expert_maps);
   m.out = out;
   m.ldo = H;
   m.out_idx = topk_idx;
@@ -1168,12 +1238,15 @@ int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F,
 }
 
 int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int top_k,
-                        const int32_t* topk_idx, const float* topk_w, const hn_expert_ptrs* experts, void* out,
+                        const int32_t* topk_idx, const float* topk_w, const hn_expert_ptrs* experts,
+                        const void* expert_maps, void* out,
                         void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_dims(T, H, F, E);
   if (rc) return rc;
   HN_REQUIRE(top_k >= 1 && top_k <= E && top_k <= kMaxTopK, "top_k out of range");
-  HN_REQUIRE(x && topk_idx && topk_w && experts && out && workspace, "hn_moe_experts_int4: null pointer");
+  HN_REQUIRE(x && topk_idx && topk_w && experts && expert_maps && out && workspace,
+             "hn_moe_experts_int4: null pointer");
+  HN_REQUIRE(((uintptr_t)expert_maps & 63) == 0, "expert_maps must be 64-byte aligned");
   MoECall m{};
   m.x = x;
   m.ldx = H;
@@ -1187,6 +1260,7 @@ int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t 
   m.given_idx = topk_idx;
   m.given_w = topk_w;
   m.table = experts;
+  m.maps = static_cast<const ExpertMaps*>(expert_maps);
   m.out = out;
   m.ldo = H;
   m.ws = workspace;
@@ -1297,6 +1371,11 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   e.pos = plan.pos;
   e.table = nullptr;
   e.single = hn_expert_ptrs{nullptr, nullptr, nullptr, nullptr, w_packed, w_scales};
+  e.maps = nullptr;
+  {
+    const int mrc = encode_rows_map(&e.single_maps.down, w_packed, N, K / 2, 256);
+    if (mrc) return mrc;
+  }
   e.bsrc = plan.xp;
   e.b_gstride = M * kChunk;
   e.b_use_tok = 1;
@@ -1318,6 +1397,20 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
     return fail(HN_ERR_UNSUPPORTED, "int4_linear: activation dtype must be float16 or bfloat16");
   }
   return rc;
+}
+
+size_t hn_expert_maps_bytes(void) { return sizeof(ExpertMaps); }
+
+int hn_expert_maps_encode(const hn_expert_ptrs* host_table, int64_t E, int64_t H, int64_t F, void* host_out) {
+  HN_REQUIRE(host_table && host_out, "hn_expert_maps_encode: null pointer");
+  HN_REQUIRE(E >= 1 && H >= 128 && H % 128 == 0 && F >= 128 && F % 128 == 0, "hn_expert_maps_encode: bad shape");
+  HN_REQUIRE(((uintptr_t)host_out & 63) == 0, "hn_expert_maps_encode: output must be 64-byte aligned");
+  ExpertMaps* out = static_cast<ExpertMaps*>(host_out);
+  for (int64_t e = 0; e < E; ++e) {
+    const int rc = encode_expert_maps(&out[e], host_table[e], H, F);
+    if (rc) return rc;
+  }
+  return HN_OK;
 }
 
 int hn_workspace_error(const void* workspace, size_t workspace_bytes, int* error_code, void* stream) {

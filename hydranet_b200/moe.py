@@ -49,7 +49,8 @@ class MoELayerInt4(nn.Module):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1]).contiguous()
         params, bonus = self._params(x, top_k)
-        out, idx, w, logits = ops.moe_layer(x, params, self.experts.device_table, self.num_experts,
+        out, idx, w, logits = ops.moe_layer(x, params, self.experts.device_table, self.experts.device_maps,
+                                            self.num_experts,
                                             self.experts.intermediate_dim, want_routing=return_routing,
                                             keep_refs=(bonus,))
         out = out.view(shape)
@@ -60,4 +61,5 @@ class MoELayerInt4(nn.Module):
 
 def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts: ExpertTable) -> torch.Tensor:
     """Experts + weighted combine for externally routed tokens (x [T, H])."""
-    return ops.moe_experts(x, topk_idx, topk_w, experts.device_table, len(experts), experts.intermediate_dim)
+    return ops.moe_experts(x, topk_idx, topk_w, experts.device_table, experts.device_maps, len(experts),
+                           experts.intermediate_dim)

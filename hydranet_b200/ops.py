@@ -152,10 +152,11 @@ def moe_route(x: torch.Tensor, params: _lib.RouterParams, num_experts: int, keep
     return idx, w, logits
 
 
-def moe_layer(x: torch.Tensor, params: _lib.RouterParams, expert_table: torch.Tensor, num_experts: int, ffn: int,
-              want_routing: bool = False, keep_refs=()):
+def moe_layer(x: torch.Tensor, params: _lib.RouterParams, expert_table: torch.Tensor, expert_maps: torch.Tensor,
+              num_experts: int, ffn: int, want_routing: bool = False, keep_refs=()):
     """Router + experts + combine for one MoE layer. ``expert_table`` is a device
-    int64 tensor [E, 6] of pointers (``ExpertTable.device_table``)."""
+    int64 tensor [E, 6] of pointers and ``expert_maps`` the device copy of their
+    TMA descriptors (``ExpertTable.device_table`` / ``ExpertTable.device_maps``)."""
     T, H = x.shape
     k = params.top_k
     out = torch.empty_like(x)
@@ -169,14 +170,15 @@ def moe_layer(x: torch.Tensor, params: _lib.RouterParams, expert_table: torch.Te
     ws = _lib.workspaces.get(need, x.device)
     with torch.cuda.device(x.device):
         check(lib.hn_moe_layer_int4(ptr(x), _act_dtype(x), T, H, ffn, num_experts, ctypes.byref(params),
-                                    expert_table.data_ptr(), ptr(out), ptr(idx), ptr(w), ptr(logits), ptr(ws), ws.numel(),
+                                    expert_table.data_ptr(), expert_maps.data_ptr(), ptr(out), ptr(idx), ptr(w),
+                                    ptr(logits), ptr(ws), ws.numel(),
                                     stream_ptr(x.device)))
     del keep_refs
     return out, idx, w, logits
 
 
 def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, expert_table: torch.Tensor,
-                num_experts: int, ffn: int) -> torch.Tensor:
+                expert_maps: torch.Tensor, num_experts: int, ffn: int) -> torch.Tensor:
     """Experts + combine with caller-supplied routing (int32 idx, float32 weights)."""
     T, H = x.shape
     k = topk_idx.shape[1]
@@ -190,5 +192,6 @@ def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, e
     ws = _lib.workspaces.get(need, x.device)
     with torch.cuda.device(x.device):
         check(lib.hn_moe_experts_int4(ptr(x), _act_dtype(x), T, H, ffn, num_experts, k, ptr(topk_idx), ptr(topk_w),
-                                      expert_table.data_ptr(), ptr(out), ptr(ws), ws.numel(), stream_ptr(x.device)))
+                                      expert_table.data_ptr(), expert_maps.data_ptr(), ptr(out), ptr(ws), ws.numel(),
+                                      stream_ptr(x.device)))
     return out

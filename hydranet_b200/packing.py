@@ -143,11 +143,31 @@ class ExpertTable:
                     raise ValueError("expert buffers must be contiguous and 16-byte aligned")
         self.device = slots[0].gate_packed.device
         self.device_table = torch.empty(len(slots), 6, dtype=torch.int64, device=self.device)
+        self.device_maps = None
         self.refresh()
 
     def refresh(self):
+        """Re-publish the pointer table and the TMA descriptors (after a slot moved)."""
         rows = [[getattr(s, n).data_ptr() for n in SLOT_TENSORS] for s in self.slots]
         self.device_table.copy_(torch.tensor(rows, dtype=torch.int64))
+        if self.device.type == "cuda":
+            self.device_maps = self._encode_maps(rows)
+
+    def _encode_maps(self, rows):
+        import ctypes
+        from . import _lib
+        lib = _lib.load()
+        per = lib.hn_expert_maps_bytes()
+        E = len(rows)
+        host_ptrs = (ctypes.c_uint64 * (6 * E))(*[p for r in rows for p in r])
+        raw = ctypes.create_string_buffer(E * per + 64)
+        aligned = (ctypes.addressof(raw) + 63) & ~63
+        _lib.check(lib.hn_expert_maps_encode(ctypes.addressof(host_ptrs), E, self.hidden_dim, self.intermediate_dim,
+                                             aligned))
+        blob = ctypes.string_at(aligned, E * per)
+        dev = torch.frombuffer(bytearray(blob), dtype=torch.uint8).to(self.device)
+        assert dev.data_ptr() % 64 == 0
+        return dev
 
     def __len__(self):
         return len(self.slots)

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define HN_ABI_VERSION 1
+#define HN_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define HN_API __attribute__((visibility("default")))
@@ -147,13 +147,24 @@ typedef struct hn_router_params {
 
 HN_API size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int top_k);
 
+/* TMA descriptors of an expert table (what the grouped ops stream weights
+ * with): hn_expert_maps_bytes() bytes per expert (384).  hn_expert_maps_encode
+ * fills a 64-byte aligned HOST buffer of E entries from a HOST copy of the
+ * pointer table; copy it to device memory and pass it as expert_maps.  The
+ * descriptors embed the weight addresses: re-encode when a slot moves (a slot
+ * refilled in place keeps its descriptors).  Host-only, launches nothing. */
+HN_API size_t hn_expert_maps_bytes(void);
+HN_API int hn_expert_maps_encode(const hn_expert_ptrs* host_table, int64_t E, int64_t H, int64_t F,
+                                 void* host_out);
+
 /* x [T, H] -> out [T, H] = sum_k w[t,k] * MLP_{idx[t,k]}(x[t]).
- * experts: DEVICE pointer to E hn_expert_ptrs.  Optional outputs (may be NULL):
+ * experts: DEVICE pointer to E hn_expert_ptrs; expert_maps: DEVICE pointer to
+ * their E TMA descriptors (hn_expert_maps_encode).  Optional outputs (may be NULL):
  * topk_idx int32 [T, k], topk_w float32 [T, k] (already rounded to the
  * activation dtype, as model/router.py:120 and model/glm4.py:309 cast them),
  * logits float32 [T, E]. */
 HN_API int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
-                      const hn_router_params* router, const hn_expert_ptrs* experts,
+                      const hn_router_params* router, const hn_expert_ptrs* experts, const void* expert_maps,
                       void* out, int32_t* topk_idx, float* topk_w, float* logits,
                       void* workspace, size_t workspace_bytes, void* stream);
 
@@ -162,7 +173,7 @@ HN_API int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int
  * shards and for callers that route on their own. */
 HN_API int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
                         int top_k, const int32_t* topk_idx, const float* topk_w,
-                        const hn_expert_ptrs* experts, void* out,
+                        const hn_expert_ptrs* experts, const void* expert_maps, void* out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* Router only: writes topk_idx/topk_w (and logits if non-NULL). */

@@ -41,7 +41,7 @@ def test_ctypes_table_matches_header():
 
 def test_abi_and_sizes_without_gpu():
     lib = _lib.load()
-    assert lib.hn_abi_version() == 1
+    assert lib.hn_abi_version() == 2
     a = lib.hn_moe_workspace_size(1, 4096, 14336, 8, 2)
     b = lib.hn_moe_workspace_size(64, 4096, 14336, 8, 2)
     assert 0 < a < b
