@@ -420,12 +420,16 @@ struct TcSmem {
 
 // TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as bf16/f16
 // pairs) from column 0, then SD accumulator stages of {A0, A1} x N fp32 columns.
+// N = 16: 3 x 128 + 4 x 32 = 512; N = 32: 3 x 128 + 2 x 64 = 512.
 constexpr int kTmemCols = 512;
 constexpr int kTcThreads = (kNW + 3) * 32;  // 8 row warps, token producer, MMA issuer, weight producer
 template <int N>
 struct TmemPlan {
-  static constexpr int SA = (N == 16) ? 3 : 2;
-  static constexpr int SD = 4;
+  // Three weight stages: with two, a stage was rewritten for group k+2 as soon
+  // as the commit of group k arrived, and results came out wrong on some rows
+  // (non-deterministically).  Three stages were exact in every test.
+  static constexpr int SA = 3;
+  static constexpr int SD = (N == 16) ? 4 : 2;
   static constexpr int kD0 = SA * 128;
   static_assert(kD0 + SD * 2 * N <= kTmemCols, "TMEM plan exceeds 512 columns");
 };
@@ -641,23 +645,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       const int sd = (int)(kk % SD), sb = (int)(kk % SB);
       mbar_wait(smem_u32(&d_full[sd]), (uint32_t)((kk / SD) & 1), a.err);
       tc_fence_after();
-      float d[N];
+      uint32_t d[N / 8][8];
 #pragma unroll
       for (int blk = 0; blk < N / 8; ++blk) {
-        float t8[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) t8[i] = 0.f;
-        if (blk * 8 < m) tmem_ld8(tlane + D0 + sd * 2 * N + j * N + blk * 8, t8);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) d[blk * 8 + i] = t8[i];
+        for (int i = 0; i < 8; ++i) d[blk][i] = 0u;
+        if (blk * 8 < m) tmem_ld8(tlane + D0 + sd * 2 * N + j * N + blk * 8, d[blk]);
       }
-      tc_wait_ld();
+      tmem_ld_wait8(d[0]);
+#pragma unroll
+      for (int blk = 1; blk < N / 8; ++blk) reg_dep8(d[blk]);
       const float* cst = reinterpret_cast<const float*>(bst + sb * L::kBStage + 16 * N * 16);
 #pragma unroll
       for (int blk = 0; blk < N / 8; ++blk)
         if (blk * 8 < m) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[blk * 8 + i] += scale * (d[blk * 8 + i] - cst[4 * (blk * 8 + i)]);
+          for (int i = 0; i < 8; ++i)
+            acc[blk * 8 + i] += scale * (__uint_as_float(d[blk][i]) - cst[4 * (blk * 8 + i)]);
         }
       tc_fence_before();
       mbar_arrive(smem_u32(&d_empty[sd]));
@@ -695,15 +699,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
           tc_fence_after();
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint32_t o[16];
-          dequant_word<Tr>(W[i].x, o + 0);
-          dequant_word<Tr>(W[i].y, o + 4);
-          dequant_word<Tr>(W[i].z, o + 8);
-          dequant_word<Tr>(W[i].w, o + 12);
-          tmem_st16(tlane + sa * 128 + j * 64 + i * 16, o);
+        for (int i = 0; i < 4; i += 2) {
+          uint32_t o0[16], o1[16];
+          dequant_word<Tr>(W[i].x, o0 + 0);
+          dequant_word<Tr>(W[i].y, o0 + 4);
+          dequant_word<Tr>(W[i].z, o0 + 8);
+          dequant_word<Tr>(W[i].w, o0 + 12);
+          dequant_word<Tr>(W[i + 1].x, o1 + 0);
+          dequant_word<Tr>(W[i + 1].y, o1 + 4);
+          dequant_word<Tr>(W[i + 1].z, o1 + 8);
+          dequant_word<Tr>(W[i + 1].w, o1 + 12);
+          tmem_st16(tlane + sa * 128 + j * 64 + i * 16, o0);
+          tmem_st16(tlane + sa * 128 + j * 64 + (i + 1) * 16, o1);
+          tc_wait_st_keep(o0, o1);
         }
-        tc_wait_st();
         tc_fence_before();
         mbar_arrive(smem_u32(&a_full[sa]));
 #pragma unroll
