@@ -67,6 +67,7 @@ struct Plan {
   int* ctr1;     // per phase-1 tile arrival counters
   int* ctr2;     // per phase-2 tile arrival counters
   int* rtctr;    // per output row-tile segment counters
+  int n_ctr;     // words from ctr1 to the end of the counter section (zeroed by the prep kernel)
 };
 
 __host__ __device__ constexpr int seg_tokens(int nt) { return 8 * nt; }
@@ -142,6 +143,9 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   __shared__ float s_w[kMaxTopK];
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const typename Tr::T* xrow = reinterpret_cast<const typename Tr::T*>(a.x) + (int64_t)t * a.ldx;
+  // The engine's arrival counters start every call at zero, whatever an
+  // earlier call of another shape left in this part of the workspace.
+  for (int i = t * 256 + tid; i < a.plan.n_ctr; i += gridDim.x * 256) a.plan.ctr1[i] = 0;
   for (int i = tid; i < a.H; i += 256) xs[i] = Tr::to_f(xrow[i]);
   __syncthreads();
 
@@ -425,9 +429,6 @@ constexpr int kTmemCols = 512;
 constexpr int kTcThreads = (kNW + 3) * 32;  // 8 row warps, token producer, MMA issuer, weight producer
 template <int N>
 struct TmemPlan {
-  // Three weight stages: with two, a stage was rewritten for group k+2 as soon
-  // as the commit of group k arrived, and results came out wrong on some rows
-  // (non-deterministically).  Three stages were exact in every test.
   static constexpr int SA = 3;
   static constexpr int SD = (N == 16) ? 4 : 2;
   static constexpr int kD0 = SA * 128;
@@ -693,7 +694,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         uint4 W[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + i) ^ swz) << 4));
-        if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));  // stage data is in registers now
         if (k >= SA) {
           mbar_wait(smem_u32(&a_empty[sa]), (uint32_t)(((k / SA) - 1) & 1), a.err);
           tc_fence_after();
@@ -715,6 +715,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         }
         tc_fence_before();
         mbar_arrive(smem_u32(&a_full[sa]));
+        // Release the weight stage only now: its next TMA write (async proxy)
+        // is not ordered after shared loads whose results are still in flight,
+        // and an arrive right after issuing them let the refill overwrite rows
+        // before some lanes had read them.  The dequant above consumed W.
+        if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));
 #pragma unroll
         for (int i = 0; i <= LAG; ++i)
           if (i == npend) sw[i] = scale;
@@ -892,12 +897,15 @@ static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
   return launch_engine_t<Tr, 32, KIND, EPI>(a, s);
 }
 
-// A workspace has a counter section at its FRONT (error word, arrival
-// counters; all zero between calls because every counter is reset by the
-// kernel that sees its final value) and a data section at its BACK.  Calls of
-// any shape can therefore share one zero-filled workspace: a counter section
-// [0, C) never overlaps another call's data section [size - D, size) as long
-// as each call's C + D fits.
+// A workspace has a counter section at its FRONT and a data section at its
+// BACK.  The error word (offset 0) and the prep kernel's arrival counter
+// (offset 256) must be zero when a call starts; the error word is only ever
+// set by a failing wait, and the route counter is reset by the kernel that
+// reads its final value.  No data section reaches below offset 512 (every
+// layout's counter section is at least 1280 bytes and the data section sits
+// above it), so those two words survive calls of any shape.  The engine
+// counters after them are zeroed by the prep kernel at the start of every
+// call, because another shape's data section may have covered them.
 struct Layout {
   size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
   size_t counts, n_segs, segs, a_tok, a_w, pos, idx, wts, xp, hp, part1, part2, R, data;  // back (relative)
@@ -955,6 +963,7 @@ static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
   p.ctr1 = reinterpret_cast<int*>(b + l.ctr1);
   p.ctr2 = reinterpret_cast<int*>(b + l.ctr2);
   p.rtctr = reinterpret_cast<int*>(b + l.rtctr);
+  p.n_ctr = (int)((l.counters - l.ctr1) / 4);
   p.counts = reinterpret_cast<int*>(d + l.counts);
   p.n_segs = reinterpret_cast<int*>(d + l.n_segs);
   p.segs = reinterpret_cast<int4*>(d + l.segs);

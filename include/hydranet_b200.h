@@ -6,10 +6,12 @@
  * synchronises and never allocates device memory.  Kernels that need scratch
  * take a caller-owned workspace whose size comes from the matching
  * *_workspace_size() query (query on the device that will run the call).
- * A workspace must be 256-byte aligned and zero-filled once when it is first
- * allocated.  The kernels leave it re-usable: its front holds arrival counters
- * that each call resets to zero, its back holds per-call data, so one
- * workspace may serve calls of any shape whose size query it satisfies.
+ * A workspace must be 256-byte aligned, and its first 512 bytes (an error
+ * word and an arrival counter) must be zero before its first use; zero-filling
+ * the whole buffer once when it is allocated is enough.  The kernels leave it
+ * re-usable: the two words stay zero unless a bounded wait failed (see
+ * hn_workspace_error), every other counter is zeroed by each call itself, so
+ * one workspace may serve calls of any shape whose size query it satisfies.
  * One workspace must not be used by two launches that may overlap on the
  * device.
  *

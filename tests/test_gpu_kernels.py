@@ -109,3 +109,48 @@ def test_repeatable_bitwise(lib):
     outs = [ops.expert_mlp_int4(x, *dev) for _ in range(4)]
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+def test_workspace_only_head_must_be_zero(lib):
+    """Only the first 512 bytes of a workspace must start at zero: the rest may
+    hold anything another call of another shape left there."""
+    M, N, K = 40, 1024, 2048
+    p, s = packed_weight(3, N, K)
+    x = act(np.random.default_rng(4).standard_normal((M, K), dtype=np.float32), "bf16")
+    need = lib.hn_int4_linear_workspace_size(M, N, K)
+    ws = torch.full((need + 4096,), 0xFF, dtype=torch.uint8, device="cuda")
+    ws[:512] = 0
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    pd, sd = torch.from_numpy(p).cuda(), torch.from_numpy(s).cuda()
+    from hydranet_b200._lib import check, ptr, stream_ptr
+    for _ in range(2):
+        check(lib.hn_int4_linear(ptr(x), K, 2, M, K, ptr(pd), ptr(sd), N, 128, ptr(out), N, ptr(ws), ws.numel(),
+                                 stream_ptr(x.device)))
+        ref = R.int4_linear_ref(to_np32(x), p, s)
+        assert rel_l2(to_np32(out), ref) <= TIGHT["bf16"]
+        ws[512:].fill_(0xFF)  # as if a call of another shape had used the rest
+    assert _lib_error(ws) == 0
+
+
+def _lib_error(ws):
+    from hydranet_b200 import _lib
+    return _lib.workspace_error(ws)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 4096, 14336), (64, 14336, 4096), (32, 14336, 4096)])
+def test_long_k_runs_bitwise_repeatable(lib, M, N, K):
+    """Mixtral-size projections: every CTA streams long runs of k-groups through
+    the weight ring; each call must give the same bits and match the oracle.
+    The L2 is flushed before each call so weights stream from HBM."""
+    p, s = packed_weight(17, N, K)
+    x = act(np.random.default_rng(5).standard_normal((M, K), dtype=np.float32), "bf16")
+    pd, sd = torch.from_numpy(p).cuda(), torch.from_numpy(s).cuda()
+    scrub = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(6):
+        scrub.add_(1)
+        outs.append(k_gemm.int4_linear(x, pd, sd))
+    ref = R.int4_linear_ref(to_np32(x), p, s)
+    for o in outs:
+        assert torch.equal(o, outs[0])
+    assert rel_l2(to_np32(outs[0]), ref) <= TIGHT["bf16"]
