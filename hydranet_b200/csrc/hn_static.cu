@@ -1,0 +1,62 @@
+// hn_int4_linear_static: hn_int4_linear with its scratch in a device array
+// compiled into the library, for callers that cannot provide device memory.
+//
+// The array is a file-scope __device__ variable, so the CUDA runtime creates
+// one zero-filled copy per device when it loads this module there; nothing is
+// allocated at call time.  Its address on the current device is looked up once
+// (cudaGetSymbolAddress) and cached.  The computation is the unchanged
+// hn_int4_linear entry point, given that array as its workspace.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace hn {
+namespace {
+
+constexpr size_t kStaticScratchBytes = HN_INT4_LINEAR_STATIC_SCRATCH_BYTES;
+static_assert(kStaticScratchBytes % 256 == 0, "static scratch size must keep 256-byte granularity");
+
+__device__ __align__(256) unsigned char g_linear_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Address of the current device's copy of g_linear_scratch.  The first call on
+// a device may load the module onto it; later calls only read the cache.
+int static_scratch(void** out) {
+  int dev = -1;
+  HN_CUDA(cudaGetDevice(&dev));
+  HN_REQUIRE(dev >= 0 && dev < kMaxDevices, "int4_linear_static: device ordinal beyond the library's table of 64");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    HN_CUDA(cudaGetSymbolAddress(&p, g_linear_scratch));
+    HN_REQUIRE(p && ((uintptr_t)p & 255) == 0, "int4_linear_static: static scratch is not 256-byte aligned");
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return HN_OK;
+}
+
+}  // namespace
+}  // namespace hn
+
+extern "C" int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K,
+                                     const uint8_t* w_packed, const uint16_t* w_scales, int64_t N, int group_size,
+                                     void* out, int64_t ldo, void* stream) {
+  const size_t need = hn_int4_linear_workspace_size(M, N, K);
+  if (need == 0) return hn::fail(HN_ERR_INVALID, "int4_linear_static: need M, N >= 1 and K >= 128");
+  if (need > hn::kStaticScratchBytes)
+    return hn::fail(HN_ERR_WORKSPACE, "int4_linear_static: M=" + std::to_string(M) + " N=" + std::to_string(N) +
+                                          " K=" + std::to_string(K) + " needs " + std::to_string(need) +
+                                          " bytes of scratch, more than the " +
+                                          std::to_string(hn::kStaticScratchBytes) +
+                                          " bytes compiled into the library; call hn_int4_linear with a workspace");
+  void* ws = nullptr;
+  const int rc = hn::static_scratch(&ws);
+  if (rc) return rc;
+  return hn_int4_linear(x, ldx, dtype, M, K, w_packed, w_scales, N, group_size, out, ldo, ws,
+                        hn::kStaticScratchBytes, stream);
+}

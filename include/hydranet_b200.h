@@ -183,6 +183,42 @@ HN_API int hn_moe_route(const void* x, int dtype, int64_t T, int64_t H, int64_t 
                  const hn_router_params* router, int32_t* topk_idx, float* topk_w, float* logits,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Allocation-free int4_linear.  No counterpart in the reference: its Python
+ * kernels allocate through PyTorch on every call.
+ *
+ * hn_int4_linear_static computes what hn_int4_linear computes, with the same
+ * arguments minus the workspace.  Its scratch is an array of
+ * HN_INT4_LINEAR_STATIC_SCRATCH_BYTES (16 MiB) compiled into this library:
+ * the CUDA runtime creates one zero-filled copy per device when it loads the
+ * library's module there, and the call itself allocates nothing.  It is meant
+ * for callers that have no device memory to hand over, for example a host
+ * that binds only this C ABI through an FFI and owns no CUDA allocator, or a
+ * serving runtime that has given all free HBM to its caches, so that a
+ * cudaMalloc on the decode path would fail or wait for the whole device.
+ *
+ *  - Shapes whose hn_int4_linear_workspace_size(M, N, K) is larger than the
+ *    array are refused with HN_ERR_WORKSPACE (for example M = 64 with
+ *    K = 14336 fits; M = 4096 with K = 14336 does not).
+ *  - The first call on each device, made with that device current, looks up
+ *    the array's address (cudaGetSymbolAddress, which may load the module onto
+ *    the device) and caches it; make that first call before any stream
+ *    capture.  A failure there is returned as HN_ERR_CUDA.
+ *  - What must be zero: the array's first 512 bytes (an error word and an
+ *    arrival counter) when a call starts.  They are zero after loading and
+ *    stay zero unless a bounded device wait times out; after that, results of
+ *    later calls on that device are undefined.
+ *  - There is ONE array per device, shared by every caller of this function.
+ *    Two calls that may overlap on the device (streams with no ordering
+ *    between them, or host threads racing on different streams) overwrite
+ *    each other's scratch and produce wrong results.  Issue them on one
+ *    stream, or use hn_int4_linear with one workspace per stream.
+ * ------------------------------------------------------------------------- */
+#define HN_INT4_LINEAR_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
+HN_API int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K,
+                                 const uint8_t* w_packed, const uint16_t* w_scales, int64_t N, int group_size,
+                                 void* out, int64_t ldo, void* stream);
+
 /* Device-side error word of a workspace (bounded waits that timed out set it).
  * Copies 4 bytes device->host on 'stream' and synchronises that stream. */
 HN_API int hn_workspace_error(const void* workspace, size_t workspace_bytes, int* error_code, void* stream);
