@@ -125,6 +125,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the waiting thread is suspended in
+// hardware until the phase completes or about hint_ns pass, instead of
+// re-issuing polls that take issue slots from the other warps of its SMSP.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -141,14 +155,15 @@ __device__ __forceinline__ int ld_volatile_s32(const int* p) {
   asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
   return v;
 }
+constexpr uint32_t kSuspendHintNs = 20000;
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
   if (err && ld_volatile_s32(err) != 0) return false;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
     if (err && ld_volatile_s32(err) != 0) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
@@ -253,6 +268,54 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(enable_d), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
+// One k-group of one matrix: eight K=16 steps D (+)= A[a + 8s] * B[desc + s*step]
+// (the first overwrites D) and the correction step D += A[a_corr] * B[desc_c].
+// The WHOLE warp executes this with warp-uniform operands and elect.sync picks
+// the one issuing lane inside the asm: issued that way an MMA costs about 18
+// cycles at N <= 32, against about 46 when one lane issues it from a divergent
+// branch.  Descriptors are passed as their 32-bit halves: the low half holds
+// the start address and LBO, the high half SBO and the version.
+template <int kStepB>
+__device__ __forceinline__ void umma_group9(uint32_t d, uint32_t a, uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                            uint32_t c_lo, uint32_t a_corr, uint32_t idesc_c) {
+  asm volatile(
+      "{\n\t.reg .pred pf, pt, e;\n\t.reg .b64 bd;\n\t.reg .b32 al, bl;\n\t"
+      "setp.ne.b32 pf, %3, %3;\n\t"
+      "setp.eq.b32 pt, %3, %3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "mov.b64 bd, {%2, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, pf;\n\t"
+      "add.u32 al, %1, 8;\n\tadd.u32 bl, %2, %5;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, %5;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, %5;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, %5;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, %5;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, %5;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, %5;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "mov.b64 bd, {%6, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], bd, %8, pt;\n\t}"
+      :
+      : "r"(d), "r"(a), "r"(b_lo), "r"(b_hi), "r"(idesc), "n"(kStepB), "r"(c_lo), "r"(a_corr), "r"(idesc_c)
+      : "memory");
+}
+
+// tcgen05.commit from one elected lane of a converged warp (the lane that
+// issued the MMAs through umma_group9's elect.sync: elect.sync picks the same
+// lane, the lowest active one, every time).
+__device__ __forceinline__ void umma_commit_elect(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
 // Arrive on an mbarrier once every previously issued tcgen05 async op of this thread completes.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -294,12 +357,51 @@ __device__ __forceinline__ void tmem_ld_wait8(uint32_t (&r)[8]) {
                :
                : "memory");
 }
+__device__ __forceinline__ void reg_dep16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
 // Orders later uses of r after a preceding (asm volatile) tcgen05.wait::ld.
 __device__ __forceinline__ void reg_dep8(uint32_t (&r)[8]) {
   asm volatile(""
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])
                :
                : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+// (a0, a1) += s * (d0, d1) with one packed fp32x2 FMA (sm_100).
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float s, uint32_t d0, uint32_t d1) {
+  asm("{\n\t.reg .b64 ta, ts, td;\n\t"
+      "mov.b64 ta, {%0, %1};\n\t"
+      "mov.b64 ts, {%2, %2};\n\t"
+      "mov.b64 td, {%3, %4};\n\t"
+      "fma.rn.f32x2 ta, ts, td, ta;\n\t"
+      "mov.b64 {%0, %1}, ta;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(s), "r"(d0), "r"(d1));
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -38,9 +38,7 @@
 
 namespace hn {
 
-constexpr int kChunk = 272;  // bytes per (token, k-group): 256 B fragments + fp32 C + 12 B pad
-constexpr int kNW = 8;       // consumer warps per engine CTA
-constexpr int kEngineThreads = (kNW + 1) * 32;
+constexpr int kChunk = 272;  // bytes per (token, k-group): 16 B correction unit + 16 units of 16 B
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 32;
 
@@ -73,14 +71,32 @@ struct Plan {
 __host__ __device__ constexpr int seg_tokens(int nt) { return 8 * nt; }
 
 // ---------------------------------------------------------------------------
-// Activation staging.  For k-group g and token t a 272-byte chunk holds 16
-// units of 16 bytes followed by the fp32 correction C (and 12 bytes of pad).
-// Unit c covers x[128*g + 8*c + i], i = 0..7, packed as bf16/f16 pairs
+// Activation staging.  For k-group g and token t a 272-byte chunk holds the
+// correction unit followed by 16 data units of 16 bytes.
+// Data unit c (at byte 16 + 16c) covers x[128*g + 8*c + i], i = 0..7, packed
+// as bf16/f16 pairs
 //   { (x0, x4), (x2, x6), (x1*s, x5*s), (x3*s, x7*s) }   (s = odd-k scale)
 // i.e. logical k 8c..8c+7 of the MMA, matching the TMEM columns the weight
 // dequantiser writes for the same 8 nibbles (dequant_word).  A unit is one
 // 16-byte row of a K-major core matrix of the tensor-core B operand.
+// The correction unit (byte 0) holds C = sum_k c_k x_k of the group as three
+// bf16 values whose sum is exactly the fp32 C, then five bf16 zeros; the
+// engine multiplies it by a constant A column of -1s in the same MMA chain,
+// so the accumulator already holds sum_k (n_k - 8) x_k.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 correction_unit(float c) {
+  const __nv_bfloat16 h0 = __float2bfloat16_rn(c);
+  const float r1 = c - __bfloat162float(h0);  // exact
+  const __nv_bfloat16 h1 = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(h1);  // exact, at most 8 significant bits
+  const __nv_bfloat16 h2 = __float2bfloat16_rn(r2);
+  uint4 u;
+  u.x = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+  u.y = (uint32_t)__bfloat16_as_ushort(h2);
+  u.z = 0u;
+  u.w = 0u;
+  return u;
+}
 template <typename Tr>
 __device__ __forceinline__ void pack_unit(const float (&v)[8], uint4& out, float& cpart) {
   const float s = Tr::kOddScale;
@@ -160,14 +176,14 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
     uint4 packed;
     float cp;
     pack_unit<Tr>(v, packed, cp);
-    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk + ch * 16) = packed;
+    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk + 16 + ch * 16) = packed;
     cpart[u] = cp;
   }
   __syncthreads();
   for (int g = tid; g < a.H / 128; g += 256) {
     float c = 0.f;
     for (int u = 0; u < 16; ++u) c += cpart[g * 16 + u];
-    *reinterpret_cast<float4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk + 256) = make_float4(c, 0.f, 0.f, 0.f);
+    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk) = correction_unit(c);
   }
 
   // 2. routing for this token
@@ -406,10 +422,10 @@ struct TileMap {
 //   weight ring: ST stages of 32 KB = one 2-D TMA box pair (A0 rows, A1 rows)
 //     x 128 B (two 128-wide k-groups), 128B-swizzled: the 16-byte chunk c of
 //     row r sits at chunk c ^ (r & 7) of the row.
-//   token ring: SB stages of [17 chunks][N tokens][16 B]; chunk c < 16 holds
-//     logical k [8c, 8c+8) of each token, chunk 16 its correction C.  For MMA
-//     k-step s the K-major core matrices are chunks 2s and 2s+1: LBO (K
-//     direction) = 16*N bytes, SBO (8-token blocks) = 128 bytes.
+//   token ring: SB stages of [17 units][N tokens][16 B]: unit 0 is the
+//     correction unit, unit 1 + c holds logical k [8c, 8c+8).  For MMA k-step
+//     s the K-major core matrices are units 1+2s and 2+2s: LBO (K direction)
+//     = 16*N bytes, SBO (8-token blocks) = 128 bytes.
 //   htile / cpart: epilogue staging.
 template <int N, int ST, int SB>
 struct TcSmem {
@@ -422,17 +438,27 @@ struct TcSmem {
   static constexpr int kTotal = 1024 /* alignment slack */ + kHdr + kW + kB + kH;
 };
 
-// TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as bf16/f16
-// pairs) from column 0, then SD accumulator stages of {A0, A1} x N fp32 columns.
-// N = 16: 3 x 128 + 4 x 32 = 512; N = 32: 3 x 128 + 2 x 64 = 512.
+// TMEM columns: SA = 2 weight stages of {A0, A1} x 64 columns (128 k as
+// bf16/f16 pairs) from column 0, SD accumulator stages of {A0, A1} x N fp32
+// columns from column 256, and the 8-column constant A block of the
+// correction step after them.  N = 16: 256 + 4 x 32 + 8; N = 32: 256 + 3 x 64 + 8.
 constexpr int kTmemCols = 512;
-constexpr int kTcThreads = (kNW + 3) * 32;  // 8 row warps, token producer, MMA issuer, weight producer
+// Warp roles (a warp runs on SMSP warp % 4): dequant warps, fold warps, then
+// one role warp on each SMSP.
+constexpr int kDeqWarps = 8;
+constexpr int kFoldWarps = 8;
+constexpr int kTokWarp = 16;   // token producer (SMSP 0)
+constexpr int kMmaWarp0 = 17;  // MMA issuer of matrix 0 (SMSP 1), allocates TMEM
+constexpr int kWgtWarp = 18;   // weight producer (SMSP 2)
+constexpr int kMmaWarp1 = 19;  // MMA issuer of matrix 1 (SMSP 3)
+constexpr int kTcThreads = 20 * 32;
 template <int N>
 struct TmemPlan {
-  static constexpr int SA = 3;
-  static constexpr int SD = (N == 16) ? 4 : 2;
+  static constexpr int SA = 2;
+  static constexpr int SD = (N == 16) ? 4 : 3;
   static constexpr int kD0 = SA * 128;
-  static_assert(kD0 + SD * 2 * N <= kTmemCols, "TMEM plan exceeds 512 columns");
+  static constexpr int kCorr = kD0 + SD * 2 * N;
+  static_assert(kCorr + 8 <= kTmemCols, "TMEM plan exceeds 512 columns");
 };
 
 // Per-thread view of the tile: thread (matrix j, row r).
@@ -470,27 +496,51 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Persistent grouped GEMV on the 5th-generation tensor cores.
+//
+// Work items are (tile, k-group pair); CTA c owns items [c*NI/P, (c+1)*NI/P)
+// (stream-K), so every CTA streams the same number of weight bytes.  Warp
+// roles (a warp runs on SMSP warp % 4):
+//   warps 0-7    dequant warps: warp w dequantises matrix j = w >> 2 for TMEM
+//                lanes 32*(w&3).. (its 32 rows), all 128 k of each group, into
+//                the A stage;
+//   warps 8-15   fold warps: warp w owns the same rows of matrix (w >> 2) & 1
+//                and folds each group's accumulator into fp32 registers,
+//                acc += scale[row, group] * D, for all N tokens; they also run
+//                the stream-K fix-up and the epilogue;
+//   warp 16      token producer: cp.async of each group's token units;
+//   warps 17, 19 MMA issuers for matrix 0 and matrix 1: per k-group eight
+//                K=16 steps with the dequantised weights (TMEM) as A and the
+//                tokens (SMEM) as B, then the correction step, into one TMEM
+//                accumulator stage; the two matrices use separate columns, so
+//                two warps on two SMSPs can issue them independently;
+//   warp 18      weight producer: one 32 KB 2-D TMA box pair per item.
+// Dequantising and folding are separate warps so that a warp never waits for
+// a TMEM store and a TMEM load of two different groups one after the other.
+// All hand-offs are mbarriers with bounded waits.
 template <typename Tr, int N, int KIND, int EPI, int ST, int SB>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_constant__ EngineArgs a) {
   using L = TcSmem<N, ST, SB>;
-  constexpr int SA = TmemPlan<N>::SA, SD = TmemPlan<N>::SD, D0 = TmemPlan<N>::kD0;
-  constexpr int LAG = SD - 1;   // a k-group's accumulator is flushed LAG groups after its dequant
+  constexpr int SA = TmemPlan<N>::SA, SD = TmemPlan<N>::SD, D0 = TmemPlan<N>::kD0, CORR = TmemPlan<N>::kCorr;
   constexpr int LOOK = SB - 2;  // token producer signals a stage LOOK stages after issuing it
   static_assert(LOOK >= 1 && SA <= 4 && SD <= 4 && SB <= 16 && ST <= 8, "stage counts");
   constexpr uint32_t IDESC = umma_idesc<Tr, 128, N>();
+  constexpr uint32_t IDESC_CORR = umma_idesc<BF16, 128, N>();
+  constexpr uint32_t kDescHi = (128u >> 4) | (1u << 14);  // SBO = 128 B, descriptor version 1 (bit 46)
+  constexpr int kFoldThreads = kFoldWarps * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* a_full = bars;        // [SA] row threads -> MMA
-  uint64_t* a_empty = bars + 4;   // [SA] MMA commit -> row threads
-  uint64_t* d_full = bars + 8;    // [SD] MMA commit -> row threads
-  uint64_t* d_empty = bars + 12;  // [SD] row threads -> MMA
-  uint64_t* b_full = bars + 16;   // [SB] token producer -> MMA
-  uint64_t* b_empty = bars + 32;  // [SB] row threads -> token producer
-  uint64_t* w_full = bars + 48;   // [ST] weight TMA -> row threads
-  uint64_t* w_empty = bars + 56;  // [ST] row threads -> weight producer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 64);
-  int* bcast = reinterpret_cast<int*>(bars + 65);
+  uint64_t* a_full = bars;        // [SA][2] dequant warps of matrix j -> its MMA warp
+  uint64_t* a_empty = bars + 8;   // [SA][2] MMA commit (matrix j) -> its dequant warps
+  uint64_t* d_full = bars + 16;   // [SD] both MMA warps' commits -> fold warps
+  uint64_t* d_empty = bars + 20;  // [SD] fold warps -> MMA warps
+  uint64_t* b_full = bars + 24;   // [SB] token producer -> MMA warps
+  uint64_t* b_empty = bars + 40;  // [SB] both MMA warps' commits -> token producer
+  uint64_t* w_full = bars + 56;   // [ST] weight TMA -> dequant warps
+  uint64_t* w_empty = bars + 64;  // [ST] dequant warps -> weight producer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 72);
+  int* bcast = reinterpret_cast<int*>(bars + 73);
   uint8_t* wst = smem + L::kHdr;
   uint8_t* bst = wst + L::kW;
   float* htile = reinterpret_cast<float*>(bst + L::kB);
@@ -510,25 +560,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   auto begin_of = [&](int64_t cc) -> int64_t { return cc * NI / P; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SA; ++s) {
-      mbar_init(smem_u32(&a_full[s]), kNW * 32);
+    for (int s = 0; s < 2 * SA; ++s) {
+      mbar_init(smem_u32(&a_full[s]), kDeqWarps / 2);
       mbar_init(smem_u32(&a_empty[s]), 1);
     }
     for (int s = 0; s < SD; ++s) {
-      mbar_init(smem_u32(&d_full[s]), 1);
-      mbar_init(smem_u32(&d_empty[s]), kNW * 32);
+      mbar_init(smem_u32(&d_full[s]), 2);
+      mbar_init(smem_u32(&d_empty[s]), kFoldWarps);
     }
     for (int s = 0; s < SB; ++s) {
       mbar_init(smem_u32(&b_full[s]), 32);
-      mbar_init(smem_u32(&b_empty[s]), kNW * 32);
+      mbar_init(smem_u32(&b_empty[s]), 2);
     }
     for (int s = 0; s < ST; ++s) {
       mbar_init(smem_u32(&w_full[s]), 1);
-      mbar_init(smem_u32(&w_empty[s]), kNW * 32);
+      mbar_init(smem_u32(&w_empty[s]), kDeqWarps);
     }
     fence_barrier_init();
   }
-  if (warp == kNW + 1) {
+  if (warp == kMmaWarp0) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
@@ -537,7 +587,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == kNW + 2) {
+  if (warp == kWgtWarp) {
     // ------------------------- weight producer (2-D TMA) -------------------------
     if (lane == 0) {
       int64_t ks = 0;
@@ -561,9 +611,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       }
     }
     __syncwarp();
-  } else if (warp == kNW) {
+  } else if (warp == kTokWarp) {
     // ------------------------- token producer -------------------------
-    // Lane l copies the 17 chunks of token l of the segment; a stage is
+    // Lane l copies the 17 units of token l of the segment; a stage is
     // signalled (after its copies landed and a proxy fence) LOOK stages later.
     int64_t k = 0;
     for (int64_t it = b0; it < b1; ++it) {
@@ -598,199 +648,198 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     cp_async_wait<0>();
     fence_proxy_async_smem();
     for (int64_t kk = (k > LOOK ? k - LOOK : 0); kk < k; ++kk) mbar_arrive(smem_u32(&b_full[kk % SB]));
-  } else if (warp == kNW + 1) {
-    // ------------------------------ MMA issuer ------------------------------
-    if (lane == 0) {
-      int64_t k = 0;
-      for (int64_t it = b0; it < b1; ++it) {
-        const int gp = (int)(it % GP);
-        const int ng = min(2, a.G - 2 * gp);
-        for (int gi = 0; gi < ng; ++gi, ++k) {
-          const int sa = (int)(k % SA), sd = (int)(k % SD), sb = (int)(k % SB);
-          mbar_wait(smem_u32(&a_full[sa]), (uint32_t)((k / SA) & 1), a.err);
-          mbar_wait(smem_u32(&b_full[sb]), (uint32_t)((k / SB) & 1), a.err);
-          if (k >= SD) mbar_wait(smem_u32(&d_empty[sd]), (uint32_t)(((k / SD) - 1) & 1), a.err);
-          tc_fence_after();
-          const uint32_t bbase = smem_u32(bst + sb * L::kBStage);
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int s = 0; s < 8; ++s) {
-              const uint64_t bdesc = umma_sdesc_noswizzle(bbase + s * 32 * N, 16 * N, 128);
-              umma_ts(tbase + D0 + sd * 2 * N + j * N, tbase + sa * 128 + j * 64 + s * 8, bdesc, IDESC,
-                      s > 0 ? 1u : 0u);
-            }
-          umma_commit(smem_u32(&a_empty[sa]));
-          umma_commit(smem_u32(&d_full[sd]));
-        }
+  } else if (warp == kMmaWarp0 || warp == kMmaWarp1) {
+    // ------------------------------ MMA issuers ------------------------------
+    // The whole warp runs this loop (operands stay warp-uniform); the MMAs and
+    // commits are issued by one elected lane.
+    const int mj = warp == kMmaWarp0 ? 0 : 1;
+    int64_t k = 0;
+    for (int64_t it = b0; it < b1; ++it) {
+      const int gp = (int)(it % GP);
+      const int ng = min(2, a.G - 2 * gp);
+      for (int gi = 0; gi < ng; ++gi, ++k) {
+        const int sa = (int)(k % SA), sd = (int)(k % SD), sb = (int)(k % SB);
+        mbar_wait(smem_u32(&b_full[sb]), (uint32_t)((k / SB) & 1), a.err);
+        if (k >= SD) mbar_wait(smem_u32(&d_empty[sd]), (uint32_t)(((k / SD) - 1) & 1), a.err);
+        mbar_wait(smem_u32(&a_full[2 * sa + mj]), (uint32_t)((k / SA) & 1), a.err);
+        tc_fence_after();
+        // B descriptors: low half = start address >> 4 | (LBO >> 4) << 16,
+        // high half = SBO >> 4 | version bit; step s starts at unit 1 + 2s.
+        const uint32_t c_lo = ((smem_u32(bst + sb * L::kBStage) >> 4) & 0x3FFFu) | (uint32_t)(N << 16);
+        umma_group9<2 * N>(tbase + D0 + sd * 2 * N + mj * N, tbase + sa * 128 + mj * 64, c_lo + N, kDescHi, IDESC,
+                           c_lo, tbase + CORR, IDESC_CORR);
+        umma_commit_elect(smem_u32(&a_empty[2 * sa + mj]));
+        umma_commit_elect(smem_u32(&b_empty[sb]));
+        umma_commit_elect(smem_u32(&d_full[sd]));
       }
     }
     __syncwarp();
-  } else {
-    // ------------------------------- row threads -------------------------------
-    const int j = warp >> 2, q = warp & 3, r = q * 32 + lane;
+  } else if (warp < kDeqWarps) {
+    // ------------------------------ dequant warps ------------------------------
+    const int q = warp & 3, j = warp >> 2, r = q * 32 + lane;
     const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
-    constexpr int kRows = kNW * 32;
-    const int wrow = (j * 128 + r) * 128;  // this thread's row inside a weight stage
+    const uint8_t* wrow = wst + (j * 128 + r) * 128;  // this thread's row inside a weight stage
     const int swz = r & 7;
-
+    if (j == 0) {
+      // constant A block of the correction step: k0..k2 = -1 (bf16), rest 0
+      uint32_t cv8[8] = {0xBF80BF80u, 0x0000BF80u, 0u, 0u, 0u, 0u, 0u, 0u};
+      tmem_st8(tlane + CORR, cv8);
+      tc_wait_st();
+      tc_fence_before();
+    }
+    int64_t k = 0, ks = 0;
+#pragma unroll 1
+    for (int64_t it = b0; it < b1; ++it, ++ks) {
+      const int gp = (int)(it % GP);
+      const int ng = min(2, a.G - 2 * gp);
+      const int ws = (int)(ks % ST);
+      mbar_wait(smem_u32(&w_full[ws]), (uint32_t)((ks / ST) & 1), a.err);
+      const uint8_t* wrow_p = wrow + ws * L::kWStage;
+#pragma unroll 1
+      for (int gi = 0; gi < ng; ++gi, ++k) {
+        const int sa = (int)(k % SA);
+        uint4 W[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + i) ^ swz) << 4));
+        if (k >= SA) {
+          mbar_wait(smem_u32(&a_empty[2 * sa + j]), (uint32_t)(((k / SA) - 1) & 1), a.err);
+          tc_fence_after();
+        }
+        const uint32_t acol = tlane + sa * 128 + j * 64;
+        uint32_t o0[16], o1[16], o2[16], o3[16];
+        dequant_word<Tr>(W[0].x, o0 + 0);
+        dequant_word<Tr>(W[0].y, o0 + 4);
+        dequant_word<Tr>(W[0].z, o0 + 8);
+        dequant_word<Tr>(W[0].w, o0 + 12);
+        dequant_word<Tr>(W[1].x, o1 + 0);
+        dequant_word<Tr>(W[1].y, o1 + 4);
+        dequant_word<Tr>(W[1].z, o1 + 8);
+        dequant_word<Tr>(W[1].w, o1 + 12);
+        tmem_st16(acol, o0);
+        tmem_st16(acol + 16, o1);
+        dequant_word<Tr>(W[2].x, o2 + 0);
+        dequant_word<Tr>(W[2].y, o2 + 4);
+        dequant_word<Tr>(W[2].z, o2 + 8);
+        dequant_word<Tr>(W[2].w, o2 + 12);
+        dequant_word<Tr>(W[3].x, o3 + 0);
+        dequant_word<Tr>(W[3].y, o3 + 4);
+        dequant_word<Tr>(W[3].z, o3 + 8);
+        dequant_word<Tr>(W[3].w, o3 + 12);
+        tmem_st16(acol + 32, o2);
+        tmem_st16(acol + 48, o3);
+        tc_wait_st_keep(o0, o1);
+        tc_wait_st_keep(o2, o3);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&a_full[2 * sa + j]));
+          // The weight stage is released only after every lane consumed its
+          // shared loads (the dequant above read W): the refill is an
+          // async-proxy write that is not ordered after loads still in flight.
+          if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));
+        }
+      }
+    }
+  } else if (warp < kDeqWarps + kFoldWarps) {
+    // ------------------------------- fold warps -------------------------------
+    const int fw = warp - kDeqWarps;
+    const int q = fw & 3, j = fw >> 2, r = q * 32 + lane;
+    const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
     int tile = (int)(b0 / GP);
     RowView cv;
     load_rowview<KIND>(a, tile, n_segs, j, r, cv);
     float acc[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) acc[n] = 0.f;
-
-    // flush of group counter kk: acc += scale * (D - C) for the active 8-token blocks
-    auto flush = [&](int64_t kk, float scale, int m) {
-      const int sd = (int)(kk % SD), sb = (int)(kk % SB);
-      mbar_wait(smem_u32(&d_full[sd]), (uint32_t)((kk / SD) & 1), a.err);
-      tc_fence_after();
-      uint32_t d[N / 8][8];
-#pragma unroll
-      for (int blk = 0; blk < N / 8; ++blk) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) d[blk][i] = 0u;
-        if (blk * 8 < m) tmem_ld8(tlane + D0 + sd * 2 * N + j * N + blk * 8, d[blk]);
-      }
-      tmem_ld_wait8(d[0]);
-#pragma unroll
-      for (int blk = 1; blk < N / 8; ++blk) reg_dep8(d[blk]);
-      const float* cst = reinterpret_cast<const float*>(bst + sb * L::kBStage + 16 * N * 16);
-#pragma unroll
-      for (int blk = 0; blk < N / 8; ++blk)
-        if (blk * 8 < m) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            acc[blk * 8 + i] += scale * (__uint_as_float(d[blk][i]) - cst[4 * (blk * 8 + i)]);
-        }
-      tc_fence_before();
-      mbar_arrive(smem_u32(&d_empty[sd]));
-      mbar_arrive(smem_u32(&b_empty[sb]));
+    // Group scales of the current item, and of the next one when it is in the
+    // same tile (loaded one item ahead so the loads never stall a group).
+    auto load_scales = [&](int gp_, float (&sc)[2]) {
+      const int g0 = 2 * gp_;
+      sc[0] = __half2float(__ushort_as_half(__ldg(cv.s + g0)));
+      sc[1] = g0 + 1 < a.G ? __half2float(__ushort_as_half(__ldg(cv.s + g0 + 1))) : 0.f;
     };
-
-    // Accumulators of the last `npend` k-groups (their scales in sw[0..npend-1],
-    // oldest first) are still in TMEM; a group is flushed LAG groups after its
-    // dequant, or at the end of its tile.
-    int npend = 0;
-    float sw[LAG + 1];
-#pragma unroll
-    for (int i = 0; i <= LAG; ++i) sw[i] = 0.f;
-    int64_t k = 0;  // group counter (same sequence as the MMA issuer and the token producer)
-    int64_t ks = 0; // weight stage counter
+    float sc_cur[2], sc_nxt[2];
+    load_scales((int)(b0 - (int64_t)tile * GP), sc_nxt);
+    int64_t k = 0;
 #pragma unroll 1
-    for (int64_t it = b0; it < b1; ++it, ++ks) {
+    for (int64_t it = b0; it < b1; ++it) {
       const int gp = (int)(it - (int64_t)tile * GP);
       const int ng = min(2, a.G - 2 * gp);
-      const int ws = (int)(ks % ST);
-      mbar_wait(smem_u32(&w_full[ws]), (uint32_t)((ks / ST) & 1), a.err);
-      const uint8_t* wrow_p = wst + ws * L::kWStage + wrow;
+      sc_cur[0] = sc_nxt[0];
+      sc_cur[1] = sc_nxt[1];
+      if (gp + 1 < GP && it + 1 < b1) load_scales(gp + 1, sc_nxt);
 #pragma unroll 1
       for (int gi = 0; gi < ng; ++gi, ++k) {
         const int grp = 2 * gp + gi;
-        const int sa = (int)(k % SA);
-        const bool tile_end = (grp == a.G - 1) || (it == b1 - 1 && gi == ng - 1);
-        const float scale = __half2float(__ushort_as_half(__ldg(cv.s + grp)));
-        uint4 W[4];
+        const int sd = (int)(k % SD);
+        const float scale = gi ? sc_cur[1] : sc_cur[0];
+        const int m = cv.m;
+        mbar_wait(smem_u32(&d_full[sd]), (uint32_t)((k / SD) & 1), a.err);
+        tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + i) ^ swz) << 4));
-        if (k >= SA) {
-          mbar_wait(smem_u32(&a_empty[sa]), (uint32_t)(((k / SA) - 1) & 1), a.err);
-          tc_fence_after();
-        }
+        for (int h = 0; h < N / 16; ++h) {
+          if (h * 16 < m) {
+            uint32_t d[16];
+            tmem_ld16(tlane + D0 + sd * 2 * N + j * N + h * 16, d);
+            tmem_ld_wait16(d);
 #pragma unroll
-        for (int i = 0; i < 4; i += 2) {
-          uint32_t o0[16], o1[16];
-          dequant_word<Tr>(W[i].x, o0 + 0);
-          dequant_word<Tr>(W[i].y, o0 + 4);
-          dequant_word<Tr>(W[i].z, o0 + 8);
-          dequant_word<Tr>(W[i].w, o0 + 12);
-          dequant_word<Tr>(W[i + 1].x, o1 + 0);
-          dequant_word<Tr>(W[i + 1].y, o1 + 4);
-          dequant_word<Tr>(W[i + 1].z, o1 + 8);
-          dequant_word<Tr>(W[i + 1].w, o1 + 12);
-          tmem_st16(tlane + sa * 128 + j * 64 + i * 16, o0);
-          tmem_st16(tlane + sa * 128 + j * 64 + (i + 1) * 16, o1);
-          tc_wait_st_keep(o0, o1);
+            for (int n = 0; n < 16; n += 2) ffma2(acc[h * 16 + n], acc[h * 16 + n + 1], scale, d[n], d[n + 1]);
+          }
         }
         tc_fence_before();
-        mbar_arrive(smem_u32(&a_full[sa]));
-        // Release the weight stage only now: its next TMA write (async proxy)
-        // is not ordered after shared loads whose results are still in flight,
-        // and an arrive right after issuing them let the refill overwrite rows
-        // before some lanes had read them.  The dequant above consumed W.
-        if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));
-#pragma unroll
-        for (int i = 0; i <= LAG; ++i)
-          if (i == npend) sw[i] = scale;
-        ++npend;
-        if (!tile_end) {
-          if (npend > LAG) {
-            flush(k - LAG, sw[0], cv.m);
-#pragma unroll
-            for (int i = 0; i < LAG; ++i) sw[i] = sw[i + 1];
-            --npend;
-          }
-          continue;
-        }
-#pragma unroll
-        for (int i = 0; i <= LAG; ++i)
-          if (i < npend) flush(k - npend + 1 + i, sw[i], cv.m);
-        npend = 0;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&d_empty[sd]));
+        const bool tile_end = (grp == a.G - 1) || (it == b1 - 1 && gi == ng - 1);
+        if (!tile_end) continue;
         // ---------------- finish this CTA's piece of the tile ----------------
         const int64_t ts = (int64_t)tile * GP, te = ts + GP;
         bool own = true;
         if (!(b0 <= ts && b1 >= te)) {
+          // Every piece (the last arriver's own too) goes through its partial
+          // slot; the last arriver sums the slots in CTA order, so the result
+          // does not depend on which CTA finishes last.
           const int slot = (ts <= b0) ? 0 : 1;
-          float* dst = a.part + ((((int64_t)c * 2 + slot) * kNW + warp) * N) * 32 + lane;
+          float* dst = a.part + ((((int64_t)c * 2 + slot) * kFoldWarps + fw) * N) * 32 + lane;
 #pragma unroll
           for (int n = 0; n < N; ++n) dst[n * 32] = acc[n];
           __threadfence();
-          named_bar_sync(1, kRows);
+          named_bar_sync(1, kFoldThreads);
           const int64_t c0 = cta_of(ts), c1 = cta_of(te - 1);
-          if (threadIdx.x == 0) bcast[0] = (atomicAdd(&a.tile_ctr[tile], 1) == (int)(c1 - c0));
-          named_bar_sync(1, kRows);
+          if (fw == 0 && lane == 0) bcast[0] = (atomicAdd(&a.tile_ctr[tile], 1) == (int)(c1 - c0));
+          named_bar_sync(1, kFoldThreads);
           own = bcast[0] != 0;
           if (own) {
             __threadfence();
-            float sum[N];
 #pragma unroll
-            for (int n = 0; n < N; ++n) sum[n] = 0.f;
+            for (int n = 0; n < N; ++n) acc[n] = 0.f;
             for (int64_t cc = c0; cc <= c1; ++cc) {
-              if (cc == c) {
+              const int64_t bc = begin_of(cc);
+              const int sl = (bc >= ts && bc < te) ? 0 : 1;
+              const float* src = a.part + ((((int64_t)cc * 2 + sl) * kFoldWarps + fw) * N) * 32 + lane;
 #pragma unroll
-                for (int n = 0; n < N; ++n) sum[n] += acc[n];
-              } else {
-                const int64_t bc = begin_of(cc);
-                const int sl = (bc >= ts && bc < te) ? 0 : 1;
-                const float* src = a.part + ((((int64_t)cc * 2 + sl) * kNW + warp) * N) * 32 + lane;
-#pragma unroll
-                for (int n = 0; n < N; ++n) sum[n] += ld_cg_f32(src + n * 32);
-              }
+              for (int n = 0; n < N; ++n) acc[n] += ld_cg_f32(src + n * 32);
             }
-#pragma unroll
-            for (int n = 0; n < N; ++n) acc[n] = sum[n];
-            if (threadIdx.x == 0) a.tile_ctr[tile] = 0;
+            if (fw == 0 && lane == 0) a.tile_ctr[tile] = 0;
           }
         }
         if (own) {
-          const int m = cv.m;
+          const int ft = threadIdx.x - kDeqWarps * 32;  // 0 .. kFoldThreads-1
           if (KIND == KIND_GATEUP) {
             if (j == 1) {
 #pragma unroll
               for (int n = 0; n < N; ++n) htile[r * (N + 1) + n] = acc[n];
             }
-            named_bar_sync(1, kRows);
+            named_bar_sync(1, kFoldThreads);
             if (j == 0) {
 #pragma unroll
               for (int n = 0; n < N; ++n) {
-                const float h = silu_f(acc[n]) * htile[r * (N + 1) + n];
-                htile[r * (N + 1) + n] = Tr::to_f(Tr::from_f(h));
+                const float hv = silu_f(acc[n]) * htile[r * (N + 1) + n];
+                htile[r * (N + 1) + n] = Tr::to_f(Tr::from_f(hv));
               }
             }
-            named_bar_sync(1, kRows);
+            named_bar_sync(1, kFoldThreads);
             uint8_t* dstp = a.hp + (int64_t)cv.rt * a.hp_gstride;
-            for (int task = threadIdx.x; task < m * 16; task += kRows) {
+            for (int task = ft; task < m * 16; task += kFoldThreads) {
               const int tok = task >> 4, ch = task & 15;
               float v[8];
 #pragma unroll
@@ -798,17 +847,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
               uint4 pk;
               float cp;
               pack_unit<Tr>(v, pk, cp);
-              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + tok) * kChunk + ch * 16) = pk;
+              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + tok) * kChunk + 16 + ch * 16) = pk;
               cpart[tok * 16 + ch] = cp;
             }
-            named_bar_sync(1, kRows);
-            if (threadIdx.x < m) {
+            named_bar_sync(1, kFoldThreads);
+            if (ft < m) {
               float cs = 0.f;
-              for (int u = 0; u < 16; ++u) cs += cpart[threadIdx.x * 16 + u];
-              *reinterpret_cast<float4*>(dstp + (int64_t)(cv.p0 + threadIdx.x) * kChunk + 256) =
-                  make_float4(cs, 0.f, 0.f, 0.f);
+              for (int u = 0; u < 16; ++u) cs += cpart[ft * 16 + u];
+              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + ft) * kChunk) = correction_unit(cs);
             }
-            named_bar_sync(1, kRows);
+            named_bar_sync(1, kFoldThreads);
           } else {
             const int row = cv.rt * 256 + j * 128 + r;
             if (row < a.N) {
@@ -825,20 +873,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
             }
             if (EPI == EPI_COMBINE) {
               __threadfence();
-              named_bar_sync(1, kRows);
-              if (threadIdx.x == 0) bcast[1] = (atomicAdd(&a.rt_ctr[cv.rt], 1) == n_segs - 1);
-              named_bar_sync(1, kRows);
+              named_bar_sync(1, kFoldThreads);
+              if (ft == 0) bcast[1] = (atomicAdd(&a.rt_ctr[cv.rt], 1) == n_segs - 1);
+              named_bar_sync(1, kFoldThreads);
               if (bcast[1]) {
                 __threadfence();
                 const int r0 = cv.rt * 256, nr = min(256, a.N - r0);
-                for (int task = threadIdx.x; task < a.T * nr; task += kRows) {
+                for (int task = ft; task < a.T * nr; task += kFoldThreads) {
                   const int t = task / nr, rr = r0 + task - t * nr;
                   float sacc = 0.f;
                   for (int kk = 0; kk < a.topk; ++kk)
                     sacc += ld_cg_f32(a.R + (int64_t)a.pos[t * a.topk + kk] * a.N + rr);
                   reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)t * a.ldo + rr] = Tr::from_f(sacc);
                 }
-                if (threadIdx.x == 0) a.rt_ctr[cv.rt] = 0;
+                if (ft == 0) a.rt_ctr[cv.rt] = 0;
               }
             }
           }
@@ -849,13 +897,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       if (gp == GP - 1 && it + 1 < b1) {
         ++tile;
         load_rowview<KIND>(a, tile, n_segs, j, r, cv);
+        load_scales(0, sc_nxt);
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kNW + 1) {
+  if (warp == kMmaWarp0) {
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
   }
@@ -946,7 +995,7 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.wts = take(4 * TK);
   l.xp = take((size_t)(Kin / 128) * T * kChunk);
   l.hp = take(F ? (size_t)(F / 128) * TK * kChunk : 0);
-  const size_t part = (size_t)P * 2 * kNW * 8 * nt * 32 * 4;
+  const size_t part = (size_t)P * 2 * 8 * (8 * nt) * 32 * 4;  // [CTA][2 slots][fold warp][N][32] fp32
   l.part1 = take(F ? part : 0);
   l.part2 = take(part);
   l.R = take(combine ? (size_t)TK * N2 * 4 : 0);
