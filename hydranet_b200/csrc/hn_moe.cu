@@ -438,10 +438,10 @@ struct TcSmem {
   static constexpr int kTotal = 1024 /* alignment slack */ + kHdr + kW + kB + kH;
 };
 
-// TMEM columns: SA = 2 weight stages of {A0, A1} x 64 columns (128 k as
-// bf16/f16 pairs) from column 0, SD accumulator stages of {A0, A1} x N fp32
-// columns from column 256, and the 8-column constant A block of the
-// correction step after them.  N = 16: 256 + 4 x 32 + 8; N = 32: 256 + 3 x 64 + 8.
+// TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as bf16/f16
+// pairs) from column 0, SD accumulator stages of {A0, A1} x N fp32 columns
+// after them, and the 8-column constant A block of the correction step.
+// N = 16: 3 x 128 + 3 x 32 + 8; N = 32: 2 x 128 + 3 x 64 + 8.
 constexpr int kTmemCols = 512;
 // Warp roles (a warp runs on SMSP warp % 4): dequant warps, fold warps, then
 // one role warp on each SMSP.
@@ -454,8 +454,8 @@ constexpr int kMmaWarp1 = 19;  // MMA issuer of matrix 1 (SMSP 3)
 constexpr int kTcThreads = 20 * 32;
 template <int N>
 struct TmemPlan {
-  static constexpr int SA = 2;
-  static constexpr int SD = (N == 16) ? 4 : 3;
+  static constexpr int SA = (N == 16) ? 3 : 2;
+  static constexpr int SD = 3;
   static constexpr int kD0 = SA * 128;
   static constexpr int kCorr = kD0 + SD * 2 * N;
   static_assert(kCorr + 8 <= kTmemCols, "TMEM plan exceeds 512 columns");
@@ -496,6 +496,22 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Stage index and phase bit of a ring of S mbarrier-guarded stages, advanced
+// once per use.  A consumer waits on full[idx] with parity `phase`; a producer
+// waits on empty[idx] with parity `phase ^ 1`, which a freshly initialised
+// barrier already satisfies, so the first round needs no special case.
+template <int S>
+struct Ring {
+  int idx = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++idx == S) {
+      idx = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 // Persistent grouped GEMV on the 5th-generation tensor cores.
 //
 // Work items are (tile, k-group pair); CTA c owns items [c*NI/P, (c+1)*NI/P)
@@ -522,8 +538,11 @@ template <typename Tr, int N, int KIND, int EPI, int ST, int SB>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_constant__ EngineArgs a) {
   using L = TcSmem<N, ST, SB>;
   constexpr int SA = TmemPlan<N>::SA, SD = TmemPlan<N>::SD, D0 = TmemPlan<N>::kD0, CORR = TmemPlan<N>::kCorr;
-  constexpr int LOOK = SB - 2;  // token producer signals a stage LOOK stages after issuing it
-  static_assert(LOOK >= 1 && SA <= 4 && SD <= 4 && SB <= 16 && ST <= 8, "stage counts");
+  // The token producer signals stage k after issuing group k + LOOK (its
+  // copies then had LOOK groups of time to land); issuing k + LOOK needs the
+  // MMA of k + LOOK - SB to be done, so SB - LOOK groups of slack remain.
+  constexpr int LOOK = 3;
+  static_assert(LOOK >= 1 && SB - LOOK >= 4 && SA <= 4 && SD <= 4 && SB <= 16 && ST <= 8, "stage counts");
   constexpr uint32_t IDESC = umma_idesc<Tr, 128, N>();
   constexpr uint32_t IDESC_CORR = umma_idesc<BF16, 128, N>();
   constexpr uint32_t kDescHi = (128u >> 4) | (1u << 14);  // SBO = 128 B, descriptor version 1 (bit 46)
@@ -558,6 +577,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   const int64_t b0 = c * NI / P, b1 = (c + 1) * NI / P;
   auto cta_of = [&](int64_t i) -> int64_t { return ((i + 1) * P - 1) / NI; };
   auto begin_of = [&](int64_t cc) -> int64_t { return cc * NI / P; };
+  // Items are walked with 32-bit counters: (tile0, gp0) is the first item.
+  const int n_items = (int)(b1 - b0);
+  const int tile0 = (int)(b0 / GP), gp0 = (int)(b0 - (int64_t)tile0 * GP);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2 * SA; ++s) {
@@ -590,23 +612,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   if (warp == kWgtWarp) {
     // ------------------------- weight producer (2-D TMA) -------------------------
     if (lane == 0) {
-      int64_t ks = 0;
-      for (int64_t it = b0; it < b1; ++it, ++ks) {
-        const int tile = (int)(it / GP), gp = (int)(it - (int64_t)tile * GP);
+      Ring<ST> rw;
+      int tile = tile0, gp = gp0;
+      for (int i = 0; i < n_items; ++i) {
         int seg, rt;
         TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
         const int e = a.segs[seg].x;
         const ExpertMaps* em = a.maps ? a.maps + e : &a.single_maps;
-        const int s = (int)(ks % ST);
-        if (ks >= ST) mbar_wait(smem_u32(&w_empty[s]), (uint32_t)(((ks / ST) - 1) & 1), a.err);
-        const uint32_t bar = smem_u32(&w_full[s]);
+        mbar_wait(smem_u32(&w_empty[rw.idx]), rw.phase ^ 1u, a.err);
+        const uint32_t bar = smem_u32(&w_full[rw.idx]);
         mbar_arrive_expect_tx(bar, L::kWStage);
-        const uint32_t dst = smem_u32(wst + s * L::kWStage);
+        const uint32_t dst = smem_u32(wst + rw.idx * L::kWStage);
         if (KIND == KIND_GATEUP) {
           tma_load_2d(dst, &em->gate, gp * 128, rt * 128, bar);
           tma_load_2d(dst + 16384, &em->up, gp * 128, rt * 128, bar);
         } else {
           tma_load_2d(dst, &em->down, gp * 128, rt * 256, bar);
+        }
+        rw.next();
+        if (++gp == GP) {
+          gp = 0;
+          ++tile;
         }
       }
     }
@@ -615,9 +641,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     // ------------------------- token producer -------------------------
     // Lane l copies the 17 units of token l of the segment; a stage is
     // signalled (after its copies landed and a proxy fence) LOOK stages later.
-    int64_t k = 0;
-    for (int64_t it = b0; it < b1; ++it) {
-      const int tile = (int)(it / GP), gp = (int)(it - (int64_t)tile * GP);
+    Ring<SB> rb, rs;  // rb: stage being filled; rs: next stage to signal (LOOK behind)
+    int k = 0, tile = tile0, gp = gp0;
+    for (int i = 0; i < n_items; ++i) {
       int seg, rt;
       TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
       const int4 sg = a.segs[seg];
@@ -629,39 +655,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       const int ng = min(2, a.G - 2 * gp);
       for (int gi = 0; gi < ng; ++gi, ++k) {
         const int grp = 2 * gp + gi;
-        const int stage = (int)(k % SB);
-        if (k >= SB) mbar_wait(smem_u32(&b_empty[stage]), (uint32_t)(((k / SB) - 1) & 1), a.err);
+        mbar_wait(smem_u32(&b_empty[rb.idx]), rb.phase ^ 1u, a.err);
         if (src_tok) {
-          const uint32_t dst = smem_u32(bst + stage * L::kBStage + 16 * lane);
+          const uint32_t dst = smem_u32(bst + rb.idx * L::kBStage + 16 * lane);
           const uint8_t* src = src_tok + (int64_t)grp * a.b_gstride;
 #pragma unroll
           for (int ch = 0; ch < 17; ++ch) cp_async16(dst + 16 * N * ch, src + ch * 16);
         }
         cp_async_commit();
+        rb.next();
         if (k >= LOOK) {
           cp_async_wait<LOOK>();
           fence_proxy_async_smem();  // generic-proxy writes -> read by the tensor core (async proxy)
-          mbar_arrive(smem_u32(&b_full[(k - LOOK) % SB]));
+          mbar_arrive(smem_u32(&b_full[rs.idx]));
+          rs.next();
         }
+      }
+      if (++gp == GP) {
+        gp = 0;
+        ++tile;
       }
     }
     cp_async_wait<0>();
     fence_proxy_async_smem();
-    for (int64_t kk = (k > LOOK ? k - LOOK : 0); kk < k; ++kk) mbar_arrive(smem_u32(&b_full[kk % SB]));
+    for (int r = 0; r < min(k, LOOK); ++r) {
+      mbar_arrive(smem_u32(&b_full[rs.idx]));
+      rs.next();
+    }
   } else if (warp == kMmaWarp0 || warp == kMmaWarp1) {
     // ------------------------------ MMA issuers ------------------------------
     // The whole warp runs this loop (operands stay warp-uniform); the MMAs and
     // commits are issued by one elected lane.
     const int mj = warp == kMmaWarp0 ? 0 : 1;
-    int64_t k = 0;
-    for (int64_t it = b0; it < b1; ++it) {
-      const int gp = (int)(it % GP);
+    Ring<SA> ra;
+    Ring<SD> rd;
+    Ring<SB> rb;
+    int gp = gp0;
+    for (int i = 0; i < n_items; ++i) {
       const int ng = min(2, a.G - 2 * gp);
-      for (int gi = 0; gi < ng; ++gi, ++k) {
-        const int sa = (int)(k % SA), sd = (int)(k % SD), sb = (int)(k % SB);
-        mbar_wait(smem_u32(&b_full[sb]), (uint32_t)((k / SB) & 1), a.err);
-        if (k >= SD) mbar_wait(smem_u32(&d_empty[sd]), (uint32_t)(((k / SD) - 1) & 1), a.err);
-        mbar_wait(smem_u32(&a_full[2 * sa + mj]), (uint32_t)((k / SA) & 1), a.err);
+      for (int gi = 0; gi < ng; ++gi) {
+        const int sa = ra.idx, sd = rd.idx, sb = rb.idx;
+        mbar_wait(smem_u32(&b_full[sb]), rb.phase, a.err);
+        mbar_wait(smem_u32(&d_empty[sd]), rd.phase ^ 1u, a.err);
+        mbar_wait(smem_u32(&a_full[2 * sa + mj]), ra.phase, a.err);
         tc_fence_after();
         // B descriptors: low half = start address >> 4 | (LBO >> 4) << 16,
         // high half = SBO >> 4 | version bit; step s starts at unit 1 + 2s.
@@ -671,7 +707,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         umma_commit_elect(smem_u32(&a_empty[2 * sa + mj]));
         umma_commit_elect(smem_u32(&b_empty[sb]));
         umma_commit_elect(smem_u32(&d_full[sd]));
+        ra.next();
+        rd.next();
+        rb.next();
       }
+      if (++gp == GP) gp = 0;
     }
     __syncwarp();
   } else if (warp < kDeqWarps) {
@@ -687,24 +727,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       tc_wait_st();
       tc_fence_before();
     }
-    int64_t k = 0, ks = 0;
+    Ring<ST> rw;
+    Ring<SA> ra;
+    int gp = gp0;
 #pragma unroll 1
-    for (int64_t it = b0; it < b1; ++it, ++ks) {
-      const int gp = (int)(it % GP);
+    for (int it = 0; it < n_items; ++it) {
       const int ng = min(2, a.G - 2 * gp);
-      const int ws = (int)(ks % ST);
-      mbar_wait(smem_u32(&w_full[ws]), (uint32_t)((ks / ST) & 1), a.err);
+      const int ws = rw.idx;
+      mbar_wait(smem_u32(&w_full[ws]), rw.phase, a.err);
       const uint8_t* wrow_p = wrow + ws * L::kWStage;
 #pragma unroll 1
-      for (int gi = 0; gi < ng; ++gi, ++k) {
-        const int sa = (int)(k % SA);
+      for (int gi = 0; gi < ng; ++gi) {
+        const int sa = ra.idx;
         uint4 W[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + i) ^ swz) << 4));
-        if (k >= SA) {
-          mbar_wait(smem_u32(&a_empty[2 * sa + j]), (uint32_t)(((k / SA) - 1) & 1), a.err);
-          tc_fence_after();
-        }
+        mbar_wait(smem_u32(&a_empty[2 * sa + j]), ra.phase ^ 1u, a.err);
+        tc_fence_after();
         const uint32_t acol = tlane + sa * 128 + j * 64;
         uint32_t o0[16], o1[16], o2[16], o3[16];
         dequant_word<Tr>(W[0].x, o0 + 0);
@@ -738,14 +777,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
           // async-proxy write that is not ordered after loads still in flight.
           if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));
         }
+        ra.next();
       }
+      rw.next();
+      if (++gp == GP) gp = 0;
     }
   } else if (warp < kDeqWarps + kFoldWarps) {
     // ------------------------------- fold warps -------------------------------
     const int fw = warp - kDeqWarps;
     const int q = fw & 3, j = fw >> 2, r = q * 32 + lane;
     const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
-    int tile = (int)(b0 / GP);
+    int tile = tile0;
     RowView cv;
     load_rowview<KIND>(a, tile, n_segs, j, r, cv);
     float acc[N];
@@ -759,22 +801,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       sc[1] = g0 + 1 < a.G ? __half2float(__ushort_as_half(__ldg(cv.s + g0 + 1))) : 0.f;
     };
     float sc_cur[2], sc_nxt[2];
-    load_scales((int)(b0 - (int64_t)tile * GP), sc_nxt);
-    int64_t k = 0;
+    load_scales(gp0, sc_nxt);
+    Ring<SD> rd;
+    int gp = gp0;
 #pragma unroll 1
-    for (int64_t it = b0; it < b1; ++it) {
-      const int gp = (int)(it - (int64_t)tile * GP);
+    for (int it = 0; it < n_items; ++it) {
       const int ng = min(2, a.G - 2 * gp);
       sc_cur[0] = sc_nxt[0];
       sc_cur[1] = sc_nxt[1];
-      if (gp + 1 < GP && it + 1 < b1) load_scales(gp + 1, sc_nxt);
+      if (gp + 1 < GP && it + 1 < n_items) load_scales(gp + 1, sc_nxt);
 #pragma unroll 1
-      for (int gi = 0; gi < ng; ++gi, ++k) {
+      for (int gi = 0; gi < ng; ++gi) {
         const int grp = 2 * gp + gi;
-        const int sd = (int)(k % SD);
+        const int sd = rd.idx;
         const float scale = gi ? sc_cur[1] : sc_cur[0];
         const int m = cv.m;
-        mbar_wait(smem_u32(&d_full[sd]), (uint32_t)((k / SD) & 1), a.err);
+        mbar_wait(smem_u32(&d_full[sd]), rd.phase, a.err);
         tc_fence_after();
 #pragma unroll
         for (int h = 0; h < N / 16; ++h) {
@@ -789,7 +831,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&d_empty[sd]));
-        const bool tile_end = (grp == a.G - 1) || (it == b1 - 1 && gi == ng - 1);
+        rd.next();
+        const bool tile_end = (grp == a.G - 1) || (it == n_items - 1 && gi == ng - 1);
         if (!tile_end) continue;
         // ---------------- finish this CTA's piece of the tile ----------------
         const int64_t ts = (int64_t)tile * GP, te = ts + GP;
@@ -894,10 +937,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 #pragma unroll
         for (int n = 0; n < N; ++n) acc[n] = 0.f;
       }
-      if (gp == GP - 1 && it + 1 < b1) {
-        ++tile;
-        load_rowview<KIND>(a, tile, n_segs, j, r, cv);
-        load_scales(0, sc_nxt);
+      if (++gp == GP) {
+        gp = 0;
+        if (it + 1 < n_items) {
+          ++tile;
+          load_rowview<KIND>(a, tile, n_segs, j, r, cv);
+          load_scales(0, sc_nxt);
+        }
       }
     }
   }
@@ -918,7 +964,7 @@ static int pick_nt(int64_t max_tokens_per_expert) { return max_tokens_per_expert
 
 template <int N>
 struct TcTune {
-  static constexpr int ST = 4, SB = 6;
+  static constexpr int ST = 4, SB = 8;
 };
 
 template <typename Tr, int N, int KIND, int EPI>
