@@ -41,6 +41,7 @@ namespace hn {
 constexpr int kChunk = 272;  // bytes per (token, k-group): 16 B correction unit + 16 units of 16 B
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 32;
+constexpr int kPlanSmemEntries = 4096;  // routing entries the plan builder copies into shared memory
 
 enum { KIND_GATEUP = 0, KIND_DOWN = 1 };
 enum { EPI_COMBINE = 0, EPI_STORE = 1 };
@@ -139,6 +140,7 @@ struct RouteArgs {
   float* out_w;
   float* out_logits;
   int seg;
+  int wbuf_off;  // byte offset of the router-weight chunk in dynamic shared memory
   Plan plan;
 };
 
@@ -148,21 +150,61 @@ __device__ __forceinline__ float load_any(const void* p, int dtype, int64_t i) {
   return __half2float(reinterpret_cast<const __half*>(p)[i]);
 }
 
+// Router weights are brought into shared memory in chunks of whole expert rows
+// (at most kRouteChunkBytes) by one bulk async copy each, so a chunk costs one
+// memory round trip.  The kernel body is kept free of large unrolled blocks:
+// at small T one CTA runs it once, and every instruction it executes is
+// fetched into the instruction cache once.
+constexpr int kRouteChunkBytes = 64 * 1024;
+
+__host__ __device__ inline int route_esize(int dtype) { return dtype == HN_DTYPE_F32 ? 4 : 2; }
+__host__ __device__ inline int route_chunk_experts(int H, int E, int dtype) {
+  const int per = kRouteChunkBytes / (H * route_esize(dtype));
+  return per < 1 ? 1 : (per < E ? per : E);
+}
+
 template <typename Tr>
 __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   extern __shared__ __align__(16) float rsm[];
   float* xs = rsm;                 // [H]
   float* lg = xs + a.H;            // [E]
   float* cpart = lg + a.E;         // [H/8]
+  float* scs = cpart + a.H / 8;    // [E] selection scores
+  // plan copies of the routing follow scs (see the plan section); the router
+  // weight chunk sits at the end of the dynamic shared memory
   __shared__ int s_last;
   __shared__ int s_idx[kMaxTopK];
   __shared__ float s_w[kMaxTopK];
+  __shared__ __align__(8) uint64_t s_wbar;
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const typename Tr::T* xrow = reinterpret_cast<const typename Tr::T*>(a.x) + (int64_t)t * a.ldx;
+  const int esz = route_esize(a.rw_dtype);
+  const int CE = route_chunk_experts(a.H, a.E, a.rw_dtype);
+  const bool bulk = a.mode == ROUTE_COMPUTE && (reinterpret_cast<uintptr_t>(a.rw) & 15) == 0;
+  uint8_t* wbuf = reinterpret_cast<uint8_t*>(rsm) + a.wbuf_off;
+  if (bulk && tid == 0) {
+    mbar_init(smem_u32(&s_wbar), 1);
+    fence_barrier_init();
+    const uint32_t bytes = (uint32_t)(min(CE, a.E) * a.H * esz);
+    mbar_arrive_expect_tx(smem_u32(&s_wbar), bytes);
+    bulk_g2s(smem_u32(wbuf), a.rw, bytes, smem_u32(&s_wbar));
+  }
   // The engine's arrival counters start every call at zero, whatever an
   // earlier call of another shape left in this part of the workspace.
   for (int i = t * 256 + tid; i < a.plan.n_ctr; i += gridDim.x * 256) a.plan.ctr1[i] = 0;
-  for (int i = tid; i < a.H; i += 256) xs[i] = Tr::to_f(xrow[i]);
+  if ((reinterpret_cast<uintptr_t>(xrow) & 15) == 0) {
+    const uint4* xv = reinterpret_cast<const uint4*>(xrow);
+    for (int i = tid; i < a.H / 8; i += 256) {
+      const uint4 v = __ldg(xv + i);
+      const typename Tr::T2* h2 = reinterpret_cast<const typename Tr::T2*>(&v);
+      for (int u = 0; u < 4; ++u) {
+        xs[8 * i + 2 * u] = Tr::to_f(h2[u].x);
+        xs[8 * i + 2 * u + 1] = Tr::to_f(h2[u].y);
+      }
+    }
+  } else {
+    for (int i = tid; i < a.H; i += 256) xs[i] = Tr::to_f(xrow[i]);
+  }
   __syncthreads();
 
   // 1. staged activations + per-group correction C
@@ -188,14 +230,59 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
 
   // 2. routing for this token
   if (a.mode == ROUTE_COMPUTE) {
-    for (int e = warp; e < a.E; e += 8) {
-      float acc = 0.f;
-      for (int i = lane; i < a.H; i += 32) acc += xs[i] * load_any(a.rw, a.rw_dtype, (int64_t)e * a.H + i);
-#pragma unroll
-      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) lg[e] = a.logits_act ? Tr::to_f(Tr::from_f(acc)) : acc;
+    // router logits, one warp per expert row of the chunk in shared memory
+    for (int c0 = 0; c0 < a.E; c0 += CE) {
+      const int ce = min(CE, a.E - c0);
+      if (bulk) mbar_wait(smem_u32(&s_wbar), (uint32_t)((c0 / CE) & 1), a.plan.err);
+      for (int r = warp; r < ce; r += 8) {
+        const int e = c0 + r;
+        float acc = 0.f;
+        if (bulk) {
+          const uint8_t* row = wbuf + (size_t)r * a.H * esz;
+          if (esz == 4) {
+            for (int i = lane; i < a.H / 4; i += 32) {
+              const float4 w = reinterpret_cast<const float4*>(row)[i];
+              acc = fmaf(xs[4 * i], w.x, acc);
+              acc = fmaf(xs[4 * i + 1], w.y, acc);
+              acc = fmaf(xs[4 * i + 2], w.z, acc);
+              acc = fmaf(xs[4 * i + 3], w.w, acc);
+            }
+          } else {
+            const bool bf = a.rw_dtype == HN_DTYPE_BF16;
+            for (int i = lane; i < a.H / 8; i += 32) {
+              const uint4 w = reinterpret_cast<const uint4*>(row)[i];
+              const uint32_t q[4] = {w.x, w.y, w.z, w.w};
+              for (int c = 0; c < 4; ++c) {
+                float lo, hi;
+                if (bf) {
+                  lo = __uint_as_float(q[c] << 16);
+                  hi = __uint_as_float(q[c] & 0xFFFF0000u);
+                } else {
+                  const __half2 hh = *reinterpret_cast<const __half2*>(&q[c]);
+                  lo = __low2float(hh);
+                  hi = __high2float(hh);
+                }
+                acc = fmaf(xs[8 * i + 2 * c], lo, acc);
+                acc = fmaf(xs[8 * i + 2 * c + 1], hi, acc);
+              }
+            }
+          }
+        } else {
+          for (int i = lane; i < a.H; i += 32) acc += xs[i] * load_any(a.rw, a.rw_dtype, (int64_t)e * a.H + i);
+        }
+        for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) lg[e] = a.logits_act ? Tr::to_f(Tr::from_f(acc)) : acc;
+      }
+      __syncthreads();
+      if (bulk && c0 + CE < a.E && tid == 0) {
+        // every warp has finished with the chunk (its values were consumed
+        // before the barrier above), so the buffer can be refilled
+        const uint32_t bytes = (uint32_t)(min(CE, a.E - c0 - CE) * a.H * esz);
+        mbar_arrive_expect_tx(smem_u32(&s_wbar), bytes);
+        bulk_g2s(smem_u32(wbuf), reinterpret_cast<const uint8_t*>(a.rw) + (size_t)(c0 + CE) * a.H * esz, bytes,
+                 smem_u32(&s_wbar));
+      }
     }
-    __syncthreads();
     if (warp == 0) {
       // optional cache-affinity bonus (model/router.py:132-175)
       if (a.kind == HN_ROUTER_SOFTMAX_TOPK && a.bonus) {
@@ -219,29 +306,25 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
       }
       if (a.out_logits)
         for (int e = lane; e < a.E; e += 32) a.out_logits[(int64_t)t * a.E + e] = lg[e];
-      // selection scores; ties resolve to the lower expert index
-      float sc[kMaxExperts / 32];
-      const int per = (a.E + 31) / 32;
-      for (int j = 0; j < per; ++j) {
-        const int e = lane + 32 * j;
-        float v = -INFINITY;
-        if (e < a.E) {
-          v = lg[e];
-          if (a.kind == HN_ROUTER_SIGMOID_TOPK) {
-            v = 1.0f / (1.0f + expf(-v));
-            if (a.bias) v += a.bias[e];
-          }
-          if (v != v) v = -INFINITY;  // a NaN score never wins a slot
+      // selection scores in shared memory; ties resolve to the lower index
+      for (int e = lane; e < a.E; e += 32) {
+        float v = lg[e];
+        if (a.kind == HN_ROUTER_SIGMOID_TOPK) {
+          v = 1.0f / (1.0f + expf(-v));
+          if (a.bias) v += a.bias[e];
         }
-        sc[j] = v;
+        if (v != v) v = -INFINITY;  // a NaN score never wins a slot
+        scs[e] = v;
       }
+      __syncwarp();
+#pragma unroll 1
       for (int k = 0; k < a.K; ++k) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-        for (int j = 0; j < per; ++j) {
-          const int e = lane + 32 * j;
-          if (e < a.E && (sc[j] > bv || (sc[j] == bv && e < bi))) {
-            bv = sc[j];
+        for (int e = lane; e < a.E; e += 32) {
+          const float v = scs[e];
+          if (v > bv || (v == bv && e < bi)) {
+            bv = v;
             bi = e;
           }
         }
@@ -254,40 +337,42 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
           }
         }
         if (bi >= a.E) bi = 0;  // unreachable for finite scores; keeps the index in range
-        if ((bi & 31) == lane) sc[bi >> 5] = -INFINITY;
-        if (lane == 0) s_idx[k] = bi;
+        if (lane == 0) {
+          s_idx[k] = bi;
+          scs[bi] = -INFINITY;
+        }
+        __syncwarp();
       }
-      __syncwarp();
       if (lane == 0) {
-        float w[kMaxTopK];
+        // weights are built in shared memory (s_w)
         if (a.kind == HN_ROUTER_SOFTMAX_TOPK) {
           // softmax over the selected logits (model/router.py:114), renormalised (:117)
           float mx = -INFINITY;
           for (int k = 0; k < a.K; ++k) mx = fmaxf(mx, lg[s_idx[k]]);
-          float s = 0.f;
+          float sum = 0.f;
           for (int k = 0; k < a.K; ++k) {
-            w[k] = expf(lg[s_idx[k]] - mx);
-            s += w[k];
+            s_w[k] = expf(lg[s_idx[k]] - mx);
+            sum += s_w[k];
           }
           float s2 = 0.f;
           for (int k = 0; k < a.K; ++k) {
-            w[k] = w[k] / s;
-            s2 += w[k];
+            s_w[k] = s_w[k] / sum;
+            s2 += s_w[k];
           }
-          for (int k = 0; k < a.K; ++k) w[k] = w[k] / s2;
+          for (int k = 0; k < a.K; ++k) s_w[k] = s_w[k] / s2;
         } else {
           // sigmoid scores of the selected experts, unbiased (model/glm4.py:300-307)
-          float s = 0.f;
+          float sum = 0.f;
           for (int k = 0; k < a.K; ++k) {
-            w[k] = 1.0f / (1.0f + expf(-lg[s_idx[k]]));
-            s += w[k];
+            s_w[k] = 1.0f / (1.0f + expf(-lg[s_idx[k]]));
+            sum += s_w[k];
           }
           for (int k = 0; k < a.K; ++k) {
-            if (a.norm) w[k] = w[k] / (s + 1e-9f);
-            w[k] = w[k] * a.scaling;
+            if (a.norm) s_w[k] = s_w[k] / (sum + 1e-9f);
+            s_w[k] = s_w[k] * a.scaling;
           }
         }
-        for (int k = 0; k < a.K; ++k) s_w[k] = Tr::to_f(Tr::from_f(w[k]));  // cast to the activation dtype
+        for (int k = 0; k < a.K; ++k) s_w[k] = Tr::to_f(Tr::from_f(s_w[k]));  // cast to the activation dtype
       }
       __syncwarp();
     }
@@ -325,10 +410,19 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   __threadfence();
   int* cnt = reinterpret_cast<int*>(rsm);  // reuse (>= E ints available: H >= 128 floats)
   int* off = cnt + a.E;
-  for (int e = tid; e < a.E; e += 256) cnt[e] = 0;
-  __syncthreads();
   const int TK = a.T * a.K;
-  for (int i = tid; i < TK; i += 256) atomicAdd(&cnt[__ldcg(a.plan.idx + i)], 1);
+  // every token's routing, read once into shared memory when it fits
+  const bool in_smem = TK <= kPlanSmemEntries;
+  int* pidx = reinterpret_cast<int*>(rsm + a.H + 2 * a.E + a.H / 8);
+  float* pwts = reinterpret_cast<float*>(pidx + (in_smem ? TK : 0));
+  for (int e = tid; e < a.E; e += 256) cnt[e] = 0;
+  if (in_smem)
+    for (int i = tid; i < TK; i += 256) {
+      pidx[i] = __ldcg(a.plan.idx + i);
+      pwts[i] = __ldcg(a.plan.wts + i);
+    }
+  __syncthreads();
+  for (int i = tid; i < TK; i += 256) atomicAdd(&cnt[in_smem ? pidx[i] : __ldcg(a.plan.idx + i)], 1);
   __syncthreads();
   if (tid == 0) {
     int o = 0, ns = 0;
@@ -350,13 +444,14 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
     for (int t0 = 0; t0 < a.T; t0 += 32) {
       const int tt = t0 + lane;
       for (int k = 0; k < a.K; ++k) {
-        const bool hit = tt < a.T && __ldcg(a.plan.idx + (int64_t)tt * a.K + k) == e;
+        const int64_t at = (int64_t)tt * a.K + k;
+        const bool hit = tt < a.T && (in_smem ? pidx[at] : __ldcg(a.plan.idx + at)) == e;
         const unsigned bal = __ballot_sync(0xffffffffu, hit);
         if (hit) {
           const int p = off[e] + base + __popc(bal & ((1u << lane) - 1u));
           a.plan.pos[(int64_t)tt * a.K + k] = p;
           a.plan.a_tok[p] = tt;
-          a.plan.a_w[p] = __ldcg(a.plan.wts + (int64_t)tt * a.K + k);
+          a.plan.a_w[p] = in_smem ? pwts[at] : __ldcg(a.plan.wts + at);
         }
         base += __popc(bal);
       }
@@ -583,7 +678,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2 * SA; ++s) {
-      mbar_init(smem_u32(&a_full[s]), kDeqWarps / 2);
+      mbar_init(smem_u32(&a_full[s]), kDeqWarps / 2);  // the dequant warps of one matrix
       mbar_init(smem_u32(&a_empty[s]), 1);
     }
     for (int s = 0; s < SD; ++s) {
@@ -727,25 +822,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       tc_wait_st();
       tc_fence_before();
     }
+    // Software-pipelined: the shared loads of the next group (and, at an item
+    // boundary, the wait for the next weight stage) are issued while this
+    // group's TMEM stores are in flight.
     Ring<ST> rw;
     Ring<SA> ra;
     int gp = gp0;
-#pragma unroll 1
-    for (int it = 0; it < n_items; ++it) {
-      const int ng = min(2, a.G - 2 * gp);
-      const int ws = rw.idx;
-      mbar_wait(smem_u32(&w_full[ws]), rw.phase, a.err);
-      const uint8_t* wrow_p = wrow + ws * L::kWStage;
-#pragma unroll 1
-      for (int gi = 0; gi < ng; ++gi) {
-        const int sa = ra.idx;
-        uint4 W[4];
+    int ng = min(2, a.G - 2 * gp);
+    mbar_wait(smem_u32(&w_full[rw.idx]), rw.phase, a.err);
+    uint4 Wn[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + i) ^ swz) << 4));
-        mbar_wait(smem_u32(&a_empty[2 * sa + j]), ra.phase ^ 1u, a.err);
-        tc_fence_after();
-        const uint32_t acol = tlane + sa * 128 + j * 64;
-        uint32_t o0[16], o1[16], o2[16], o3[16];
+    for (int i = 0; i < 4; ++i) Wn[i] = *reinterpret_cast<const uint4*>(wrow + rw.idx * L::kWStage + ((i ^ swz) << 4));
+    int gi = 0;
+#pragma unroll 1
+    for (int it = 0; it < n_items;) {
+      const int sa = ra.idx, ws = rw.idx;
+      uint4 W[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) W[i] = Wn[i];
+      mbar_wait(smem_u32(&a_empty[2 * sa + j]), ra.phase ^ 1u, a.err);
+      tc_fence_after();
+      const uint32_t acol = tlane + sa * 128 + j * 64;
+      {
+        uint32_t o0[16], o1[16];
         dequant_word<Tr>(W[0].x, o0 + 0);
         dequant_word<Tr>(W[0].y, o0 + 4);
         dequant_word<Tr>(W[0].z, o0 + 8);
@@ -756,6 +855,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         dequant_word<Tr>(W[1].w, o1 + 12);
         tmem_st16(acol, o0);
         tmem_st16(acol + 16, o1);
+      }
+      {
+        uint32_t o2[16], o3[16];
         dequant_word<Tr>(W[2].x, o2 + 0);
         dequant_word<Tr>(W[2].y, o2 + 4);
         dequant_word<Tr>(W[2].z, o2 + 8);
@@ -766,21 +868,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         dequant_word<Tr>(W[3].w, o3 + 12);
         tmem_st16(acol + 32, o2);
         tmem_st16(acol + 48, o3);
-        tc_wait_st_keep(o0, o1);
-        tc_wait_st_keep(o2, o3);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(smem_u32(&a_full[2 * sa + j]));
-          // The weight stage is released only after every lane consumed its
-          // shared loads (the dequant above read W): the refill is an
-          // async-proxy write that is not ordered after loads still in flight.
-          if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));
-        }
-        ra.next();
       }
-      rw.next();
-      if (++gp == GP) gp = 0;
+      // advance to the next group and prefetch its weights
+      const bool last_in_item = (gi == ng - 1);
+      bool more = true;
+      if (!last_in_item) {
+        ++gi;
+      } else {
+        gi = 0;
+        ++it;
+        more = it < n_items;
+        if (++gp == GP) gp = 0;
+        ng = min(2, a.G - 2 * gp);
+        rw.next();
+        if (more) mbar_wait(smem_u32(&w_full[rw.idx]), rw.phase, a.err);
+      }
+      if (more) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          Wn[i] = *reinterpret_cast<const uint4*>(wrow + rw.idx * L::kWStage + (((gi * 4 + i) ^ swz) << 4));
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&a_full[2 * sa + j]));
+        // The weight stage is released only after every lane consumed its
+        // shared loads (the dequant above read W): the refill is an
+        // async-proxy write that is not ordered after loads still in flight.
+        if (last_in_item) mbar_arrive(smem_u32(&w_empty[ws]));
+      }
+      ra.next();
     }
   } else if (warp < kDeqWarps + kFoldWarps) {
     // ------------------------------- fold warps -------------------------------
@@ -1091,11 +1209,17 @@ static int grid_p(int nt) {
 
 template <typename Tr>
 static int launch_route(const RouteArgs& ra, cudaStream_t s) {
-  const size_t sm = (size_t)(ra.H + ra.E + ra.H / 8) * 4;
-  const size_t need = std::max(sm, (size_t)(2 * ra.E) * 4);
-  if (need > 48 * 1024) HN_CUDA(cudaFuncSetAttribute(route_prep_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    (int)need));
-  route_prep_kernel<Tr><<<ra.T, 256, need, s>>>(ra);
+  const int64_t TK = (int64_t)ra.T * ra.K;
+  RouteArgs r = ra;
+  size_t sm = (size_t)(ra.H + 2 * ra.E + ra.H / 8) * 4 + (TK <= kPlanSmemEntries ? (size_t)TK * 8 : 0);
+  sm = std::max(sm, (size_t)(2 * ra.E) * 4);
+  sm = (sm + 15) & ~(size_t)15;
+  r.wbuf_off = (int)sm;
+  if (ra.mode == ROUTE_COMPUTE) sm += (size_t)route_chunk_experts(ra.H, ra.E, ra.rw_dtype) * ra.H * route_esize(ra.rw_dtype);
+  HN_REQUIRE(sm <= 227 * 1024, "router: hidden size too large for the shared-memory plan");
+  if (sm > 48 * 1024)
+    HN_CUDA(cudaFuncSetAttribute(route_prep_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  route_prep_kernel<Tr><<<ra.T, 256, sm, s>>>(r);
   HN_CUDA(cudaGetLastError());
   return HN_OK;
 }
