@@ -410,6 +410,33 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // Dequantise one 32-bit word (8 nibbles of k = 8w..8w+7) into 4 TMEM columns of
 // bf16/f16 pairs: (n0,n4) (n2,n6) as 2^e+n, (n1,n5) (n3,n7) as 2^e+8n (bf16) or
 // 2^e+16n (f16).
+// Right shifts done on the FMA pipe: w >> k == mulhi(w, 2^(32-k)).  The
+// multipliers are passed in registers loaded from kernel arguments so the
+// compiler cannot turn them back into shifts, which would put all of the
+// dequantisation on the (half-rate) integer ALU pipe.
+struct ShiftMul {
+  uint32_t m1, m8, m9;  // 2^31, 2^24, 2^23
+};
+__device__ __forceinline__ uint32_t mulhi_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <typename Tr>
+__device__ __forceinline__ void dequant_word_fma(uint32_t w, uint32_t* o, const ShiftMul& sm) {
+  const uint32_t M = Tr::kMagic;
+  const uint32_t w8 = mulhi_u32(w, sm.m8);
+  o[0] = lop3_and_or<0x000F000Fu>(w, M);
+  o[1] = lop3_and_or<0x000F000Fu>(w8, M);
+  if constexpr (Tr::kMagic == BF16::kMagic) {
+    o[2] = lop3_and_or<0x00780078u>(mulhi_u32(w, sm.m1), M);
+    o[3] = lop3_and_or<0x00780078u>(mulhi_u32(w, sm.m9), M);
+  } else {
+    o[2] = lop3_and_or<0x00F000F0u>(w, M);
+    o[3] = lop3_and_or<0x00F000F0u>(w8, M);
+  }
+}
+
 template <typename Tr>
 __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t* o) {
   const uint32_t M = Tr::kMagic;

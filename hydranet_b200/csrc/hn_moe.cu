@@ -470,6 +470,7 @@ struct ExpertMaps {
 static_assert(sizeof(ExpertMaps) == 384, "ExpertMaps layout");
 
 struct EngineArgs {
+  ShiftMul shm;  // 2^31, 2^24, 2^23 (see dequant_word_fma)
   int K;     // reduction length (multiple of 128)
   int G;     // K / 128
   int N;     // weight rows
@@ -814,6 +815,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     const int q = warp & 3, j = warp >> 2, r = q * 32 + lane;
     const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
     const uint8_t* wrow = wst + (j * 128 + r) * 128;  // this thread's row inside a weight stage
+    const ShiftMul shm = a.shm;
     const int swz = r & 7;
     if (j == 0) {
       // constant A block of the correction step: k0..k2 = -1 (bf16), rest 0
@@ -822,83 +824,68 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       tc_wait_st();
       tc_fence_before();
     }
-    // Software-pipelined: the shared loads of the next group (and, at an item
-    // boundary, the wait for the next weight stage) are issued while this
-    // group's TMEM stores are in flight.
+    // Each group: (at an item start) wait for the weight stage, load this
+    // thread's 64 bytes of the group, wait for the A stage, dequantise into
+    // TMEM, signal.  Nothing here waits on a later item, so a group's signal
+    // never depends on the next weight stage having landed.
     Ring<ST> rw;
     Ring<SA> ra;
     int gp = gp0;
-    int ng = min(2, a.G - 2 * gp);
-    mbar_wait(smem_u32(&w_full[rw.idx]), rw.phase, a.err);
-    uint4 Wn[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) Wn[i] = *reinterpret_cast<const uint4*>(wrow + rw.idx * L::kWStage + ((i ^ swz) << 4));
-    int gi = 0;
 #pragma unroll 1
-    for (int it = 0; it < n_items;) {
-      const int sa = ra.idx, ws = rw.idx;
-      uint4 W[4];
+    for (int it = 0; it < n_items; ++it) {
+      const int ng = min(2, a.G - 2 * gp);
+      const int ws = rw.idx;
+      mbar_wait(smem_u32(&w_full[ws]), rw.phase, a.err);
+      const uint8_t* wrow_p = wrow + ws * L::kWStage;
+#pragma unroll 1
+      for (int gi = 0; gi < ng; ++gi) {
+        const int sa = ra.idx;
+        uint4 W[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) W[i] = Wn[i];
-      mbar_wait(smem_u32(&a_empty[2 * sa + j]), ra.phase ^ 1u, a.err);
-      tc_fence_after();
-      const uint32_t acol = tlane + sa * 128 + j * 64;
-      {
-        uint32_t o0[16], o1[16];
-        dequant_word<Tr>(W[0].x, o0 + 0);
-        dequant_word<Tr>(W[0].y, o0 + 4);
-        dequant_word<Tr>(W[0].z, o0 + 8);
-        dequant_word<Tr>(W[0].w, o0 + 12);
-        dequant_word<Tr>(W[1].x, o1 + 0);
-        dequant_word<Tr>(W[1].y, o1 + 4);
-        dequant_word<Tr>(W[1].z, o1 + 8);
-        dequant_word<Tr>(W[1].w, o1 + 12);
-        tmem_st16(acol, o0);
-        tmem_st16(acol + 16, o1);
+        for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + i) ^ swz) << 4));
+        mbar_wait(smem_u32(&a_empty[2 * sa + j]), ra.phase ^ 1u, a.err);
+        tc_fence_after();
+        const uint32_t acol = tlane + sa * 128 + j * 64;
+        {
+          uint32_t o0[16], o1[16];
+          dequant_word_fma<Tr>(W[0].x, o0 + 0, shm);
+          dequant_word_fma<Tr>(W[0].y, o0 + 4, shm);
+          dequant_word_fma<Tr>(W[0].z, o0 + 8, shm);
+          dequant_word_fma<Tr>(W[0].w, o0 + 12, shm);
+          dequant_word_fma<Tr>(W[1].x, o1 + 0, shm);
+          dequant_word_fma<Tr>(W[1].y, o1 + 4, shm);
+          dequant_word_fma<Tr>(W[1].z, o1 + 8, shm);
+          dequant_word_fma<Tr>(W[1].w, o1 + 12, shm);
+          tmem_st16(acol, o0);
+          tmem_st16(acol + 16, o1);
+        }
+        {
+          uint32_t o2[16], o3[16];
+          dequant_word_fma<Tr>(W[2].x, o2 + 0, shm);
+          dequant_word_fma<Tr>(W[2].y, o2 + 4, shm);
+          dequant_word_fma<Tr>(W[2].z, o2 + 8, shm);
+          dequant_word_fma<Tr>(W[2].w, o2 + 12, shm);
+          dequant_word_fma<Tr>(W[3].x, o3 + 0, shm);
+          dequant_word_fma<Tr>(W[3].y, o3 + 4, shm);
+          dequant_word_fma<Tr>(W[3].z, o3 + 8, shm);
+          dequant_word_fma<Tr>(W[3].w, o3 + 12, shm);
+          tmem_st16(acol + 32, o2);
+          tmem_st16(acol + 48, o3);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&a_full[2 * sa + j]));
+          // The weight stage is released only after every lane consumed its
+          // shared loads (the dequant above read W): the refill is an
+          // async-proxy write that is not ordered after loads still in flight.
+          if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));
+        }
+        ra.next();
       }
-      {
-        uint32_t o2[16], o3[16];
-        dequant_word<Tr>(W[2].x, o2 + 0);
-        dequant_word<Tr>(W[2].y, o2 + 4);
-        dequant_word<Tr>(W[2].z, o2 + 8);
-        dequant_word<Tr>(W[2].w, o2 + 12);
-        dequant_word<Tr>(W[3].x, o3 + 0);
-        dequant_word<Tr>(W[3].y, o3 + 4);
-        dequant_word<Tr>(W[3].z, o3 + 8);
-        dequant_word<Tr>(W[3].w, o3 + 12);
-        tmem_st16(acol + 32, o2);
-        tmem_st16(acol + 48, o3);
-      }
-      // advance to the next group and prefetch its weights
-      const bool last_in_item = (gi == ng - 1);
-      bool more = true;
-      if (!last_in_item) {
-        ++gi;
-      } else {
-        gi = 0;
-        ++it;
-        more = it < n_items;
-        if (++gp == GP) gp = 0;
-        ng = min(2, a.G - 2 * gp);
-        rw.next();
-        if (more) mbar_wait(smem_u32(&w_full[rw.idx]), rw.phase, a.err);
-      }
-      if (more) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          Wn[i] = *reinterpret_cast<const uint4*>(wrow + rw.idx * L::kWStage + (((gi * 4 + i) ^ swz) << 4));
-      }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(smem_u32(&a_full[2 * sa + j]));
-        // The weight stage is released only after every lane consumed its
-        // shared loads (the dequant above read W): the refill is an
-        // async-proxy write that is not ordered after loads still in flight.
-        if (last_in_item) mbar_arrive(smem_u32(&w_empty[ws]));
-      }
-      ra.next();
+      rw.next();
+      if (++gp == GP) gp = 0;
     }
   } else if (warp < kDeqWarps + kFoldWarps) {
     // ------------------------------- fold warps -------------------------------
@@ -1080,9 +1067,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 // Tokens per segment = N of the MMA (16 or 32); 8*nt with nt in {2, 4}.
 static int pick_nt(int64_t max_tokens_per_expert) { return max_tokens_per_expert <= 16 ? 2 : 4; }
 
+// Weight stages (32 KB each) and token stages per tile width N; the totals
+// stay within 227 KB of shared memory.
 template <int N>
 struct TcTune {
-  static constexpr int ST = 4, SB = 8;
+  static constexpr int ST = (N == 16) ? 5 : 4, SB = 8;
 };
 
 template <typename Tr, int N, int KIND, int EPI>
@@ -1351,6 +1340,7 @@ static int run_moe(const MoECall& m) {
   if (rc || !m.run_experts) return rc;
 
   EngineArgs e1{};
+  e1.shm = ShiftMul{1u << 31, 1u << 24, 1u << 23};
   e1.K = (int)m.H;
   e1.G = (int)(m.H / 128);
   e1.N = (int)m.F;
@@ -1595,6 +1585,7 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   ra.seg = seg_tokens(nt);
   ra.plan = plan;
   EngineArgs e{};
+  e.shm = ShiftMul{1u << 31, 1u << 24, 1u << 23};
   e.K = (int)K;
   e.G = (int)(K / 128);
   e.N = (int)N;
