@@ -58,63 +58,87 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+# DRAM bytes (read + write) of one gate/up engine launch, from the ncu capture
+# summarised in profiles/ (per launch, same workload); None where not captured.
+GATEUP_TRAFFIC = {1: 130372352, 64: 504572672}
+
+
 def blob_bytes(h, f, g=128):
     return 3 * (f * h // 2 + f * (h // g) * 2)
 
 
 class ClockSampler:
-    """nvidia-smi sampling during the timed region (read-only queries)."""
+    """SM clock and clock-event reasons sampled DURING the timed region.
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    NVML is polled from a thread about every millisecond (read-only queries),
+    so even a region of a few milliseconds gets samples; nvidia-smi at its
+    shortest interval is the fallback when NVML is unavailable.
+    """
 
-    def __init__(self, gpu_index: int):
+    # NVML clock-event reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, gpu_index: int, period_s: float = 0.001):
         self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+        self.period = period_s
+        self.sm, self.smax, self.mask = [], 0.0, 0
+        self._stop = threading.Event()
+        self.t = None
+        self.nvml = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self._physical_index())
+            self.smax = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nvml = (nv, h, reasons)
+            self._poll_once()  # the timed region may be shorter than one period
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except OSError:
-            self.proc = None
+        except Exception:
+            self.nvml = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _physical_index(self):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            ids = [v.strip() for v in vis.split(",") if v.strip()]
+            if self.gpu < len(ids) and ids[self.gpu].isdigit():
+                return int(ids[self.gpu])
+        return self.gpu
+
+    def _poll_once(self):
+        nv, h, reasons = self.nvml
+        self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+        self.mask |= int(reasons(h))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._poll_once()
+            except Exception:
+                return
+            time.sleep(self.period)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        if self.t is not None:
+            self._stop.set()
+            self.t.join(timeout=2)
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+                self._poll_once()
+            except Exception:
+                pass
 
     def summary(self):
-        sm, smax, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                smax = max(smax, float(parts[1]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[4:8]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        if not self.sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+        names = sorted(n for bit, n in self.REASONS.items() if self.mask & bit)
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.smax, "reasons": names,
+                "samples": len(self.sm), "source": "nvml"}
 
 
 # ---------------------------------------------------------------------------
@@ -310,8 +334,45 @@ def main():
         del graphs, outs
         torch.cuda.synchronize(dev)
 
-    # end-to-end through the public API: pinned host input -> device -> layer -> host
+    # dominant kernel: the gate/up engine, timed live with CUDA events around
+    # its own launch (the layer issued as its three phases, eager, same stream)
     T = args.tokens if args.tokens in results else max(results)
+    xk = [torch.randn(T, H, generator=torch.Generator(dev).manual_seed(T * 10 + i), device=dev).to(torch.bfloat16)
+          for i in range(n_layers)]
+    stream = torch.cuda.current_stream(dev)
+    evs = []
+
+    def mark(phase):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        evs[-1].append(ev)
+
+    with torch.no_grad():
+        for i in range(args.warmup):
+            layers[i % n_layers].forward_phases(xk[i % n_layers])
+        torch.cuda.synchronize(dev)
+        # hold the stream with a device-side sleep while the host queues every
+        # timed launch, so the kernels run back to back and the events bracket
+        # device time only (not host launch gaps)
+        torch.cuda._sleep(int(2e8))
+        for i in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            evs.append([e0])
+            layers[i % n_layers].forward_phases(xk[i % n_layers], between=mark)
+            e3 = torch.cuda.Event(enable_timing=True)
+            e3.record(stream)
+            evs[-1].append(e3)
+        torch.cuda.synchronize(dev)
+    prep_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    gu_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    down_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    gu_ms = max_over_ranks(gu_ms)
+    touched_t = results[T]["touched_experts"]
+    gu_bytes = touched_t * 2 * F * (H // 2 + 2 * (H // 128)) + T * H * 2
+    kernel_times = {"prep_ms": prep_ms, "gateup_ms": gu_ms, "down_ms": down_ms}
+
+    # end-to-end through the public API: pinned host input -> device -> layer -> host
     x_host = [torch.randn(T, H, generator=torch.Generator().manual_seed(5 + i)).to(torch.bfloat16).pin_memory()
               for i in range(n_layers)]
     x_dev = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
@@ -349,9 +410,11 @@ def main():
                        "group_size": 128, "layers_rotated": n_layers, "l2": "weights per step > L2 (126 MB), "
                        f"{n_layers} distinct layers rotated", "cuda_graph": True,
                        "parallelism": "replicas" if world > 1 else "single"},
-            "roofline": {"bound": "hbm", "achieved": hr["gbs"], "peak": hbm_peak, "unit": "GB/s",
-                         "frac": hr["frac"], "traffic": None, "kernel": "moe layer pass (route+gateup+down)",
-                         "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm", "achieved": gu_bytes / (gu_ms * 1e-3) / 1e9, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": gu_bytes / (gu_ms * 1e-3) / 1e9 / hbm_peak,
+                         "traffic": GATEUP_TRAFFIC.get(T), "kernel": "tc_engine_kernel gate/up (dominant)",
+                         "algo_bytes_per_launch": gu_bytes, "launch_ms": gu_ms, "peak_kind": peak_kind,
+                         "layer": {"achieved": hr["gbs"], "frac": hr["frac"], **kernel_times}},
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e_ms},
             "gpu_launches": 3 * args.steps,

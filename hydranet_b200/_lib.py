@@ -56,6 +56,9 @@ SIGNATURES = {
     "hn_moe_layer_int4": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, ctypes.POINTER(RouterParams),
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                   c_void_p]),
+    "hn_moe_layer_int4_phase": (c_int, [c_int, c_void_p, c_int, c_int64, c_int64, c_int64, c_int64,
+                                        ctypes.POINTER(RouterParams), c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hn_moe_experts_int4": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p,
                                     c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hn_moe_route": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, ctypes.POINTER(RouterParams), c_void_p,

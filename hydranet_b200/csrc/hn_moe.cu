@@ -1295,6 +1295,7 @@ struct MoECall {
   size_t ws_bytes;
   cudaStream_t stream;
   bool run_experts;
+  int phase;  // 0: all; 1: prep only; 2: gate/up engine only; 3: down engine only
 };
 
 template <typename Tr>
@@ -1336,8 +1337,9 @@ static int run_moe(const MoECall& m) {
   ra.out_logits = m.out_logits;
   ra.seg = seg_tokens(nt);
   ra.plan = plan;
-  int rc = launch_route<Tr>(ra, m.stream);
-  if (rc || !m.run_experts) return rc;
+  int rc = HN_OK;
+  if (m.phase == 0 || m.phase == 1) rc = launch_route<Tr>(ra, m.stream);
+  if (rc || !m.run_experts || m.phase == 1) return rc;
 
   EngineArgs e1{};
   e1.shm = ShiftMul{1u << 31, 1u << 24, 1u << 23};
@@ -1368,8 +1370,8 @@ static int run_moe(const MoECall& m) {
   e1.tile_ctr = plan.ctr1;
   e1.err = plan.err;
   e1.P = P;
-  rc = launch_engine<Tr, KIND_GATEUP, EPI_COMBINE>(nt, e1, m.stream);
-  if (rc) return rc;
+  if (m.phase == 0 || m.phase == 2) rc = launch_engine<Tr, KIND_GATEUP, EPI_COMBINE>(nt, e1, m.stream);
+  if (rc || m.phase == 2) return rc;
 
   EngineArgs e2 = e1;
   e2.K = (int)m.F;
@@ -1429,10 +1431,32 @@ size_t hn_int4_linear_workspace_size(int64_t M, int64_t N, int64_t K) {
   return make_layout(M, K, 1, 1, 0, N, nt, grid_p(nt), false).total() + 256;
 }
 
+static int moe_layer_call(int phase, const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
+                          const hn_router_params* router, const hn_expert_ptrs* experts, const void* expert_maps,
+                          void* out, int32_t* topk_idx, float* topk_w, float* logits, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
                       const hn_router_params* router, const hn_expert_ptrs* experts, const void* expert_maps,
                       void* out, int32_t* topk_idx,
                       float* topk_w, float* logits, void* workspace, size_t workspace_bytes, void* stream) {
+  return moe_layer_call(0, x, dtype, T, H, F, E, router, experts, expert_maps, out, topk_idx, topk_w, logits,
+                        workspace, workspace_bytes, stream);
+}
+
+int hn_moe_layer_int4_phase(int phase, const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
+                            const hn_router_params* router, const hn_expert_ptrs* experts, const void* expert_maps,
+                            void* out, int32_t* topk_idx, float* topk_w, float* logits, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  HN_REQUIRE(phase >= 1 && phase <= 3, "hn_moe_layer_int4_phase: phase must be 1, 2 or 3");
+  return moe_layer_call(phase, x, dtype, T, H, F, E, router, experts, expert_maps, out, topk_idx, topk_w, logits,
+                        workspace, workspace_bytes, stream);
+}
+
+static int moe_layer_call(int phase, const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
+                          const hn_router_params* router, const hn_expert_ptrs* experts, const void* expert_maps,
+                          void* out, int32_t* topk_idx, float* topk_w, float* logits, void* workspace,
+                          size_t workspace_bytes, void* stream) {
   int rc = check_dims(T, H, F, E);
   if (rc) return rc;
   rc = check_router(router, E);
@@ -1449,6 +1473,7 @@ int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F,
   m.E = E;
   m.topk = router->top_k;
   m.route_mode = ROUTE_COMPUTE;
+  m.phase = phase;
   m.router = router;
   m.table = experts;
   m.maps = static_cast<const ExpertMaps*>(expert_maps);

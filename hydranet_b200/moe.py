@@ -59,6 +59,19 @@ class MoELayerInt4(nn.Module):
         return out
 
 
+    def forward_phases(self, hidden_states: torch.Tensor, between=None, top_k: Optional[int] = None):
+        """Same result as ``forward``, issued as the three separate launches
+        (routing/staging/plan, gate+up, down+combine); ``between(phase)`` runs
+        after phases 1 and 2 (timing events, overlapping communication)."""
+        shape = hidden_states.shape
+        x = hidden_states.reshape(-1, shape[-1]).contiguous()
+        params, bonus = self._params(x, top_k)
+        out = ops.moe_layer_phases(x, params, self.experts.device_table, self.experts.device_maps,
+                                   self.num_experts, self.experts.intermediate_dim, between=between)
+        del bonus
+        return out.view(shape)
+
+
 def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts: ExpertTable) -> torch.Tensor:
     """Experts + weighted combine for externally routed tokens (x [T, H])."""
     return ops.moe_experts(x, topk_idx, topk_w, experts.device_table, experts.device_maps, len(experts),

@@ -177,6 +177,29 @@ def moe_layer(x: torch.Tensor, params: _lib.RouterParams, expert_table: torch.Te
     return out, idx, w, logits
 
 
+def moe_layer_phases(x: torch.Tensor, params: _lib.RouterParams, expert_table: torch.Tensor,
+                     expert_maps: torch.Tensor, num_experts: int, ffn: int, between=None):
+    """``moe_layer`` as its three launches (prep, gate/up, down+combine) on the
+    current stream.  ``between(phase)``, if given, is called after each of the
+    first two launches (to record events or issue other work); the result is
+    identical to ``moe_layer``."""
+    T, H = x.shape
+    k = params.top_k
+    out = torch.empty_like(x)
+    lib = load()
+    need = lib.hn_moe_workspace_size(T, H, ffn, num_experts, k)
+    ws = _lib.workspaces.get(need, x.device)
+    with torch.cuda.device(x.device):
+        for phase in (1, 2, 3):
+            check(lib.hn_moe_layer_int4_phase(phase, ptr(x), _act_dtype(x), T, H, ffn, num_experts,
+                                              ctypes.byref(params), expert_table.data_ptr(),
+                                              expert_maps.data_ptr(), ptr(out), None, None, None, ptr(ws),
+                                              ws.numel(), stream_ptr(x.device)))
+            if between is not None and phase < 3:
+                between(phase)
+    return out
+
+
 def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, expert_table: torch.Tensor,
                 expert_maps: torch.Tensor, num_experts: int, ffn: int) -> torch.Tensor:
     """Experts + combine with caller-supplied routing (int32 idx, float32 weights)."""

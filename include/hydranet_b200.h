@@ -170,6 +170,19 @@ HN_API int hn_moe_layer_int4(const void* x, int dtype, int64_t T, int64_t H, int
                       void* out, int32_t* topk_idx, float* topk_w, float* logits,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* hn_moe_layer_int4 split into its three launches, for callers that put
+ * work between them (communication of an expert-parallel layer) or time them
+ * separately: phase 1 = routing, activation staging and the dispatch plan;
+ * 2 = gate/up projections with SiLU(gate)*up; 3 = down projection and the
+ * weighted combine into out.  The state between phases lives in the
+ * workspace: issuing phases 1, 2, 3 in order on one stream with identical
+ * arguments computes exactly what one hn_moe_layer_int4 call computes.
+ * No counterpart in the reference (its layer is a Python loop). */
+HN_API int hn_moe_layer_int4_phase(int phase, const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
+                                   const hn_router_params* router, const hn_expert_ptrs* experts,
+                                   const void* expert_maps, void* out, int32_t* topk_idx, float* topk_w,
+                                   float* logits, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Same as hn_moe_layer_int4 but with routing supplied by the caller
  * (topk_idx int32 [T, k], topk_w float32 [T, k]); used for expert-parallel
  * shards and for callers that route on their own. */

@@ -189,3 +189,20 @@ def test_cuda_graph_capture(lib):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(y, ref)
+
+
+def test_phase_split_equals_one_call(lib):
+    """hn_moe_layer_int4_phase 1, 2, 3 in order == one hn_moe_layer_int4 call, bit for bit."""
+    shape = synth.MoEShape(1024, 768, 8, 2)
+    table, _ = host_moe(shape, 61)
+    rw = torch.randn(8, 1024, generator=torch.Generator("cuda").manual_seed(3), device="cuda") * 0.02
+    layer = mixtral_layer(table, rw.to(torch.bfloat16), 2)
+    x = torch.randn(24, 1024, generator=torch.Generator("cuda").manual_seed(4), device="cuda").to(torch.bfloat16)
+    seen = []
+    a = layer(x)
+    b = layer.forward_phases(x, between=seen.append)
+    assert seen == [1, 2]
+    assert torch.equal(a, b)
+    with pytest.raises(_lib.HydraNetError):
+        _lib.check(_lib.load().hn_moe_layer_int4_phase(4, None, 2, 1, 1024, 768, 8, None, None, None, None, None,
+                                                       None, None, None, 0, None))
