@@ -21,8 +21,10 @@ decode tokens.  T is swept over 1/8/32/64; the headline line is T=64.
 the reference itself is Python + Triton and is not installed on the GPU box)
 on the same config and prints the same JSON line with ``"impl": "reference"``.
 
-With ``--gpus N`` (under torchrun) every rank runs its own replica of the
-layer (weak scaling, no data-path collective); the time is the max over ranks.
+With ``--gpus N`` (under torchrun) the layer runs expert-parallel: each rank
+owns E/N experts and T tokens of its own (weak scaling), routes them, sends
+token rows to the experts' owners and gets the weighted rows back with NCCL
+all-to-alls (``hydranet_b200/ep.py``); the time is the max over ranks.
 """
 
 from __future__ import annotations
@@ -262,8 +264,12 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     _lib.load()
 
-    shape = synth.MoEShape(H, F, E, TOPK)
+    ep = world > 1
+    local_e = E // world if ep else E
+    shape = synth.MoEShape(H, F, local_e, TOPK)
     sweep = tuple(int(t) for t in args.sweep.split(","))
+    if ep:
+        sweep = (args.tokens,)  # expert-parallel runs time the headline batch only
     n_layers = max(1, args.layers)
     layers = []
     for li in range(n_layers):
@@ -272,7 +278,12 @@ def main():
         with torch.no_grad():
             r.gate.weight.copy_(torch.randn(E, H, generator=torch.Generator(dev).manual_seed(77 + li),
                                             device=dev) * 0.02)
-        layers.append(MoELayerInt4(r, table).eval())
+        if ep:
+            # experts sharded over the ranks: E/N per GPU, NCCL all-to-all dispatch and combine
+            from hydranet_b200.ep import ExpertParallelMoE
+            layers.append(ExpertParallelMoE(r, table, E).eval())
+        else:
+            layers.append(MoELayerInt4(r, table).eval())
     torch.cuda.synchronize()
     hbm_peak, _, peak_kind = peaks()
 
@@ -295,9 +306,37 @@ def main():
         touched = []
         with torch.no_grad():
             for li, layer in enumerate(layers):
-                _, ro = layer(xs[li], return_routing=True)
-                touched.append(int(torch.unique(ro.expert_indices).numel()))
+                idx = layer.router(xs[li].view(1, T, H)).expert_indices.reshape(-1)
+                if ep:
+                    # experts of THIS rank touched by any rank's tokens
+                    allidx = [torch.empty_like(idx) for _ in range(world)]
+                    dist.all_gather(allidx, idx)
+                    idx = torch.cat(allidx)
+                    idx = idx[(idx >= rank * local_e) & (idx < (rank + 1) * local_e)]
+                touched.append(int(torch.unique(idx).numel()))
         algo_bytes = statistics.mean(touched) * blob_bytes(H, F) + 2 * T * H * 2 + E * H * 2
+        if ep:
+            # eager steps (the exchange sizes its all-to-all splits on the host)
+            with torch.no_grad():
+                for i in range(args.warmup):
+                    layers[i % n_layers](xs[i % n_layers])
+                torch.cuda.synchronize(dev)
+                barrier()
+                torch.cuda.synchronize(dev)
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with ClockSampler(local) as clk:
+                    ev0.record()
+                    for i in range(args.steps):
+                        layers[i % n_layers](xs[i % n_layers])
+                    ev1.record()
+                    torch.cuda.synchronize(dev)
+            ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+            barrier()
+            results[T] = {"ms_per_step": ms, "tok_s": world * T / (ms * 1e-3),
+                          "touched_experts": statistics.mean(touched), "algo_bytes": algo_bytes,
+                          "gbs": algo_bytes / (ms * 1e-3) / 1e9, "clocks": clk.summary()}
+            results[T]["frac"] = results[T]["gbs"] / hbm_peak
+            continue
         # capture one graph per layer (warm up on a side stream first)
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
@@ -337,10 +376,13 @@ def main():
     # dominant kernel: the gate/up engine, timed live with CUDA events around
     # its own launch (the layer issued as its three phases, eager, same stream)
     T = args.tokens if args.tokens in results else max(results)
+    kernel_times, gu_ms, gu_bytes = {}, None, None
     xk = [torch.randn(T, H, generator=torch.Generator(dev).manual_seed(T * 10 + i), device=dev).to(torch.bfloat16)
           for i in range(n_layers)]
     stream = torch.cuda.current_stream(dev)
     evs = []
+    if ep:
+        xk = []
 
     def mark(phase):
         ev = torch.cuda.Event(enable_timing=True)
@@ -348,14 +390,15 @@ def main():
         evs[-1].append(ev)
 
     with torch.no_grad():
-        for i in range(args.warmup):
+        for i in range(args.warmup if not ep else 0):
             layers[i % n_layers].forward_phases(xk[i % n_layers])
         torch.cuda.synchronize(dev)
         # hold the stream with a device-side sleep while the host queues every
         # timed launch, so the kernels run back to back and the events bracket
         # device time only (not host launch gaps)
-        torch.cuda._sleep(int(2e8))
-        for i in range(args.steps):
+        if not ep:
+            torch.cuda._sleep(int(2e8))
+        for i in range(args.steps if not ep else 0):
             e0 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             evs.append([e0])
@@ -364,13 +407,13 @@ def main():
             e3.record(stream)
             evs[-1].append(e3)
         torch.cuda.synchronize(dev)
-    prep_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    gu_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-    down_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
-    gu_ms = max_over_ranks(gu_ms)
-    touched_t = results[T]["touched_experts"]
-    gu_bytes = touched_t * 2 * F * (H // 2 + 2 * (H // 128)) + T * H * 2
-    kernel_times = {"prep_ms": prep_ms, "gateup_ms": gu_ms, "down_ms": down_ms}
+    if not ep:
+        prep_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+        gu_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+        down_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+        touched_t = results[T]["touched_experts"]
+        gu_bytes = touched_t * 2 * F * (H // 2 + 2 * (H // 128)) + T * H * 2
+        kernel_times = {"prep_ms": prep_ms, "gateup_ms": gu_ms, "down_ms": down_ms}
 
     # end-to-end through the public API: pinned host input -> device -> layer -> host
     x_host = [torch.randn(T, H, generator=torch.Generator().manual_seed(5 + i)).to(torch.bfloat16).pin_memory()
@@ -409,15 +452,18 @@ def main():
             "config": {"workload": WORKLOAD, "tokens": T, "hidden": H, "ffn": F, "experts": E, "top_k": TOPK,
                        "group_size": 128, "layers_rotated": n_layers, "l2": "weights per step > L2 (126 MB), "
                        f"{n_layers} distinct layers rotated", "cuda_graph": True,
-                       "parallelism": "replicas" if world > 1 else "single"},
-            "roofline": {"bound": "hbm", "achieved": gu_bytes / (gu_ms * 1e-3) / 1e9, "peak": hbm_peak,
-                         "unit": "GB/s", "frac": gu_bytes / (gu_ms * 1e-3) / 1e9 / hbm_peak,
-                         "traffic": GATEUP_TRAFFIC.get(T), "kernel": "tc_engine_kernel gate/up (dominant)",
-                         "algo_bytes_per_launch": gu_bytes, "launch_ms": gu_ms, "peak_kind": peak_kind,
-                         "layer": {"achieved": hr["gbs"], "frac": hr["frac"], **kernel_times}},
+                       "parallelism": f"ep{world} (experts sharded, NCCL all-to-all)" if ep else "single"},
+            "roofline": ({"bound": "hbm", "achieved": gu_bytes / (gu_ms * 1e-3) / 1e9, "peak": hbm_peak,
+                          "unit": "GB/s", "frac": gu_bytes / (gu_ms * 1e-3) / 1e9 / hbm_peak,
+                          "traffic": GATEUP_TRAFFIC.get(T), "kernel": "tc_engine_kernel gate/up (dominant)",
+                          "algo_bytes_per_launch": gu_bytes, "launch_ms": gu_ms, "peak_kind": peak_kind,
+                          "layer": {"achieved": hr["gbs"], "frac": hr["frac"], **kernel_times}} if not ep else
+                         {"bound": "hbm", "achieved": hr["gbs"], "peak": hbm_peak, "unit": "GB/s",
+                          "frac": hr["frac"], "traffic": None, "peak_kind": peak_kind,
+                          "kernel": "expert-parallel layer step per rank (route, all-to-all, experts, all-to-all)"}),
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e_ms},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": (3 if not ep else 5) * args.steps,
             "clocks": hr["clocks"],
             "cpu_baseline": cpu,
             "sweep": {str(t): {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items() if k != "clocks"}

@@ -7,7 +7,8 @@ this package holds the host-side mirror of the reference's interfaces:
   and ``kernels/expert_mlp.py`` drop-ins;
 * ``hydranet_b200.router``   -- ``TopKRouter`` / ``GLM4SigmoidRouter``;
 * ``hydranet_b200.moe``      -- one-launch-per-phase grouped MoE layer;
-* ``hydranet_b200.packing``  -- the packed expert format on the GPU.
+* ``hydranet_b200.packing``  -- the packed expert format on the GPU;
+* ``hydranet_b200.ep``       -- expert parallelism over NCCL all-to-all.
 
 There is no CPU fallback: ops raise if the CUDA library is missing.
 """

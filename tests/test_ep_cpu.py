@@ -1,0 +1,103 @@
+"""Expert-parallel dispatch/combine bookkeeping on CPU ranks (gloo, world size 2).
+
+Each rank routes its own tokens with the oracle router, exchanges rows with
+``hydranet_b200.ep.ep_moe_forward`` and runs its share of the experts with a
+test-only local function built from the oracle; the result must equal the
+single-process oracle layer (``model/mixtral.py:282-370`` semantics) on that
+rank's tokens.  No GPU is involved.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from hydranet_b200 import synth
+from oracle import int4_ref as R
+
+H, F, E, K = 256, 256, 8, 3
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def experts_oracle():
+    shape = synth.MoEShape(H, F, E, K)
+    out = {}
+    for e in range(E):
+        g, u, d = synth.host_expert_weights(7, shape, e)
+        out[e] = R.DequantExpert.from_packed(*R.quantize_tensor(g), *R.quantize_tensor(u), *R.quantize_tensor(d))
+    return out
+
+
+def worker(rank, world, port, T, force_idx, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from hydranet_b200.ep import ep_moe_forward, expert_range
+        experts = experts_oracle()
+        first, last = expert_range(E, rank, world)
+        x = synth.host_activations(100 + rank, T, H)
+        rw = synth.host_normal(5, (E, H), 0.02)
+        idx, w, _ = R.softmax_topk_router_ref(x, rw, K, "f32")
+        if force_idx is not None:
+            idx = force_idx[rank].copy()
+        def local_fn(rows, local_e, weight):
+            rr = rows.numpy().astype(np.float32)
+            out = np.zeros_like(rr)
+            for i in range(rr.shape[0]):
+                e = first + int(local_e[i])
+                assert first <= e < last
+                out[i] = float(weight[i]) * experts[e](rr[i:i + 1])[0]
+            return torch.from_numpy(out)
+        y = ep_moe_forward(torch.from_numpy(x), torch.from_numpy(idx.astype(np.int64)), torch.from_numpy(w),
+                           E, local_fn)
+        ref = R.moe_combine_ref(x, idx, w, experts)
+        err = float(np.abs(y.numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
+        results[rank] = err
+    finally:
+        dist.destroy_process_group()
+
+
+def run(world, T, force_idx=None):
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = free_port()
+    procs = [ctx.Process(target=worker, args=(r, world, port, T, force_idx, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+    return [results[r] for r in range(world)]
+
+
+def test_ep_matches_single_process_oracle():
+    errs = run(2, 9)
+    assert max(errs) < 1e-5, errs
+
+
+def test_ep_uneven_and_empty_splits_and_duplicates():
+    # rank 0 sends everything to rank 1's experts (nothing to itself), picks an
+    # expert twice; rank 1 keeps everything local
+    f0 = np.array([[5, 5, 7], [6, 4, 5], [7, 7, 7]], dtype=np.int64)
+    f1 = np.array([[0, 1, 2], [3, 3, 0], [1, 2, 3]], dtype=np.int64)
+    errs = run(2, 3, force_idx={0: f0, 1: f1})
+    assert max(errs) < 1e-5, errs
+
+
+def test_expert_range_partition():
+    from hydranet_b200.ep import expert_range
+    assert [expert_range(128, r, 8) for r in range(8)][3] == (48, 64)
+    with pytest.raises(ValueError):
+        expert_range(10, 0, 4)
