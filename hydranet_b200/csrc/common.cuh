@@ -306,6 +306,43 @@ __device__ __forceinline__ void umma_group9(uint32_t d, uint32_t a, uint32_t b_l
       : "memory");
 }
 
+// Same k-group with the B operand in the K-major 128B-swizzle layout: k-step
+// s reads half s/4 of the tile (N rows of 128 B each) at byte 32*(s%4), i.e.
+// start = b_lo + (s/4)*8N + (s%4)*2 in 16-byte units.  The correction step has
+// its own descriptor (no swizzle) with high half c_hi.
+template <int N>
+__device__ __forceinline__ void umma_group9_sw128(uint32_t d, uint32_t a, uint32_t b_lo, uint32_t b_hi,
+                                                  uint32_t idesc, uint32_t c_lo, uint32_t c_hi, uint32_t a_corr,
+                                                  uint32_t idesc_c) {
+  asm volatile(
+      "{\n\t.reg .pred pf, pt, e;\n\t.reg .b64 bd;\n\t.reg .b32 al, bl;\n\t"
+      "setp.ne.b32 pf, %3, %3;\n\t"
+      "setp.eq.b32 pt, %3, %3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "mov.b64 bd, {%2, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, pf;\n\t"
+      "add.u32 al, %1, 8;\n\tadd.u32 bl, %2, 2;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, %2, 4;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, %2, 6;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, %2, %5;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, 2;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, 2;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "add.u32 al, al, 8;\n\tadd.u32 bl, bl, 2;\n\tmov.b64 bd, {bl, %3};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [al], bd, %4, pt;\n\t"
+      "mov.b64 bd, {%6, %7};\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], bd, %9, pt;\n\t}"
+      :
+      : "r"(d), "r"(a), "r"(b_lo), "r"(b_hi), "r"(idesc), "n"(8 * N), "r"(c_lo), "r"(c_hi), "r"(a_corr),
+        "r"(idesc_c)
+      : "memory");
+}
+
 // tcgen05.commit from one elected lane of a converged warp (the lane that
 // issued the MMAs through umma_group9's elect.sync: elect.sync picks the same
 // lane, the lowest active one, every time).

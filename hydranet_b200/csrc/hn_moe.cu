@@ -58,8 +58,8 @@ struct Plan {
   int* pos;      // [T*K] assignment index of (t, k)
   int* idx;      // [T*K] top-k expert ids
   float* wts;    // [T*K] top-k weights (rounded to the activation dtype)
-  uint8_t* xp;   // [K_in/128][T][kChunk]    staged activations
-  uint8_t* hp;   // [F/128][T*K][kChunk]     staged SiLU(gate)*up
+  uint8_t* xp;   // [T][K_in/128][kChunk]    staged activations (token-major)
+  uint8_t* hp;   // [T*K][F/128][kChunk]     staged SiLU(gate)*up (assignment-major)
   float* part1;  // stream-K partial tiles, phase 1
   float* part2;  // stream-K partial tiles, phase 2
   float* R;      // [T*K][H] weighted expert outputs (EPI_COMBINE)
@@ -218,14 +218,14 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
     uint4 packed;
     float cp;
     pack_unit<Tr>(v, packed, cp);
-    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk + 16 + ch * 16) = packed;
+    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)t * (a.H / 128) + g) * kChunk + 16 + ch * 16) = packed;
     cpart[u] = cp;
   }
   __syncthreads();
   for (int g = tid; g < a.H / 128; g += 256) {
     float c = 0.f;
     for (int u = 0; u < 16; ++u) c += cpart[g * 16 + u];
-    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)g * a.T + t) * kChunk) = correction_unit(c);
+    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)t * (a.H / 128) + g) * kChunk) = correction_unit(c);
   }
 
   // 2. routing for this token
@@ -485,11 +485,14 @@ struct EngineArgs {
   hn_expert_ptrs single;
   const ExpertMaps* maps;  // device array [E] of tensor maps, or NULL: use single_maps
   ExpertMaps single_maps;
-  const uint8_t* bsrc;
-  int64_t b_gstride;
+  const uint8_t* bsrc;  // staged tokens, [row][group][kChunk]
+  int64_t b_rstride;    // bytes per staged row (groups * kChunk)
+  int64_t b_rows;       // staged rows (KIND_DOWN tensor maps)
   int b_use_tok;
+  CUtensorMap bmap;     // KIND_DOWN: bsrc as uint8 [rows, b_rstride], 128 B x N boxes, 128B swizzle
+  CUtensorMap cmap;     // KIND_DOWN: same tensor, 16 B x N boxes (correction units), no swizzle
   uint8_t* hp;
-  int64_t hp_gstride;
+  int64_t hp_rstride;
   float* R;
   void* out;
   int64_t ldo;
@@ -518,20 +521,26 @@ struct TileMap {
 //   weight ring: ST stages of 32 KB = one 2-D TMA box pair (A0 rows, A1 rows)
 //     x 128 B (two 128-wide k-groups), 128B-swizzled: the 16-byte chunk c of
 //     row r sits at chunk c ^ (r & 7) of the row.
-//   token ring: SB stages of [17 units][N tokens][16 B]: unit 0 is the
-//     correction unit, unit 1 + c holds logical k [8c, 8c+8).  For MMA k-step
-//     s the K-major core matrices are units 1+2s and 2+2s: LBO (K direction)
-//     = 16*N bytes, SBO (8-token blocks) = 128 bytes.
+//   token ring: SB stages of [2 halves][N tokens][128 B], 128B-swizzled
+//     (the 16-byte unit u of token row r at u ^ (r & 7)): half h holds data
+//     units 8h..8h+7 (logical k 64h..64h+63) of the k-group; the K-major
+//     SW128 operand of MMA k-step s starts at half s/4, byte 32*(s%4), with
+//     SBO = 1024 bytes (8 token rows);
+//   correction ring: SB stages of [N tokens][16 B] correction units followed
+//     by N x 16 zero bytes (the second K half of the correction step);
 //   htile / cpart: epilogue staging.
 template <int N, int ST, int SB>
 struct TcSmem {
   static constexpr int kHdr = 1024;
   static constexpr int kWStage = 32768;
   static constexpr int kW = ST * kWStage;
-  static constexpr int kBStage = 17 * N * 16;
+  static constexpr int kBStage = 2 * N * 128;  // a multiple of 1024: stages stay swizzle-aligned
   static constexpr int kB = SB * kBStage;
+  static constexpr int kCStage = 2 * N * 16;
+  static constexpr int kC = SB * kCStage;
   static constexpr int kH = 128 * (N + 1) * 4 + N * 16 * 4;
-  static constexpr int kTotal = 1024 /* alignment slack */ + kHdr + kW + kB + kH;
+  static constexpr int kTotal = 1024 /* alignment slack */ + kHdr + kW + kB + kC + kH;
+  static_assert(kBStage % 1024 == 0, "token stages must stay 1024-byte aligned");
 };
 
 // TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as bf16/f16
@@ -641,7 +650,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   static_assert(LOOK >= 1 && SB - LOOK >= 4 && SA <= 4 && SD <= 4 && SB <= 16 && ST <= 8, "stage counts");
   constexpr uint32_t IDESC = umma_idesc<Tr, 128, N>();
   constexpr uint32_t IDESC_CORR = umma_idesc<BF16, 128, N>();
-  constexpr uint32_t kDescHi = (128u >> 4) | (1u << 14);  // SBO = 128 B, descriptor version 1 (bit 46)
+  constexpr uint32_t kDescHiSW128 = (1024u >> 4) | (1u << 14) | (2u << 29);  // SBO 1024 B, version 1, SWIZZLE_128B
+  constexpr uint32_t kDescHiCorr = (128u >> 4) | (1u << 14);                 // SBO 128 B, version 1, no swizzle
   constexpr int kFoldThreads = kFoldWarps * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -658,7 +668,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   int* bcast = reinterpret_cast<int*>(bars + 73);
   uint8_t* wst = smem + L::kHdr;
   uint8_t* bst = wst + L::kW;
-  float* htile = reinterpret_cast<float*>(bst + L::kB);
+  uint8_t* cst = bst + L::kB;
+  float* htile = reinterpret_cast<float*>(cst + L::kC);
   float* cpart = htile + 128 * (N + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -687,7 +698,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       mbar_init(smem_u32(&d_empty[s]), kFoldWarps);
     }
     for (int s = 0; s < SB; ++s) {
-      mbar_init(smem_u32(&b_full[s]), 32);
+      // KIND_DOWN fills a stage with TMA (one arrival + bytes), KIND_GATEUP
+      // with per-lane cp.async (one arrival per lane)
+      mbar_init(smem_u32(&b_full[s]), KIND == KIND_DOWN ? 1 : 32);
       mbar_init(smem_u32(&b_empty[s]), 2);
     }
     for (int s = 0; s < ST; ++s) {
@@ -700,6 +713,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
+  // zero halves of the correction ring (read by the correction MMA, never written)
+  for (int i = threadIdx.x; i < SB * N; i += kTcThreads)
+    *reinterpret_cast<uint4*>(cst + (i / N) * L::kCStage + N * 16 + (i % N) * 16) = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -737,46 +754,83 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     // ------------------------- token producer -------------------------
     // Lane l copies the 17 units of token l of the segment; a stage is
     // signalled (after its copies landed and a proxy fence) LOOK stages later.
-    Ring<SB> rb, rs;  // rb: stage being filled; rs: next stage to signal (LOOK behind)
     int k = 0, tile = tile0, gp = gp0;
-    for (int i = 0; i < n_items; ++i) {
-      int seg, rt;
-      TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
-      const int4 sg = a.segs[seg];
-      const uint8_t* src_tok = nullptr;
-      if (lane < sg.z) {
-        const int row = a.b_use_tok ? a.a_tok[sg.y + lane] : sg.y + lane;
-        src_tok = a.bsrc + (int64_t)row * kChunk;
+    if (KIND == KIND_DOWN) {
+      // Rows of a segment are consecutive (assignment order): each k-group is
+      // three TMA boxes of N rows (two 128-byte data halves, 128B swizzle, and
+      // the correction units); rows past the end are zero-filled.
+      Ring<SB> rb;
+      if (lane == 0) {
+        for (int i = 0; i < n_items; ++i) {
+          int seg, rt;
+          TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+          const int row0 = a.segs[seg].y;
+          const int ng = min(2, a.G - 2 * gp);
+          for (int gi = 0; gi < ng; ++gi, ++k) {
+            const int grp = 2 * gp + gi;
+            mbar_wait(smem_u32(&b_empty[rb.idx]), rb.phase ^ 1u, a.err);
+            const uint32_t bar = smem_u32(&b_full[rb.idx]);
+            mbar_arrive_expect_tx(bar, (uint32_t)(2 * N * 128 + N * 16));
+            const uint32_t dst = smem_u32(bst + rb.idx * L::kBStage);
+            tma_load_2d(dst, &a.bmap, grp * kChunk + 16, row0, bar);
+            tma_load_2d(dst + N * 128, &a.bmap, grp * kChunk + 16 + 128, row0, bar);
+            tma_load_2d(smem_u32(cst + rb.idx * L::kCStage), &a.cmap, grp * kChunk, row0, bar);
+            rb.next();
+          }
+          if (++gp == GP) {
+            gp = 0;
+            ++tile;
+          }
+        }
       }
-      const int ng = min(2, a.G - 2 * gp);
-      for (int gi = 0; gi < ng; ++gi, ++k) {
-        const int grp = 2 * gp + gi;
-        mbar_wait(smem_u32(&b_empty[rb.idx]), rb.phase ^ 1u, a.err);
-        if (src_tok) {
-          const uint32_t dst = smem_u32(bst + rb.idx * L::kBStage + 16 * lane);
-          const uint8_t* src = src_tok + (int64_t)grp * a.b_gstride;
+      __syncwarp();
+    } else {
+      // Gathered tokens: lane l copies token l of the segment with cp.async
+      // into the swizzled rows; a stage is signalled (after its copies landed
+      // and a proxy fence) LOOK groups later.
+      Ring<SB> rb, rs;  // rb: stage being filled; rs: next stage to signal (LOOK behind)
+      for (int i = 0; i < n_items; ++i) {
+        int seg, rt;
+        TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+        const int4 sg = a.segs[seg];
+        const uint8_t* src_tok = nullptr;
+        if (lane < sg.z) {
+          const int row = a.b_use_tok ? a.a_tok[sg.y + lane] : sg.y + lane;
+          src_tok = a.bsrc + (int64_t)row * a.b_rstride;
+        }
+        const int ng = min(2, a.G - 2 * gp);
+        for (int gi = 0; gi < ng; ++gi, ++k) {
+          const int grp = 2 * gp + gi;
+          mbar_wait(smem_u32(&b_empty[rb.idx]), rb.phase ^ 1u, a.err);
+          if (src_tok) {
+            const uint32_t dst = smem_u32(bst + rb.idx * L::kBStage + lane * 128);
+            const uint8_t* src = src_tok + (int64_t)grp * kChunk;
+            const int sw = lane & 7;
 #pragma unroll
-          for (int ch = 0; ch < 17; ++ch) cp_async16(dst + 16 * N * ch, src + ch * 16);
+            for (int u = 0; u < 16; ++u)
+              cp_async16(dst + (u >> 3) * (N * 128) + (((u & 7) ^ sw) << 4), src + 16 + u * 16);
+            cp_async16(smem_u32(cst + rb.idx * L::kCStage + lane * 16), src);
+          }
+          cp_async_commit();
+          rb.next();
+          if (k >= LOOK) {
+            cp_async_wait<LOOK>();
+            fence_proxy_async_smem();  // generic-proxy writes -> read by the tensor core (async proxy)
+            mbar_arrive(smem_u32(&b_full[rs.idx]));
+            rs.next();
+          }
         }
-        cp_async_commit();
-        rb.next();
-        if (k >= LOOK) {
-          cp_async_wait<LOOK>();
-          fence_proxy_async_smem();  // generic-proxy writes -> read by the tensor core (async proxy)
-          mbar_arrive(smem_u32(&b_full[rs.idx]));
-          rs.next();
+        if (++gp == GP) {
+          gp = 0;
+          ++tile;
         }
       }
-      if (++gp == GP) {
-        gp = 0;
-        ++tile;
+      cp_async_wait<0>();
+      fence_proxy_async_smem();
+      for (int r = 0; r < min(k, LOOK); ++r) {
+        mbar_arrive(smem_u32(&b_full[rs.idx]));
+        rs.next();
       }
-    }
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    for (int r = 0; r < min(k, LOOK); ++r) {
-      mbar_arrive(smem_u32(&b_full[rs.idx]));
-      rs.next();
     }
   } else if (warp == kMmaWarp0 || warp == kMmaWarp1) {
     // ------------------------------ MMA issuers ------------------------------
@@ -795,11 +849,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         mbar_wait(smem_u32(&d_empty[sd]), rd.phase ^ 1u, a.err);
         mbar_wait(smem_u32(&a_full[2 * sa + mj]), ra.phase, a.err);
         tc_fence_after();
-        // B descriptors: low half = start address >> 4 | (LBO >> 4) << 16,
-        // high half = SBO >> 4 | version bit; step s starts at unit 1 + 2s.
-        const uint32_t c_lo = ((smem_u32(bst + sb * L::kBStage) >> 4) & 0x3FFFu) | (uint32_t)(N << 16);
-        umma_group9<2 * N>(tbase + D0 + sd * 2 * N + mj * N, tbase + sa * 128 + mj * 64, c_lo + N, kDescHi, IDESC,
-                           c_lo, tbase + CORR, IDESC_CORR);
+        // B descriptors (32-bit halves): data = K-major SW128 tile (start,
+        // LBO ignored = 1, SBO 1024 B, layout SWIZZLE_128B); correction = K-major
+        // no-swizzle tile (LBO = N*16 B to the zero half, SBO 128 B).
+        const uint32_t b_lo = ((smem_u32(bst + sb * L::kBStage) >> 4) & 0x3FFFu) | (1u << 16);
+        const uint32_t c_lo = ((smem_u32(cst + sb * L::kCStage) >> 4) & 0x3FFFu) | (uint32_t)(N << 16);
+        umma_group9_sw128<N>(tbase + D0 + sd * 2 * N + mj * N, tbase + sa * 128 + mj * 64, b_lo, kDescHiSW128,
+                             IDESC, c_lo, kDescHiCorr, tbase + CORR, IDESC_CORR);
         umma_commit_elect(smem_u32(&a_empty[2 * sa + mj]));
         umma_commit_elect(smem_u32(&b_empty[sb]));
         umma_commit_elect(smem_u32(&d_full[sd]));
@@ -986,7 +1042,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
               }
             }
             named_bar_sync(1, kFoldThreads);
-            uint8_t* dstp = a.hp + (int64_t)cv.rt * a.hp_gstride;
+            uint8_t* dstp = a.hp + (int64_t)cv.rt * kChunk;  // group rt of each staged row
             for (int task = ft; task < m * 16; task += kFoldThreads) {
               const int tok = task >> 4, ch = task & 15;
               float v[8];
@@ -995,14 +1051,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
               uint4 pk;
               float cp;
               pack_unit<Tr>(v, pk, cp);
-              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + tok) * kChunk + 16 + ch * 16) = pk;
+              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + tok) * a.hp_rstride + 16 + ch * 16) = pk;
               cpart[tok * 16 + ch] = cp;
             }
             named_bar_sync(1, kFoldThreads);
             if (ft < m) {
               float cs = 0.f;
               for (int u = 0; u < 16; ++u) cs += cpart[ft * 16 + u];
-              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + ft) * kChunk) = correction_unit(cs);
+              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + ft) * a.hp_rstride) = correction_unit(cs);
             }
             named_bar_sync(1, kFoldThreads);
           } else {
@@ -1074,6 +1130,9 @@ struct TcTune {
   static constexpr int ST = (N == 16) ? 5 : 4, SB = 8;
 };
 
+static int encode_token_maps(CUtensorMap* data, CUtensorMap* corr, const void* base, int64_t rows,
+                             int64_t row_bytes, int box_rows);
+
 template <typename Tr, int N, int KIND, int EPI>
 static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
   using TU = TcTune<N>;
@@ -1081,6 +1140,11 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
   static_assert(2 * L::kTotal > 228 * 1024, "one engine CTA per SM: it allocates all 512 TMEM columns");
   static_assert(L::kTotal <= 227 * 1024, "engine shared memory exceeds the per-CTA limit");
   auto kern = tc_engine_kernel<Tr, N, KIND, EPI, TU::ST, TU::SB>;
+  EngineArgs e = a;
+  if (KIND == KIND_DOWN) {
+    const int rc = encode_token_maps(&e.bmap, &e.cmap, e.bsrc, e.b_rows, e.b_rstride, N);
+    if (rc) return rc;
+  }
   static bool attr_set[64] = {};  // per instantiation and device
   int dev = 0;
   HN_CUDA(cudaGetDevice(&dev));
@@ -1088,7 +1152,7 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
     HN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  kern<<<a.P, kTcThreads, L::kTotal, s>>>(a);
+  kern<<<e.P, kTcThreads, L::kTotal, s>>>(e);
   HN_CUDA(cudaGetLastError());
   return HN_OK;
 }
@@ -1263,6 +1327,31 @@ static int encode_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64
   return HN_OK;
 }
 
+// Staged token rows (uint8 [rows, row_bytes]) for the down-phase token ring:
+// data halves as 128 B x box_rows boxes with 128B swizzle, correction units as
+// 16 B x box_rows boxes without swizzle.
+static int encode_token_maps(CUtensorMap* data, CUtensorMap* corr, const void* base, int64_t rows,
+                             int64_t row_bytes, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(HN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (no CUDA driver)");
+  HN_REQUIRE(base && ((uintptr_t)base & 255) == 0 && row_bytes % 16 == 0 && rows >= 1,
+             "staged token rows must be 256-byte aligned with 16-byte multiple rows");
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t es[2] = {1u, 1u};
+  cuuint32_t box_d[2] = {128u, (cuuint32_t)box_rows};
+  CUresult r = fn(data, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box_d, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HN_ERR_CUDA, "cuTensorMapEncodeTiled (tokens) failed: " + std::to_string((int)r));
+  cuuint32_t box_c[2] = {16u, (cuuint32_t)box_rows};
+  r = fn(corr, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box_c, es,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HN_ERR_CUDA, "cuTensorMapEncodeTiled (corrections) failed: " + std::to_string((int)r));
+  return HN_OK;
+}
+
 static int encode_expert_maps(ExpertMaps* out, const hn_expert_ptrs& p, int64_t H, int64_t F) {
   memset(out, 0, sizeof(*out));
   int rc = HN_OK;
@@ -1362,10 +1451,10 @@ static int run_moe(const MoECall& m) {
     if (rc) return rc;
   }
   e1.bsrc = plan.xp;
-  e1.b_gstride = m.T * kChunk;
+  e1.b_rstride = (m.H / 128) * kChunk;
   e1.b_use_tok = 1;
   e1.hp = plan.hp;
-  e1.hp_gstride = TK * kChunk;
+  e1.hp_rstride = (m.F / 128) * kChunk;
   e1.part = plan.part1;
   e1.tile_ctr = plan.ctr1;
   e1.err = plan.err;
@@ -1379,8 +1468,9 @@ static int run_moe(const MoECall& m) {
   e2.N = (int)m.H;
   e2.n_rt = (int)((m.H + 255) / 256);
   e2.bsrc = plan.hp;
-  e2.b_gstride = TK * kChunk;
+  e2.b_rstride = (m.F / 128) * kChunk;
   e2.b_use_tok = 0;
+  e2.b_rows = TK;
   e2.R = plan.R;
   e2.out = m.out;
   e2.ldo = m.ldo;
@@ -1630,8 +1720,9 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
     if (mrc) return mrc;
   }
   e.bsrc = plan.xp;
-  e.b_gstride = M * kChunk;
+  e.b_rstride = (K / 128) * kChunk;
   e.b_use_tok = 1;
+  e.b_rows = M;
   e.out = out;
   e.ldo = ldo;
   e.part = plan.part2;
