@@ -2,33 +2,25 @@
 //
 //   route_prep_kernel   one CTA per token: router logits / top-k / weights
 //                       (or caller-given routing), the token's activations
-//                       staged into MMA-fragment order, and -- in the last CTA
-//                       to finish -- the dispatch plan (per-expert token lists
-//                       cut into segments of at most 8*NT tokens).
-//   engine_kernel       persistent grouped INT4 GEMV/GEMM over (weight-row
-//                       tile x segment) tiles, k-split "stream-K" style so every
-//                       CTA streams the same number of 128-wide k-groups.
+//                       staged as float16 in MMA operand order, and -- in the
+//                       last CTA to finish -- the dispatch plan (per-expert
+//                       token lists cut into segments of at most 8*nt tokens).
+//   tc_engine_kernel    persistent grouped INT4 GEMV/GEMM on the tcgen05 tensor
+//                       cores over (weight-row tile x segment) tiles, k-split
+//                       "stream-K" style so every CTA streams the same number
+//                       of 128-wide k-groups.
 //                       KIND_GATEUP: gate+up rows together, SiLU(gate)*up in
 //                       the epilogue, written as the next phase's operand.
 //                       KIND_DOWN: down projection; EPI_COMBINE scales by the
 //                       routing weight and sums the top-k choices per token,
 //                       EPI_STORE writes rows straight to the output.
 //
-// Weight tiles are streamed by per-thread cp.async into a per-warp ring; the
-// activation chunk of each k-group (shared by all warps) arrives by TMA bulk
-// copies issued by a producer warp and tracked by mbarriers.  The MMA is
-// mma.sync m16n8k16 with the WEIGHTS as the 16-row A operand and tokens as
-// the 8-column B operand.
-//
-// Dequantisation without subtraction: a nibble n OR-ed into the mantissa of
-// 2^e gives 2^e + n exactly (bf16: 128+n for a low nibble, 128+8n for a nibble
-// in bits 3..6; fp16: 1024+n / 1024+16n).  The B operand of odd k is
-// pre-divided by 8 (bf16) or 16 (fp16), so for every k the MMA computes
-// (n - 8 + c_k) * x_k with c_k = 136 / 24 (bf16) or 1032 / 72 (fp16).  The
-// constant part, C = sum_k c_k x_k per (token, group), is computed once when
-// the activations are staged and subtracted before the group scale is
-// applied: acc += scale[row, group] * (mma_partial - C).  Weights therefore
-// enter the MMA as the exact integers n - 8, and the scale multiplies in fp32.
+// Arithmetic follows the reference kernel (kernels/int4_expert_mlp.py:55-93):
+// weights are dequantised to float16 as (n - 8) * scale with one rounding,
+// activations enter as float16, and products accumulate in fp32.  The
+// dequantised tile is written to tensor memory and used as the A operand of
+// tcgen05.mma (M = 128 weight rows), the tokens are the B operand (N = 16 or
+// 32) in shared memory, and each piece of a tile accumulates in TMEM.
 #include <algorithm>
 #include <cstring>
 #include <string>
@@ -38,7 +30,7 @@
 
 namespace hn {
 
-constexpr int kChunk = 272;  // bytes per (token, k-group): 16 B correction unit + 16 units of 16 B
+constexpr int kChunk = 256;  // bytes per (token, k-group): 16 units of 16 B (128 float16)
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 32;
 constexpr int kPlanSmemEntries = 4096;  // routing entries the plan builder copies into shared memory
@@ -54,6 +46,7 @@ struct Plan {
   int* n_segs;   // [1]
   int4* segs;    // [max_segs] {expert, first assignment, tokens, 0}
   int* a_tok;    // [T*K] token of assignment p
+  int* a_tk;     // [T*K] t*K + slot of assignment p (inverse of pos)
   float* a_w;    // [T*K] routing weight of assignment p
   int* pos;      // [T*K] assignment index of (t, k)
   int* idx;      // [T*K] top-k expert ids
@@ -65,55 +58,33 @@ struct Plan {
   float* R;      // [T*K][H] weighted expert outputs (EPI_COMBINE)
   int* ctr1;     // per phase-1 tile arrival counters
   int* ctr2;     // per phase-2 tile arrival counters
-  int* rtctr;    // per output row-tile segment counters
+  int* rtctr;    // [row tiles][T] contributions summed into (row tile, token) so far
   int n_ctr;     // words from ctr1 to the end of the counter section (zeroed by the prep kernel)
 };
 
 __host__ __device__ constexpr int seg_tokens(int nt) { return 8 * nt; }
 
 // ---------------------------------------------------------------------------
-// Activation staging.  For k-group g and token t a 272-byte chunk holds the
-// correction unit followed by 16 data units of 16 bytes.
-// Data unit c (at byte 16 + 16c) covers x[128*g + 8*c + i], i = 0..7, packed
-// as bf16/f16 pairs
-//   { (x0, x4), (x2, x6), (x1*s, x5*s), (x3*s, x7*s) }   (s = odd-k scale)
-// i.e. logical k 8c..8c+7 of the MMA, matching the TMEM columns the weight
-// dequantiser writes for the same 8 nibbles (dequant_word).  A unit is one
-// 16-byte row of a K-major core matrix of the tensor-core B operand.
-// The correction unit (byte 0) holds C = sum_k c_k x_k of the group as three
-// bf16 values whose sum is exactly the fp32 C, then five bf16 zeros; the
-// engine multiplies it by a constant A column of -1s in the same MMA chain,
-// so the accumulator already holds sum_k (n_k - 8) x_k.
+// Activation staging.  For k-group g and token t a 256-byte chunk holds 16
+// units of 16 bytes; unit c covers x[128*g + 8*c + i], i = 0..7, as float16
+// pairs in the order
+//   { (x0, x4), (x2, x6), (x1, x5), (x3, x7) },
+// the order in which dequant_word_f16 produces the same 8 nibbles of a packed
+// 32-bit word, so TMEM column 4c + i of a dequantised weight row and 32-bit
+// word i of unit c hold the same two k.  A unit is one 16-byte row of a
+// K-major core matrix of the tensor-core B operand.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint4 correction_unit(float c) {
-  const __nv_bfloat16 h0 = __float2bfloat16_rn(c);
-  const float r1 = c - __bfloat162float(h0);  // exact
-  const __nv_bfloat16 h1 = __float2bfloat16_rn(r1);
-  const float r2 = r1 - __bfloat162float(h1);  // exact, at most 8 significant bits
-  const __nv_bfloat16 h2 = __float2bfloat16_rn(r2);
-  uint4 u;
-  u.x = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-  u.y = (uint32_t)__bfloat16_as_ushort(h2);
-  u.z = 0u;
-  u.w = 0u;
-  return u;
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  return (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
 }
-template <typename Tr>
-__device__ __forceinline__ void pack_unit(const float (&v)[8], uint4& out, float& cpart) {
-  const float s = Tr::kOddScale;
-  uint4 u;
-  u.x = Tr::pack(v[0], v[4]);
-  u.y = Tr::pack(v[2], v[6]);
-  u.z = Tr::pack(v[1] * s, v[5] * s);
-  u.w = Tr::pack(v[3] * s, v[7] * s);
-  // effective odd values are what the MMA actually sees (times 1/s, exact)
-  const typename Tr::T2* oz = reinterpret_cast<const typename Tr::T2*>(&u.z);
-  const typename Tr::T2* ow = reinterpret_cast<const typename Tr::T2*>(&u.w);
-  float2 fz = make_float2(Tr::to_f(oz->x), Tr::to_f(oz->y));
-  float2 fw = make_float2(Tr::to_f(ow->x), Tr::to_f(ow->y));
-  const float inv = 1.0f / s;
-  cpart = Tr::kCorrEven * (((v[0] + v[2]) + v[4]) + v[6]) + Tr::kCorrOdd * inv * (((fz.x + fw.x) + fz.y) + fw.y);
-  out = u;
+__device__ __forceinline__ uint4 pack_unit(const float (&v)[8]) {
+  return make_uint4(pack_h2(v[0], v[4]), pack_h2(v[2], v[6]), pack_h2(v[1], v[5]), pack_h2(v[3], v[7]));
+}
+// Byte offset of k (0..127) inside a staged chunk: unit k / 8, then the
+// position of i = k % 8 in the order above (i with its three bits reversed).
+__device__ __forceinline__ int staged_offset(int k) {
+  const int i = k & 7;
+  return (k >> 3) * 16 + (((i & 1) << 2) | (i & 2) | (i >> 2)) * 2;
 }
 
 
@@ -168,8 +139,7 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   extern __shared__ __align__(16) float rsm[];
   float* xs = rsm;                 // [H]
   float* lg = xs + a.H;            // [E]
-  float* cpart = lg + a.E;         // [H/8]
-  float* scs = cpart + a.H / 8;    // [E] selection scores
+  float* scs = lg + a.E;           // [E] selection scores
   // plan copies of the routing follow scs (see the plan section); the router
   // weight chunk sits at the end of the dynamic shared memory
   __shared__ int s_last;
@@ -207,25 +177,13 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   }
   __syncthreads();
 
-  // 1. staged activations + per-group correction C
-  const int units = a.H / 8;
-  for (int u = tid; u < units; u += 256) {
+  // 1. staged activations
+  for (int u = tid; u < a.H / 8; u += 256) {
     const int g = u >> 4, ch = u & 15;
-    const int k0 = g * 128 + ch * 8;
     float v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = xs[k0 + i];
-    uint4 packed;
-    float cp;
-    pack_unit<Tr>(v, packed, cp);
-    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)t * (a.H / 128) + g) * kChunk + 16 + ch * 16) = packed;
-    cpart[u] = cp;
-  }
-  __syncthreads();
-  for (int g = tid; g < a.H / 128; g += 256) {
-    float c = 0.f;
-    for (int u = 0; u < 16; ++u) c += cpart[g * 16 + u];
-    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)t * (a.H / 128) + g) * kChunk) = correction_unit(c);
+    for (int i = 0; i < 8; ++i) v[i] = xs[g * 128 + ch * 8 + i];
+    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)t * (a.H / 128) + g) * kChunk + ch * 16) = pack_unit(v);
   }
 
   // 2. routing for this token
@@ -413,7 +371,7 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   const int TK = a.T * a.K;
   // every token's routing, read once into shared memory when it fits
   const bool in_smem = TK <= kPlanSmemEntries;
-  int* pidx = reinterpret_cast<int*>(rsm + a.H + 2 * a.E + a.H / 8);
+  int* pidx = reinterpret_cast<int*>(rsm + a.H + 2 * a.E);
   float* pwts = reinterpret_cast<float*>(pidx + (in_smem ? TK : 0));
   for (int e = tid; e < a.E; e += 256) cnt[e] = 0;
   if (in_smem)
@@ -451,6 +409,7 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
           const int p = off[e] + base + __popc(bal & ((1u << lane) - 1u));
           a.plan.pos[(int64_t)tt * a.K + k] = p;
           a.plan.a_tok[p] = tt;
+          a.plan.a_tk[p] = (int)at;
           a.plan.a_w[p] = in_smem ? pwts[at] : __ldcg(a.plan.wts + at);
         }
         base += __popc(bal);
@@ -470,7 +429,6 @@ struct ExpertMaps {
 static_assert(sizeof(ExpertMaps) == 384, "ExpertMaps layout");
 
 struct EngineArgs {
-  ShiftMul shm;  // 2^31, 2^24, 2^23 (see dequant_word_fma)
   int K;     // reduction length (multiple of 128)
   int G;     // K / 128
   int N;     // weight rows
@@ -479,6 +437,7 @@ struct EngineArgs {
   const int4* segs;
   const int* n_segs;
   const int* a_tok;
+  const int* a_tk;
   const float* a_w;
   const int* pos;
   const hn_expert_ptrs* table;
@@ -487,10 +446,9 @@ struct EngineArgs {
   ExpertMaps single_maps;
   const uint8_t* bsrc;  // staged tokens, [row][group][kChunk]
   int64_t b_rstride;    // bytes per staged row (groups * kChunk)
-  int64_t b_rows;       // staged rows (KIND_DOWN tensor maps)
+  int64_t b_rows;       // staged rows (KIND_DOWN tensor map)
   int b_use_tok;
-  CUtensorMap bmap;     // KIND_DOWN: bsrc as uint8 [rows, b_rstride], 128 B x N boxes, 128B swizzle
-  CUtensorMap cmap;     // KIND_DOWN: same tensor, 16 B x N boxes (correction units), no swizzle
+  CUtensorMap bmap;     // KIND_DOWN: bsrc as uint8 [b_rows, b_rstride], 128 B x N boxes, 128B swizzle
   uint8_t* hp;
   int64_t hp_rstride;
   float* R;
@@ -522,13 +480,10 @@ struct TileMap {
 //     x 128 B (two 128-wide k-groups), 128B-swizzled: the 16-byte chunk c of
 //     row r sits at chunk c ^ (r & 7) of the row.
 //   token ring: SB stages of [2 halves][N tokens][128 B], 128B-swizzled
-//     (the 16-byte unit u of token row r at u ^ (r & 7)): half h holds data
-//     units 8h..8h+7 (logical k 64h..64h+63) of the k-group; the K-major
-//     SW128 operand of MMA k-step s starts at half s/4, byte 32*(s%4), with
-//     SBO = 1024 bytes (8 token rows);
-//   correction ring: SB stages of [N tokens][16 B] correction units followed
-//     by N x 16 zero bytes (the second K half of the correction step);
-//   htile / cpart: epilogue staging.
+//     (the 16-byte unit u of token row r at u ^ (r & 7)): half h holds units
+//     8h..8h+7 (k 64h..64h+63) of the k-group; the K-major SW128 operand of
+//     MMA k-step s starts at half s/4, byte 32*(s%4), with SBO = 1024 bytes
+//     (8 token rows).
 template <int N, int ST, int SB>
 struct TcSmem {
   static constexpr int kHdr = 1024;
@@ -536,61 +491,69 @@ struct TcSmem {
   static constexpr int kW = ST * kWStage;
   static constexpr int kBStage = 2 * N * 128;  // a multiple of 1024: stages stay swizzle-aligned
   static constexpr int kB = SB * kBStage;
-  static constexpr int kCStage = 2 * N * 16;
-  static constexpr int kC = SB * kCStage;
-  static constexpr int kH = 128 * (N + 1) * 4 + N * 16 * 4;
-  static constexpr int kTotal = 1024 /* alignment slack */ + kHdr + kW + kB + kC + kH;
+  static constexpr int kTotal = 1024 /* alignment slack */ + kHdr + kW + kB;
   static_assert(kBStage % 1024 == 0, "token stages must stay 1024-byte aligned");
 };
 
-// TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as bf16/f16
-// pairs) from column 0, SD accumulator stages of {A0, A1} x N fp32 columns
-// after them, and the 8-column constant A block of the correction step.
-// N = 16: 3 x 128 + 3 x 32 + 8; N = 32: 2 x 128 + 3 x 64 + 8.
+// Warp roles (a warp runs on SMSP warp % 4): dequant warps, epilogue warps,
+// then one role warp on each SMSP.
 constexpr int kTmemCols = 512;
-// Warp roles (a warp runs on SMSP warp % 4): dequant warps, fold warps, then
-// one role warp on each SMSP.
-constexpr int kDeqWarps = 8;
-constexpr int kFoldWarps = 8;
-constexpr int kTokWarp = 16;   // token producer (SMSP 0)
-constexpr int kMmaWarp0 = 17;  // MMA issuer of matrix 0 (SMSP 1), allocates TMEM
-constexpr int kWgtWarp = 18;   // weight producer (SMSP 2)
-constexpr int kMmaWarp1 = 19;  // MMA issuer of matrix 1 (SMSP 3)
-constexpr int kTcThreads = 20 * 32;
+constexpr int kKSplit = 2;                       // dequant warps per (matrix, TMEM lane quarter)
+constexpr int kDeqWarps = 8 * kKSplit;
+constexpr int kEpiWarps = 4;                     // one per TMEM lane quarter
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kTokWarp = kDeqWarps + kEpiWarps;  // token producer (SMSP 0)
+constexpr int kMmaWarp0 = kTokWarp + 1;          // MMA issuer of matrix 0 (SMSP 1), allocates TMEM
+constexpr int kWgtWarp = kTokWarp + 2;           // weight producer (SMSP 2)
+constexpr int kMmaWarp1 = kTokWarp + 3;          // MMA issuer of matrix 1 (SMSP 3)
+constexpr int kTcThreads = (kTokWarp + 4) * 32;
+static_assert(kTokWarp % 4 == 0, "the four role warps must sit on the four SMSPs");
+
+// TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as float16
+// pairs) from column 0, then two tile accumulators of {A0, A1} x N fp32
+// columns (the MMA fills one while the epilogue drains the other).
+// N = 16: 3 x 128 + 2 x 32; N = 32: 3 x 128 + 2 x 64.
 template <int N>
 struct TmemPlan {
-  static constexpr int SA = (N == 16) ? 3 : 2;
-  static constexpr int SD = 3;
+  static constexpr int kDCols = 2 * N;
+  static constexpr int kFit = (kTmemCols - 2 * kDCols) / 128;
+  static constexpr int SA = kFit > 4 ? 4 : kFit;
   static constexpr int kD0 = SA * 128;
-  static constexpr int kCorr = kD0 + SD * 2 * N;
-  static_assert(kCorr + 8 <= kTmemCols, "TMEM plan exceeds 512 columns");
+  static_assert(SA >= 2 && kD0 + 2 * kDCols <= kTmemCols, "TMEM plan exceeds 512 columns");
 };
 
-// Per-thread view of the tile: thread (matrix j, row r).
-struct RowView {
-  int seg, rt, m, p0, e;
-  const uint16_t* s;  // this thread's scale row (+ group)
+// Segment, row tile, token count and first assignment of a tile.
+struct TileInfo {
+  int seg, rt, m, p0;
 };
-
 template <int KIND>
-__device__ __forceinline__ void load_rowview(const EngineArgs& a, int tile, int n_segs, int j, int r, RowView& v) {
+__device__ __forceinline__ TileInfo tile_info(const EngineArgs& a, int tile, int n_segs) {
+  TileInfo v;
   TileMap<KIND>::split(tile, a.n_rt, n_segs, v.seg, v.rt);
   const int4 sg = a.segs[v.seg];
   v.m = sg.z;
   v.p0 = sg.y;
-  v.e = sg.x;
-  const hn_expert_ptrs ep = a.table ? a.table[sg.x] : a.single;
-  const uint16_t* S;
-  int row;
-  if (KIND == KIND_GATEUP) {
-    S = j ? ep.up_scales : ep.gate_scales;
-    row = v.rt * 128 + r;
-  } else {
-    S = ep.down_scales;
-    row = v.rt * 256 + j * 128 + r;
-  }
-  row = min(row, a.N - 1);  // rows past N read row N-1's scales and are never stored
-  v.s = S + (int64_t)row * a.G;
+  return v;
+}
+template <int KIND>
+__device__ __forceinline__ int tile_expert(const EngineArgs& a, int tile, int n_segs) {
+  int seg, rt;
+  TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+  return __ldg(&a.segs[seg].x);
+}
+// Scale matrix of (expert e, matrix j) and the offset of row r's scale row in
+// a tile; rows past N read row N-1's scales and are never stored.
+template <int KIND>
+__device__ __forceinline__ const uint16_t* scale_base(const EngineArgs& a, int e, int j) {
+  const hn_expert_ptrs* ep = a.table ? a.table + e : &a.single;
+  return KIND == KIND_GATEUP ? (j ? ep->up_scales : ep->gate_scales) : ep->down_scales;
+}
+template <int KIND>
+__device__ __forceinline__ int64_t scale_off(const EngineArgs& a, int tile, int n_segs, int j, int r) {
+  int seg, rt;
+  TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+  const int row = KIND == KIND_GATEUP ? rt * 128 + r : rt * 256 + j * 128 + r;
+  return (int64_t)min(row, a.N - 1) * a.G;
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -617,49 +580,45 @@ struct Ring {
   }
 };
 
-// Persistent grouped GEMV on the 5th-generation tensor cores.
+// Persistent grouped GEMV/GEMM on the 5th-generation tensor cores.
 //
 // Work items are (tile, k-group pair); CTA c owns items [c*NI/P, (c+1)*NI/P)
-// (stream-K), so every CTA streams the same number of weight bytes.  Warp
-// roles (a warp runs on SMSP warp % 4):
-//   warps 0-7    dequant warps: warp w dequantises matrix j = w >> 2 for TMEM
-//                lanes 32*(w&3).. (its 32 rows), all 128 k of each group, into
-//                the A stage;
-//   warps 8-15   fold warps: warp w owns the same rows of matrix (w >> 2) & 1
-//                and folds each group's accumulator into fp32 registers,
-//                acc += scale[row, group] * D, for all N tokens; they also run
-//                the stream-K fix-up and the epilogue;
-//   warp 16      token producer: cp.async of each group's token units;
-//   warps 17, 19 MMA issuers for matrix 0 and matrix 1: per k-group eight
-//                K=16 steps with the dequantised weights (TMEM) as A and the
-//                tokens (SMEM) as B, then the correction step, into one TMEM
-//                accumulator stage; the two matrices use separate columns, so
-//                two warps on two SMSPs can issue them independently;
-//   warp 18      weight producer: one 32 KB 2-D TMA box pair per item.
-// Dequantising and folding are separate warps so that a warp never waits for
-// a TMEM store and a TMEM load of two different groups one after the other.
+// (stream-K), so every CTA streams the same number of weight bytes.  A tile's
+// k-groups that one CTA runs (a "piece") accumulate in one TMEM accumulator.
+// Warp roles (a warp runs on SMSP warp % 4):
+//   warps 0-15   dequant warps: warp w dequantises matrix j = (w >> 2) & 1 for
+//                TMEM lanes 32*(w&3).. (its 32 rows), k-half w >> 3 (64 k) of
+//                each group, as float16 (n - 8) * scale, into the A stage;
+//   warps 16-19  epilogue warps (one per lane quarter, both matrices): at the
+//                end of each piece they drain the accumulator, write the
+//                stream-K partial or run the epilogue;
+//   warp 20      token producer: the token ring (TMA boxes for the down
+//                phase, per-lane cp.async gathers for gate/up);
+//   warps 21, 23 MMA issuers for matrix 0 and matrix 1: per k-group eight K=16
+//                steps with the dequantised weights (TMEM) as A and the tokens
+//                (SMEM) as B into the piece's accumulator; the two matrices use
+//                separate columns, so two warps on two SMSPs issue them
+//                independently;
+//   warp 22      weight producer: one 32 KB 2-D TMA box pair per item.
 // All hand-offs are mbarriers with bounded waits.
 template <typename Tr, int N, int KIND, int EPI, int ST, int SB>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_constant__ EngineArgs a) {
   using L = TcSmem<N, ST, SB>;
-  constexpr int SA = TmemPlan<N>::SA, SD = TmemPlan<N>::SD, D0 = TmemPlan<N>::kD0, CORR = TmemPlan<N>::kCorr;
+  constexpr int SA = TmemPlan<N>::SA, D0 = TmemPlan<N>::kD0, DC = TmemPlan<N>::kDCols;
   // The token producer signals stage k after issuing group k + LOOK (its
   // copies then had LOOK groups of time to land); issuing k + LOOK needs the
   // MMA of k + LOOK - SB to be done, so SB - LOOK groups of slack remain.
   constexpr int LOOK = 3;
-  static_assert(LOOK >= 1 && SB - LOOK >= 4 && SA <= 4 && SD <= 4 && SB <= 16 && ST <= 8, "stage counts");
-  constexpr uint32_t IDESC = umma_idesc<Tr, 128, N>();
-  constexpr uint32_t IDESC_CORR = umma_idesc<BF16, 128, N>();
+  static_assert(LOOK >= 1 && SB - LOOK >= 4 && SA <= 4 && SB <= 16 && ST <= 8, "stage counts");
+  constexpr uint32_t IDESC = umma_idesc<F16, 128, N>();
   constexpr uint32_t kDescHiSW128 = (1024u >> 4) | (1u << 14) | (2u << 29);  // SBO 1024 B, version 1, SWIZZLE_128B
-  constexpr uint32_t kDescHiCorr = (128u >> 4) | (1u << 14);                 // SBO 128 B, version 1, no swizzle
-  constexpr int kFoldThreads = kFoldWarps * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   uint64_t* a_full = bars;        // [SA][2] dequant warps of matrix j -> its MMA warp
   uint64_t* a_empty = bars + 8;   // [SA][2] MMA commit (matrix j) -> its dequant warps
-  uint64_t* d_full = bars + 16;   // [SD] both MMA warps' commits -> fold warps
-  uint64_t* d_empty = bars + 20;  // [SD] fold warps -> MMA warps
+  uint64_t* d_full = bars + 16;   // [2] both MMA warps' commits at a piece end -> epilogue warps
+  uint64_t* d_empty = bars + 20;  // [2] epilogue warps -> MMA warps
   uint64_t* b_full = bars + 24;   // [SB] token producer -> MMA warps
   uint64_t* b_empty = bars + 40;  // [SB] both MMA warps' commits -> token producer
   uint64_t* w_full = bars + 56;   // [ST] weight TMA -> dequant warps
@@ -668,9 +627,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   int* bcast = reinterpret_cast<int*>(bars + 73);
   uint8_t* wst = smem + L::kHdr;
   uint8_t* bst = wst + L::kW;
-  uint8_t* cst = bst + L::kB;
-  float* htile = reinterpret_cast<float*>(cst + L::kC);
-  float* cpart = htile + 128 * (N + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_segs = *a.n_segs;
@@ -687,15 +643,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   // Items are walked with 32-bit counters: (tile0, gp0) is the first item.
   const int n_items = (int)(b1 - b0);
   const int tile0 = (int)(b0 / GP), gp0 = (int)(b0 - (int64_t)tile0 * GP);
+  const int tile_last = (int)((b1 - 1) / GP);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2 * SA; ++s) {
-      mbar_init(smem_u32(&a_full[s]), kDeqWarps / 2);  // the dequant warps of one matrix
+      mbar_init(smem_u32(&a_full[s]), 4 * kKSplit);  // the dequant warps of one matrix
       mbar_init(smem_u32(&a_empty[s]), 1);
     }
-    for (int s = 0; s < SD; ++s) {
+    for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&d_full[s]), 2);
-      mbar_init(smem_u32(&d_empty[s]), kFoldWarps);
+      mbar_init(smem_u32(&d_empty[s]), kEpiWarps);
     }
     for (int s = 0; s < SB; ++s) {
       // KIND_DOWN fills a stage with TMA (one arrival + bytes), KIND_GATEUP
@@ -713,10 +670,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
-  // zero halves of the correction ring (read by the correction MMA, never written)
-  for (int i = threadIdx.x; i < SB * N; i += kTcThreads)
-    *reinterpret_cast<uint4*>(cst + (i / N) * L::kCStage + N * 16 + (i % N) * 16) = make_uint4(0u, 0u, 0u, 0u);
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -752,13 +705,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     __syncwarp();
   } else if (warp == kTokWarp) {
     // ------------------------- token producer -------------------------
-    // Lane l copies the 17 units of token l of the segment; a stage is
-    // signalled (after its copies landed and a proxy fence) LOOK stages later.
     int k = 0, tile = tile0, gp = gp0;
     if (KIND == KIND_DOWN) {
       // Rows of a segment are consecutive (assignment order): each k-group is
-      // three TMA boxes of N rows (two 128-byte data halves, 128B swizzle, and
-      // the correction units); rows past the end are zero-filled.
+      // two TMA boxes of N rows x 128 B (128B swizzle); rows past the end are
+      // zero-filled.
       Ring<SB> rb;
       if (lane == 0) {
         for (int i = 0; i < n_items; ++i) {
@@ -770,11 +721,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
             const int grp = 2 * gp + gi;
             mbar_wait(smem_u32(&b_empty[rb.idx]), rb.phase ^ 1u, a.err);
             const uint32_t bar = smem_u32(&b_full[rb.idx]);
-            mbar_arrive_expect_tx(bar, (uint32_t)(2 * N * 128 + N * 16));
+            mbar_arrive_expect_tx(bar, (uint32_t)(2 * N * 128));
             const uint32_t dst = smem_u32(bst + rb.idx * L::kBStage);
-            tma_load_2d(dst, &a.bmap, grp * kChunk + 16, row0, bar);
-            tma_load_2d(dst + N * 128, &a.bmap, grp * kChunk + 16 + 128, row0, bar);
-            tma_load_2d(smem_u32(cst + rb.idx * L::kCStage), &a.cmap, grp * kChunk, row0, bar);
+            tma_load_2d(dst, &a.bmap, grp * kChunk, row0, bar);
+            tma_load_2d(dst + N * 128, &a.bmap, grp * kChunk + 128, row0, bar);
             rb.next();
           }
           if (++gp == GP) {
@@ -808,8 +758,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
             const int sw = lane & 7;
 #pragma unroll
             for (int u = 0; u < 16; ++u)
-              cp_async16(dst + (u >> 3) * (N * 128) + (((u & 7) ^ sw) << 4), src + 16 + u * 16);
-            cp_async16(smem_u32(cst + rb.idx * L::kCStage + lane * 16), src);
+              cp_async16(dst + (u >> 3) * (N * 128) + (((u & 7) ^ sw) << 4), src + u * 16);
           }
           cp_async_commit();
           rb.next();
@@ -838,29 +787,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     // commits are issued by one elected lane.
     const int mj = warp == kMmaWarp0 ? 0 : 1;
     Ring<SA> ra;
-    Ring<SD> rd;
     Ring<SB> rb;
+    Ring<2> rd;
     int gp = gp0;
+    uint32_t acc = 0;  // 0: the next group starts a piece (overwrites the accumulator)
     for (int i = 0; i < n_items; ++i) {
       const int ng = min(2, a.G - 2 * gp);
       for (int gi = 0; gi < ng; ++gi) {
-        const int sa = ra.idx, sd = rd.idx, sb = rb.idx;
+        const int sa = ra.idx, sb = rb.idx;
+        if (acc == 0) mbar_wait(smem_u32(&d_empty[rd.idx]), rd.phase ^ 1u, a.err);
         mbar_wait(smem_u32(&b_full[sb]), rb.phase, a.err);
-        mbar_wait(smem_u32(&d_empty[sd]), rd.phase ^ 1u, a.err);
         mbar_wait(smem_u32(&a_full[2 * sa + mj]), ra.phase, a.err);
         tc_fence_after();
-        // B descriptors (32-bit halves): data = K-major SW128 tile (start,
-        // LBO ignored = 1, SBO 1024 B, layout SWIZZLE_128B); correction = K-major
-        // no-swizzle tile (LBO = N*16 B to the zero half, SBO 128 B).
+        // B descriptor (32-bit halves): K-major SW128 tile (start, LBO ignored
+        // = 1, SBO 1024 B, layout SWIZZLE_128B)
         const uint32_t b_lo = ((smem_u32(bst + sb * L::kBStage) >> 4) & 0x3FFFu) | (1u << 16);
-        const uint32_t c_lo = ((smem_u32(cst + sb * L::kCStage) >> 4) & 0x3FFFu) | (uint32_t)(N << 16);
-        umma_group9_sw128<N>(tbase + D0 + sd * 2 * N + mj * N, tbase + sa * 128 + mj * 64, b_lo, kDescHiSW128,
-                             IDESC, c_lo, kDescHiCorr, tbase + CORR, IDESC_CORR);
+        umma_group8_sw128<N>(tbase + D0 + rd.idx * DC + mj * N, tbase + sa * 128 + mj * 64, b_lo, kDescHiSW128,
+                             IDESC, acc);
         umma_commit_elect(smem_u32(&a_empty[2 * sa + mj]));
         umma_commit_elect(smem_u32(&b_empty[sb]));
-        umma_commit_elect(smem_u32(&d_full[sd]));
+        const bool end = (2 * gp + gi == a.G - 1) || (i == n_items - 1 && gi == ng - 1);
+        if (end) {
+          umma_commit_elect(smem_u32(&d_full[rd.idx]));
+          rd.next();
+        }
+        acc = end ? 0u : 1u;
         ra.next();
-        rd.next();
         rb.next();
       }
       if (++gp == GP) gp = 0;
@@ -868,65 +820,61 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     __syncwarp();
   } else if (warp < kDeqWarps) {
     // ------------------------------ dequant warps ------------------------------
-    const int q = warp & 3, j = warp >> 2, r = q * 32 + lane;
+    constexpr int kC = 4 / kKSplit;  // 16-byte chunks (32 k each) of a group per thread
+    const int q = warp & 3, j = (warp >> 2) & 1, h = warp >> 3, r = q * 32 + lane;
     const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
     const uint8_t* wrow = wst + (j * 128 + r) * 128;  // this thread's row inside a weight stage
-    const ShiftMul shm = a.shm;
     const int swz = r & 7;
-    if (j == 0) {
-      // constant A block of the correction step: k0..k2 = -1 (bf16), rest 0
-      uint32_t cv8[8] = {0xBF80BF80u, 0x0000BF80u, 0u, 0u, 0u, 0u, 0u, 0u};
-      tmem_st8(tlane + CORR, cv8);
-      tc_wait_st();
-      tc_fence_before();
-    }
-    // Each group: (at an item start) wait for the weight stage, load this
-    // thread's 64 bytes of the group, wait for the A stage, dequantise into
-    // TMEM, signal.  Nothing here waits on a later item, so a group's signal
-    // never depends on the next weight stage having landed.
+    // Scales: those of the next item are loaded while this one runs.  The
+    // scale row of the next tile (its base pointer) and the expert of the
+    // tile after it are loaded a whole tile ahead, so no load result is
+    // consumed by the instruction stream that issued it within a tile.
+    int tile = tile0, gp = gp0;
+    const uint16_t* sp = scale_base<KIND>(a, tile_expert<KIND>(a, tile, n_segs), j) + scale_off<KIND>(a, tile, n_segs, j, r);
+    const uint16_t* nb = tile + 1 <= tile_last ? scale_base<KIND>(a, tile_expert<KIND>(a, tile + 1, n_segs), j) : sp;
+    int nne = tile + 2 <= tile_last ? tile_expert<KIND>(a, tile + 2, n_segs) : 0;
+    uint32_t sn0 = __ldg(sp + 2 * gp);
+    uint32_t sn1 = 2 * gp + 1 < a.G ? __ldg(sp + 2 * gp + 1) : 0u;
     Ring<ST> rw;
     Ring<SA> ra;
-    int gp = gp0;
 #pragma unroll 1
     for (int it = 0; it < n_items; ++it) {
       const int ng = min(2, a.G - 2 * gp);
+      const uint32_t sc0 = sn0, sc1 = sn1;
+      if (it + 1 < n_items) {
+        if (++gp == GP) {
+          gp = 0;
+          ++tile;
+          sp = nb + scale_off<KIND>(a, tile, n_segs, j, r);
+          nb = tile + 1 <= tile_last ? scale_base<KIND>(a, nne, j) : sp;
+          nne = tile + 2 <= tile_last ? tile_expert<KIND>(a, tile + 2, n_segs) : 0;
+        }
+        sn0 = __ldg(sp + 2 * gp);
+        sn1 = 2 * gp + 1 < a.G ? __ldg(sp + 2 * gp + 1) : 0u;
+      }
       const int ws = rw.idx;
       mbar_wait(smem_u32(&w_full[ws]), rw.phase, a.err);
       const uint8_t* wrow_p = wrow + ws * L::kWStage;
 #pragma unroll 1
       for (int gi = 0; gi < ng; ++gi) {
         const int sa = ra.idx;
-        uint4 W[4];
+        uint4 W[kC];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + i) ^ swz) << 4));
+        for (int i = 0; i < kC; ++i)
+          W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + h * kC + i) ^ swz) << 4));
+        const uint32_t sv = gi ? sc1 : sc0;
+        const uint32_t s2 = sv | (sv << 16);
         mbar_wait(smem_u32(&a_empty[2 * sa + j]), ra.phase ^ 1u, a.err);
         tc_fence_after();
-        const uint32_t acol = tlane + sa * 128 + j * 64;
-        {
-          uint32_t o0[16], o1[16];
-          dequant_word_fma<Tr>(W[0].x, o0 + 0, shm);
-          dequant_word_fma<Tr>(W[0].y, o0 + 4, shm);
-          dequant_word_fma<Tr>(W[0].z, o0 + 8, shm);
-          dequant_word_fma<Tr>(W[0].w, o0 + 12, shm);
-          dequant_word_fma<Tr>(W[1].x, o1 + 0, shm);
-          dequant_word_fma<Tr>(W[1].y, o1 + 4, shm);
-          dequant_word_fma<Tr>(W[1].z, o1 + 8, shm);
-          dequant_word_fma<Tr>(W[1].w, o1 + 12, shm);
-          tmem_st16(acol, o0);
-          tmem_st16(acol + 16, o1);
-        }
-        {
-          uint32_t o2[16], o3[16];
-          dequant_word_fma<Tr>(W[2].x, o2 + 0, shm);
-          dequant_word_fma<Tr>(W[2].y, o2 + 4, shm);
-          dequant_word_fma<Tr>(W[2].z, o2 + 8, shm);
-          dequant_word_fma<Tr>(W[2].w, o2 + 12, shm);
-          dequant_word_fma<Tr>(W[3].x, o3 + 0, shm);
-          dequant_word_fma<Tr>(W[3].y, o3 + 4, shm);
-          dequant_word_fma<Tr>(W[3].z, o3 + 8, shm);
-          dequant_word_fma<Tr>(W[3].w, o3 + 12, shm);
-          tmem_st16(acol + 32, o2);
-          tmem_st16(acol + 48, o3);
+        const uint32_t acol = tlane + sa * 128 + j * 64 + h * (16 * kC);
+#pragma unroll
+        for (int i = 0; i < kC; ++i) {
+          uint32_t o[16];
+          dequant_word_f16(W[i].x, s2, o + 0);
+          dequant_word_f16(W[i].y, s2, o + 4);
+          dequant_word_f16(W[i].z, s2, o + 8);
+          dequant_word_f16(W[i].w, s2, o + 12);
+          tmem_st16(acol + 16 * i, o);
         }
         tc_wait_st();
         tc_fence_before();
@@ -941,171 +889,170 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         ra.next();
       }
       rw.next();
-      if (++gp == GP) gp = 0;
     }
-  } else if (warp < kDeqWarps + kFoldWarps) {
-    // ------------------------------- fold warps -------------------------------
-    const int fw = warp - kDeqWarps;
-    const int q = fw & 3, j = fw >> 2, r = q * 32 + lane;
+  } else {
+    // ------------------------------ epilogue warps ------------------------------
+    const int q = warp & 3, r = q * 32 + lane;
+    const int et = threadIdx.x - kDeqWarps * 32;  // 0 .. kEpiThreads-1
     const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
-    int tile = tile0;
-    RowView cv;
-    load_rowview<KIND>(a, tile, n_segs, j, r, cv);
-    float acc[N];
+    // One 16-token chunk of the piece's result: v0 = matrix 0 (gate rows, or
+    // the first 128 down rows), v1 = matrix 1 (up rows, or down rows 128..255).
+    auto emit = [&](const TileInfo& ti, int hc, const float (&v0)[16], const float (&v1)[16]) {
+      if (KIND == KIND_GATEUP) {
+        // SiLU(gate) * up as float16 into the down phase's staged operand:
+        // row r of row tile rt is k = r of k-group rt
+        uint8_t* dstp = a.hp + (int64_t)ti.rt * kChunk + staged_offset(r);
 #pragma unroll
-    for (int n = 0; n < N; ++n) acc[n] = 0.f;
-    // Group scales of the current item, and of the next one when it is in the
-    // same tile (loaded one item ahead so the loads never stall a group).
-    auto load_scales = [&](int gp_, float (&sc)[2]) {
-      const int g0 = 2 * gp_;
-      sc[0] = __half2float(__ushort_as_half(__ldg(cv.s + g0)));
-      sc[1] = g0 + 1 < a.G ? __half2float(__ushort_as_half(__ldg(cv.s + g0 + 1))) : 0.f;
+        for (int n = 0; n < 16; ++n) {
+          const int tok = hc * 16 + n;
+          if (tok < ti.m) {
+            const float hv = silu_f(v0[n]) * v1[n];
+            *reinterpret_cast<__half*>(dstp + (int64_t)(ti.p0 + tok) * a.hp_rstride) = __float2half_rn(hv);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int row = ti.rt * 256 + jj * 128 + r;
+          if (row < a.N) {
+#pragma unroll
+            for (int n = 0; n < 16; ++n) {
+              const int tok = hc * 16 + n;
+              if (tok < ti.m) {
+                const int p = ti.p0 + tok;
+                const float v = jj ? v1[n] : v0[n];
+                if (EPI == EPI_STORE)
+                  reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)a.a_tok[p] * a.ldo + row] = Tr::from_f(v);
+                else
+                  a.R[(int64_t)a.a_tk[p] * a.N + row] = v * a.a_w[p];
+              }
+            }
+          }
+        }
+      }
     };
-    float sc_cur[2], sc_nxt[2];
-    load_scales(gp0, sc_nxt);
-    Ring<SD> rd;
-    int gp = gp0;
+    // Top-k combine, spread over the tiles: R holds weight * y for every
+    // (token, slot) row; each (row tile, token) counts the contributions
+    // written so far, and the tile that writes a token's last one sums its
+    // slots in slot order (the same order whichever tile does it) into the
+    // output.  The counter is reset by that tile.
+    auto combine = [&](const TileInfo& ti) {
+      __threadfence();
+      named_bar_sync(1, kEpiThreads);
+      if (et < ti.m) {
+        const int t = a.a_tok[ti.p0 + et];
+        int* ctr = a.rt_ctr + (int64_t)ti.rt * a.T + t;
+        const bool last = atomicAdd(ctr, 1) == a.topk - 1;
+        if (last) *ctr = 0;
+        bcast[2 + et] = last ? t : -1;
+      }
+      named_bar_sync(1, kEpiThreads);
+      __threadfence();
+      const int r0 = ti.rt * 256 + 2 * et;
+      if (r0 < a.N) {  // N is a multiple of 128: rows r0, r0 + 1
+        const float* Rb = a.R + r0;
+        typename Tr::T* ob = reinterpret_cast<typename Tr::T*>(a.out) + r0;
+#pragma unroll 4
+        for (int i = 0; i < ti.m; ++i) {
+          const int t = bcast[2 + i];
+          if (t >= 0) {
+            float x = 0.f, y = 0.f;
+            for (int kk = 0; kk < a.topk; ++kk) {
+              const float2 v = __ldcg(reinterpret_cast<const float2*>(Rb + (int64_t)(t * a.topk + kk) * a.N));
+              x += v.x;
+              y += v.y;
+            }
+            ob[(int64_t)t * a.ldo] = Tr::from_f(x);
+            ob[(int64_t)t * a.ldo + 1] = Tr::from_f(y);
+          }
+        }
+      }
+    };
+    Ring<2> rd;
 #pragma unroll 1
-    for (int it = 0; it < n_items; ++it) {
-      const int ng = min(2, a.G - 2 * gp);
-      sc_cur[0] = sc_nxt[0];
-      sc_cur[1] = sc_nxt[1];
-      if (gp + 1 < GP && it + 1 < n_items) load_scales(gp + 1, sc_nxt);
+    for (int tile = tile0; tile <= tile_last; ++tile) {
+      const TileInfo ti = tile_info<KIND>(a, tile, n_segs);
+      const int64_t ts = (int64_t)tile * GP, te = ts + GP;
+      const uint32_t dcol = tlane + D0 + rd.idx * DC;
+      mbar_wait(smem_u32(&d_full[rd.idx]), rd.phase, a.err);
+      tc_fence_after();
+      bool own = true;
+      if (b0 <= ts && b1 >= te) {
+        // the whole tile ran here: epilogue straight from the accumulator
 #pragma unroll 1
-      for (int gi = 0; gi < ng; ++gi) {
-        const int grp = 2 * gp + gi;
-        const int sd = rd.idx;
-        const float scale = gi ? sc_cur[1] : sc_cur[0];
-        const int m = cv.m;
-        mbar_wait(smem_u32(&d_full[sd]), rd.phase, a.err);
-        tc_fence_after();
+        for (int hc = 0; hc < N / 16; ++hc) {
+          if (hc * 16 < ti.m) {
+            uint32_t d0[16], d1[16];
+            tmem_ld16(dcol + hc * 16, d0);
+            tmem_ld16(dcol + N + hc * 16, d1);
+            tmem_ld_wait16x2(d0, d1);
+            float v0[16], v1[16];
 #pragma unroll
-        for (int h = 0; h < N / 16; ++h) {
-          if (h * 16 < m) {
-            uint32_t d[16];
-            tmem_ld16(tlane + D0 + sd * 2 * N + j * N + h * 16, d);
-            tmem_ld_wait16(d);
-#pragma unroll
-            for (int n = 0; n < 16; n += 2) ffma2(acc[h * 16 + n], acc[h * 16 + n + 1], scale, d[n], d[n + 1]);
+            for (int n = 0; n < 16; ++n) {
+              v0[n] = __uint_as_float(d0[n]);
+              v1[n] = __uint_as_float(d1[n]);
+            }
+            emit(ti, hc, v0, v1);
           }
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&d_empty[sd]));
-        rd.next();
-        const bool tile_end = (grp == a.G - 1) || (it == n_items - 1 && gi == ng - 1);
-        if (!tile_end) continue;
-        // ---------------- finish this CTA's piece of the tile ----------------
-        const int64_t ts = (int64_t)tile * GP, te = ts + GP;
-        bool own = true;
-        if (!(b0 <= ts && b1 >= te)) {
-          // Every piece (the last arriver's own too) goes through its partial
-          // slot; the last arriver sums the slots in CTA order, so the result
-          // does not depend on which CTA finishes last.
-          const int slot = (ts <= b0) ? 0 : 1;
-          float* dst = a.part + ((((int64_t)c * 2 + slot) * kFoldWarps + fw) * N) * 32 + lane;
+        if (lane == 0) mbar_arrive(smem_u32(&d_empty[rd.idx]));
+      } else {
+        // Every piece of a split tile (the last arriver's own too) goes
+        // through its partial slot; the last arriver sums the slots in CTA
+        // order, so the result does not depend on which CTA finishes last.
+        const int slot = (ts <= b0) ? 0 : 1;
+        float* dst = a.part + ((((int64_t)c * 2 + slot) * 2 * kEpiWarps + q) * N) * 32 + lane;
+#pragma unroll 1
+        for (int hc = 0; hc < N / 16; ++hc) {
+          if (hc * 16 < ti.m) {
+            uint32_t d0[16], d1[16];
+            tmem_ld16(dcol + hc * 16, d0);
+            tmem_ld16(dcol + N + hc * 16, d1);
+            tmem_ld_wait16x2(d0, d1);
 #pragma unroll
-          for (int n = 0; n < N; ++n) dst[n * 32] = acc[n];
-          __threadfence();
-          named_bar_sync(1, kFoldThreads);
-          const int64_t c0 = cta_of(ts), c1 = cta_of(te - 1);
-          if (fw == 0 && lane == 0) bcast[0] = (atomicAdd(&a.tile_ctr[tile], 1) == (int)(c1 - c0));
-          named_bar_sync(1, kFoldThreads);
-          own = bcast[0] != 0;
-          if (own) {
-            __threadfence();
-#pragma unroll
-            for (int n = 0; n < N; ++n) acc[n] = 0.f;
-            for (int64_t cc = c0; cc <= c1; ++cc) {
-              const int64_t bc = begin_of(cc);
-              const int sl = (bc >= ts && bc < te) ? 0 : 1;
-              const float* src = a.part + ((((int64_t)cc * 2 + sl) * kFoldWarps + fw) * N) * 32 + lane;
-#pragma unroll
-              for (int n = 0; n < N; ++n) acc[n] += ld_cg_f32(src + n * 32);
+            for (int n = 0; n < 16; ++n) {
+              dst[(hc * 16 + n) * 32] = __uint_as_float(d0[n]);
+              dst[(kEpiWarps * N + hc * 16 + n) * 32] = __uint_as_float(d1[n]);
             }
-            if (fw == 0 && lane == 0) a.tile_ctr[tile] = 0;
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&d_empty[rd.idx]));
+        __threadfence();
+        named_bar_sync(1, kEpiThreads);
+        const int64_t c0 = cta_of(ts), c1 = cta_of(te - 1);
+        if (et == 0) bcast[0] = (atomicAdd(&a.tile_ctr[tile], 1) == (int)(c1 - c0));
+        named_bar_sync(1, kEpiThreads);
+        own = bcast[0] != 0;
         if (own) {
-          const int ft = threadIdx.x - kDeqWarps * 32;  // 0 .. kFoldThreads-1
-          if (KIND == KIND_GATEUP) {
-            if (j == 1) {
+          __threadfence();
+#pragma unroll 1
+          for (int hc = 0; hc < N / 16; ++hc) {
+            if (hc * 16 < ti.m) {
+              float v0[16], v1[16];
 #pragma unroll
-              for (int n = 0; n < N; ++n) htile[r * (N + 1) + n] = acc[n];
-            }
-            named_bar_sync(1, kFoldThreads);
-            if (j == 0) {
+              for (int n = 0; n < 16; ++n) v0[n] = v1[n] = 0.f;
+              for (int64_t cc = c0; cc <= c1; ++cc) {
+                const int64_t bc = begin_of(cc);
+                const int sl = (bc >= ts && bc < te) ? 0 : 1;
+                const float* src = a.part + ((((int64_t)cc * 2 + sl) * 2 * kEpiWarps + q) * N) * 32 + lane;
 #pragma unroll
-              for (int n = 0; n < N; ++n) {
-                const float hv = silu_f(acc[n]) * htile[r * (N + 1) + n];
-                htile[r * (N + 1) + n] = Tr::to_f(Tr::from_f(hv));
-              }
-            }
-            named_bar_sync(1, kFoldThreads);
-            uint8_t* dstp = a.hp + (int64_t)cv.rt * kChunk;  // group rt of each staged row
-            for (int task = ft; task < m * 16; task += kFoldThreads) {
-              const int tok = task >> 4, ch = task & 15;
-              float v[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) v[i] = htile[(ch * 8 + i) * (N + 1) + tok];
-              uint4 pk;
-              float cp;
-              pack_unit<Tr>(v, pk, cp);
-              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + tok) * a.hp_rstride + 16 + ch * 16) = pk;
-              cpart[tok * 16 + ch] = cp;
-            }
-            named_bar_sync(1, kFoldThreads);
-            if (ft < m) {
-              float cs = 0.f;
-              for (int u = 0; u < 16; ++u) cs += cpart[ft * 16 + u];
-              *reinterpret_cast<uint4*>(dstp + (int64_t)(cv.p0 + ft) * a.hp_rstride) = correction_unit(cs);
-            }
-            named_bar_sync(1, kFoldThreads);
-          } else {
-            const int row = cv.rt * 256 + j * 128 + r;
-            if (row < a.N) {
-#pragma unroll
-              for (int n = 0; n < N; ++n) {
-                if (n < m) {
-                  const int p = cv.p0 + n;
-                  if (EPI == EPI_STORE)
-                    reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)a.a_tok[p] * a.ldo + row] = Tr::from_f(acc[n]);
-                  else
-                    a.R[(int64_t)p * a.N + row] = acc[n] * a.a_w[p];
+                for (int n = 0; n < 16; ++n) {
+                  v0[n] += ld_cg_f32(src + (hc * 16 + n) * 32);
+                  v1[n] += ld_cg_f32(src + (kEpiWarps * N + hc * 16 + n) * 32);
                 }
               }
-            }
-            if (EPI == EPI_COMBINE) {
-              __threadfence();
-              named_bar_sync(1, kFoldThreads);
-              if (ft == 0) bcast[1] = (atomicAdd(&a.rt_ctr[cv.rt], 1) == n_segs - 1);
-              named_bar_sync(1, kFoldThreads);
-              if (bcast[1]) {
-                __threadfence();
-                const int r0 = cv.rt * 256, nr = min(256, a.N - r0);
-                for (int task = ft; task < a.T * nr; task += kFoldThreads) {
-                  const int t = task / nr, rr = r0 + task - t * nr;
-                  float sacc = 0.f;
-                  for (int kk = 0; kk < a.topk; ++kk)
-                    sacc += ld_cg_f32(a.R + (int64_t)a.pos[t * a.topk + kk] * a.N + rr);
-                  reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)t * a.ldo + rr] = Tr::from_f(sacc);
-                }
-                if (ft == 0) a.rt_ctr[cv.rt] = 0;
-              }
+              emit(ti, hc, v0, v1);
             }
           }
-        }
-#pragma unroll
-        for (int n = 0; n < N; ++n) acc[n] = 0.f;
-      }
-      if (++gp == GP) {
-        gp = 0;
-        if (it + 1 < n_items) {
-          ++tile;
-          load_rowview<KIND>(a, tile, n_segs, j, r, cv);
-          load_scales(0, sc_nxt);
+          if (et == 0) a.tile_ctr[tile] = 0;
         }
       }
+      if (KIND == KIND_DOWN && EPI == EPI_COMBINE && own) combine(ti);
+      rd.next();
     }
   }
 
@@ -1127,11 +1074,10 @@ static int pick_nt(int64_t max_tokens_per_expert) { return max_tokens_per_expert
 // stay within 227 KB of shared memory.
 template <int N>
 struct TcTune {
-  static constexpr int ST = (N == 16) ? 5 : 4, SB = 8;
+  static constexpr int ST = 5, SB = 8;
 };
 
-static int encode_token_maps(CUtensorMap* data, CUtensorMap* corr, const void* base, int64_t rows,
-                             int64_t row_bytes, int box_rows);
+static int encode_token_map(CUtensorMap* data, const void* base, int64_t rows, int64_t row_bytes, int box_rows);
 
 template <typename Tr, int N, int KIND, int EPI>
 static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
@@ -1142,7 +1088,7 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
   auto kern = tc_engine_kernel<Tr, N, KIND, EPI, TU::ST, TU::SB>;
   EngineArgs e = a;
   if (KIND == KIND_DOWN) {
-    const int rc = encode_token_maps(&e.bmap, &e.cmap, e.bsrc, e.b_rows, e.b_rstride, N);
+    const int rc = encode_token_map(&e.bmap, e.bsrc, e.b_rows, e.b_rstride, N);
     if (rc) return rc;
   }
   static bool attr_set[64] = {};  // per instantiation and device
@@ -1174,7 +1120,7 @@ static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
 // call, because another shape's data section may have covered them.
 struct Layout {
   size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
-  size_t counts, n_segs, segs, a_tok, a_w, pos, idx, wts, xp, hp, part1, part2, R, data;  // back (relative)
+  size_t counts, n_segs, segs, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, part1, part2, R, data;  // back (relative)
   size_t total() const { return counters + data; }
 };
 
@@ -1199,13 +1145,14 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.route_ctr = take(4);
   l.ctr1 = take(F ? 4 * max_segs * (F / 128) : 0);
   l.ctr2 = take(4 * max_segs * n_rt2);
-  l.rtctr = take(4 * n_rt2);
+  l.rtctr = take(combine ? 4 * n_rt2 * T : 4);
   l.counters = o;
   o = 0;
   l.counts = take(4 * E);
   l.n_segs = take(4);
   l.segs = take(16 * max_segs);
   l.a_tok = take(4 * TK);
+  l.a_tk = take(4 * TK);
   l.a_w = take(4 * TK);
   l.pos = take(4 * TK);
   l.idx = take(4 * TK);
@@ -1234,6 +1181,7 @@ static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
   p.n_segs = reinterpret_cast<int*>(d + l.n_segs);
   p.segs = reinterpret_cast<int4*>(d + l.segs);
   p.a_tok = reinterpret_cast<int*>(d + l.a_tok);
+  p.a_tk = reinterpret_cast<int*>(d + l.a_tk);
   p.a_w = reinterpret_cast<float*>(d + l.a_w);
   p.pos = reinterpret_cast<int*>(d + l.pos);
   p.idx = reinterpret_cast<int*>(d + l.idx);
@@ -1264,7 +1212,7 @@ template <typename Tr>
 static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   const int64_t TK = (int64_t)ra.T * ra.K;
   RouteArgs r = ra;
-  size_t sm = (size_t)(ra.H + 2 * ra.E + ra.H / 8) * 4 + (TK <= kPlanSmemEntries ? (size_t)TK * 8 : 0);
+  size_t sm = (size_t)(ra.H + 2 * ra.E) * 4 + (TK <= kPlanSmemEntries ? (size_t)TK * 8 : 0);
   sm = std::max(sm, (size_t)(2 * ra.E) * 4);
   sm = (sm + 15) & ~(size_t)15;
   r.wbuf_off = (int)sm;
@@ -1328,10 +1276,8 @@ static int encode_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64
 }
 
 // Staged token rows (uint8 [rows, row_bytes]) for the down-phase token ring:
-// data halves as 128 B x box_rows boxes with 128B swizzle, correction units as
-// 16 B x box_rows boxes without swizzle.
-static int encode_token_maps(CUtensorMap* data, CUtensorMap* corr, const void* base, int64_t rows,
-                             int64_t row_bytes, int box_rows) {
+// 128 B x box_rows boxes with 128B swizzle.
+static int encode_token_map(CUtensorMap* data, const void* base, int64_t rows, int64_t row_bytes, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(HN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (no CUDA driver)");
   HN_REQUIRE(base && ((uintptr_t)base & 255) == 0 && row_bytes % 16 == 0 && rows >= 1,
@@ -1344,11 +1290,6 @@ static int encode_token_maps(CUtensorMap* data, CUtensorMap* corr, const void* b
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(HN_ERR_CUDA, "cuTensorMapEncodeTiled (tokens) failed: " + std::to_string((int)r));
-  cuuint32_t box_c[2] = {16u, (cuuint32_t)box_rows};
-  r = fn(corr, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box_c, es,
-         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(HN_ERR_CUDA, "cuTensorMapEncodeTiled (corrections) failed: " + std::to_string((int)r));
   return HN_OK;
 }
 
@@ -1431,7 +1372,6 @@ static int run_moe(const MoECall& m) {
   if (rc || !m.run_experts || m.phase == 1) return rc;
 
   EngineArgs e1{};
-  e1.shm = ShiftMul{1u << 31, 1u << 24, 1u << 23};
   e1.K = (int)m.H;
   e1.G = (int)(m.H / 128);
   e1.N = (int)m.F;
@@ -1441,6 +1381,7 @@ static int run_moe(const MoECall& m) {
   e1.segs = plan.segs;
   e1.n_segs = plan.n_segs;
   e1.a_tok = plan.a_tok;
+  e1.a_tk = plan.a_tk;
   e1.a_w = plan.a_w;
   e1.pos = plan.pos;
   e1.table = m.table;
@@ -1700,7 +1641,6 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   ra.seg = seg_tokens(nt);
   ra.plan = plan;
   EngineArgs e{};
-  e.shm = ShiftMul{1u << 31, 1u << 24, 1u << 23};
   e.K = (int)K;
   e.G = (int)(K / 128);
   e.N = (int)N;
@@ -1710,6 +1650,7 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   e.segs = plan.segs;
   e.n_segs = plan.n_segs;
   e.a_tok = plan.a_tok;
+  e.a_tk = plan.a_tk;
   e.a_w = plan.a_w;
   e.pos = plan.pos;
   e.table = nullptr;
