@@ -136,10 +136,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 // Bounded wait: gives up after kWaitLimitNs, records DEV_ERR_WAIT_TIMEOUT in
 // *err and returns false, so a kernel whose partner never arrives still ends.
-// Once any thread of the launch has recorded an error, every later wait of
-// every thread gives up at once (it polls *err), so a failing launch finishes
-// within about one wait limit instead of one limit per wait.
+// A wait first polls the barrier alone (kQuietPolls suspending try_waits, at
+// most kQuietPolls * kSuspendHintNs): reading *err is a global-memory round
+// trip, and a wait that branched on it before polling would pay that latency
+// even when the phase completes a few cycles later.  Past the quiet polls it
+// reads *err every kQuietPolls polls, so once any thread of the launch has
+// recorded an error every other wait gives up within a few milliseconds, and
+// a failing launch finishes within about one wait limit.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr int kQuietPolls = 16;
 __device__ __forceinline__ int ld_volatile_s32(const int* p) {
   int v;
   asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
@@ -148,13 +153,15 @@ __device__ __forceinline__ int ld_volatile_s32(const int* p) {
 constexpr uint32_t kSuspendHintNs = 20000;
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  if (err && ld_volatile_s32(err) != 0) return false;
+#pragma unroll 1
+  for (int i = 0; i < kQuietPolls; ++i)
+    if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 8; ++i)
-      if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
     if (err && ld_volatile_s32(err) != 0) return false;
+#pragma unroll 1
+    for (int i = 0; i < kQuietPolls; ++i)
+      if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
   if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);

@@ -825,33 +825,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
     const uint8_t* wrow = wst + (j * 128 + r) * 128;  // this thread's row inside a weight stage
     const int swz = r & 7;
-    // Scales: those of the next item are loaded while this one runs.  The
-    // scale row of the next tile (its base pointer) and the expert of the
+    // Scale prefetch cursor, two items ahead of the dequantisation: fetch()
+    // loads the two group scales of the item at (ptile, pgp) and advances.
+    // The scale row of the next tile (its base pointer) and the expert of the
     // tile after it are loaded a whole tile ahead, so no load result is
-    // consumed by the instruction stream that issued it within a tile.
-    int tile = tile0, gp = gp0;
-    const uint16_t* sp = scale_base<KIND>(a, tile_expert<KIND>(a, tile, n_segs), j) + scale_off<KIND>(a, tile, n_segs, j, r);
-    const uint16_t* nb = tile + 1 <= tile_last ? scale_base<KIND>(a, tile_expert<KIND>(a, tile + 1, n_segs), j) : sp;
-    int nne = tile + 2 <= tile_last ? tile_expert<KIND>(a, tile + 2, n_segs) : 0;
-    uint32_t sn0 = __ldg(sp + 2 * gp);
-    uint32_t sn1 = 2 * gp + 1 < a.G ? __ldg(sp + 2 * gp + 1) : 0u;
+    // consumed soon after it was issued.
+    int ptile = tile0, pgp = gp0, pleft = n_items;
+    const uint16_t* sp =
+        scale_base<KIND>(a, tile_expert<KIND>(a, ptile, n_segs), j) + scale_off<KIND>(a, ptile, n_segs, j, r);
+    const uint16_t* nb = ptile + 1 <= tile_last ? scale_base<KIND>(a, tile_expert<KIND>(a, ptile + 1, n_segs), j) : sp;
+    int nne = ptile + 2 <= tile_last ? tile_expert<KIND>(a, ptile + 2, n_segs) : 0;
+    auto fetch = [&](uint32_t& s0, uint32_t& s1) {
+      if (pleft <= 0) return;
+      s0 = __ldg(sp + 2 * pgp);
+      s1 = 2 * pgp + 1 < a.G ? __ldg(sp + 2 * pgp + 1) : 0u;
+      if (--pleft > 0 && ++pgp == GP) {
+        pgp = 0;
+        ++ptile;
+        sp = nb + scale_off<KIND>(a, ptile, n_segs, j, r);
+        nb = ptile + 1 <= tile_last ? scale_base<KIND>(a, nne, j) : sp;
+        nne = ptile + 2 <= tile_last ? tile_expert<KIND>(a, ptile + 2, n_segs) : 0;
+      }
+    };
+    uint32_t sc0 = 0, sc1 = 0, n10 = 0, n11 = 0, n20 = 0, n21 = 0;  // scales of items it, it+1, it+2
+    fetch(sc0, sc1);
+    fetch(n10, n11);
+    fetch(n20, n21);
+    int gp = gp0;
     Ring<ST> rw;
     Ring<SA> ra;
 #pragma unroll 1
     for (int it = 0; it < n_items; ++it) {
       const int ng = min(2, a.G - 2 * gp);
-      const uint32_t sc0 = sn0, sc1 = sn1;
-      if (it + 1 < n_items) {
-        if (++gp == GP) {
-          gp = 0;
-          ++tile;
-          sp = nb + scale_off<KIND>(a, tile, n_segs, j, r);
-          nb = tile + 1 <= tile_last ? scale_base<KIND>(a, nne, j) : sp;
-          nne = tile + 2 <= tile_last ? tile_expert<KIND>(a, tile + 2, n_segs) : 0;
-        }
-        sn0 = __ldg(sp + 2 * gp);
-        sn1 = 2 * gp + 1 < a.G ? __ldg(sp + 2 * gp + 1) : 0u;
-      }
       const int ws = rw.idx;
       mbar_wait(smem_u32(&w_full[ws]), rw.phase, a.err);
       const uint8_t* wrow_p = wrow + ws * L::kWStage;
@@ -889,6 +894,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         ra.next();
       }
       rw.next();
+      if (++gp == GP) gp = 0;
+      sc0 = n10;
+      sc1 = n11;
+      n10 = n20;
+      n11 = n21;
+      fetch(n20, n21);
     }
   } else {
     // ------------------------------ epilogue warps ------------------------------
