@@ -62,7 +62,7 @@ def peaks():
 
 # DRAM bytes (read + write) of one gate/up engine launch, from the ncu capture
 # summarised in profiles/ (per launch, same workload); None where not captured.
-GATEUP_TRAFFIC = {1: 130372352, 64: 504572672}
+GATEUP_TRAFFIC = {64: 503473408}
 
 
 def blob_bytes(h, f, g=128):
