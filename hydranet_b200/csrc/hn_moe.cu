@@ -564,6 +564,23 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// The same load with an L2 cache policy (createpolicy): weights are read
+// once per layer, so they are loaded evict-first and leave L2 to what is
+// reused (staged tokens, scales, routing plan, router weights, code).
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3}], [%4], %5;" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 // Stage index and phase bit of a ring of S mbarrier-guarded stages, advanced
 // once per use.  A consumer waits on full[idx] with parity `phase`; a producer
 // waits on empty[idx] with parity `phase ^ 1`, which a freshly initialised
@@ -678,6 +695,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   if (warp == kWgtWarp) {
     // ------------------------- weight producer (2-D TMA) -------------------------
     if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
       Ring<ST> rw;
       int tile = tile0, gp = gp0;
       for (int i = 0; i < n_items; ++i) {
@@ -690,10 +708,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         mbar_arrive_expect_tx(bar, L::kWStage);
         const uint32_t dst = smem_u32(wst + rw.idx * L::kWStage);
         if (KIND == KIND_GATEUP) {
-          tma_load_2d(dst, &em->gate, gp * 128, rt * 128, bar);
-          tma_load_2d(dst + 16384, &em->up, gp * 128, rt * 128, bar);
+          tma_load_2d_hint(dst, &em->gate, gp * 128, rt * 128, bar, pol);
+          tma_load_2d_hint(dst + 16384, &em->up, gp * 128, rt * 128, bar, pol);
         } else {
-          tma_load_2d(dst, &em->down, gp * 128, rt * 256, bar);
+          tma_load_2d_hint(dst, &em->down, gp * 128, rt * 256, bar, pol);
         }
         rw.next();
         if (++gp == GP) {
