@@ -1,6 +1,6 @@
 // Shared helpers of the sm_100a INT4 MoE kernels: error plumbing, dtype
 // traits, and inline-PTX wrappers (cp.async, TMA bulk copies, mbarriers,
-// mma.sync).
+// tcgen05, programmatic dependent launch).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -166,6 +166,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
   if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);
   return false;
+}
+
+// Programmatic dependent launch: griddepcontrol.wait blocks until the
+// preceding grid of the stream has completed and its memory is visible (it
+// returns at once when the launch had no programmatic dependency);
+// launch_dependents lets the next grid of the stream start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // TMA bulk copy (non-tensor) global -> shared, completion on an mbarrier.

@@ -459,6 +459,7 @@ struct EngineArgs {
   int* rt_ctr;
   int* err;
   int P;
+  int early;  // KIND_DOWN after a gate/up launch: only the token producer waits for it
 };
 
 template <int KIND>
@@ -646,22 +647,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   uint8_t* bst = wst + L::kW;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_segs = *a.n_segs;
-  const int n_tiles = a.n_rt * n_segs;
-  const int GP = (a.G + 1) >> 1;  // k-group pairs per tile
-  const int64_t NI = (int64_t)n_tiles * GP;
-  if (NI <= 0) return;
-  const int64_t P = min((int64_t)a.P, NI);
-  const int64_t c = blockIdx.x;
-  if (c >= P) return;
-  const int64_t b0 = c * NI / P, b1 = (c + 1) * NI / P;
-  auto cta_of = [&](int64_t i) -> int64_t { return ((i + 1) * P - 1) / NI; };
-  auto begin_of = [&](int64_t cc) -> int64_t { return cc * NI / P; };
-  // Items are walked with 32-bit counters: (tile0, gp0) is the first item.
-  const int n_items = (int)(b1 - b0);
-  const int tile0 = (int)(b0 / GP), gp0 = (int)(b0 - (int64_t)tile0 * GP);
-  const int tile_last = (int)((b1 - 1) / GP);
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2 * SA; ++s) {
       mbar_init(smem_u32(&a_full[s]), 4 * kKSplit);  // the dequant warps of one matrix
@@ -692,7 +677,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == kWgtWarp) {
+  // Programmatic dependent launch: everything above runs while the previous
+  // kernel of the stream finishes.  The gate/up phase reads the routing plan
+  // and the staged tokens of the prep kernel, so it waits here, then lets the
+  // down phase launch.  A down phase that follows a gate/up launch (a.early)
+  // needs only the plan for its weight and dequant pipeline -- the plan was
+  // complete and visible before that gate/up launch let it start -- and its
+  // token producer waits for the gate/up results itself; any other launch
+  // waits here for its predecessor.
+  if (KIND == KIND_GATEUP || !a.early) griddep_wait();
+  if (KIND == KIND_GATEUP) griddep_launch_dependents();
+  const int n_segs = *a.n_segs;
+  const int n_tiles = a.n_rt * n_segs;
+  const int GP = (a.G + 1) >> 1;  // k-group pairs per tile
+  const int64_t NI = (int64_t)n_tiles * GP;
+  const int64_t P = min((int64_t)a.P, NI);
+  const int64_t c = blockIdx.x;
+  const int64_t b0 = c * NI / P, b1 = (c + 1) * NI / P;
+  auto cta_of = [&](int64_t i) -> int64_t { return ((i + 1) * P - 1) / NI; };
+  auto begin_of = [&](int64_t cc) -> int64_t { return cc * NI / P; };
+  // Items are walked with 32-bit counters: (tile0, gp0) is the first item.
+  const int n_items = (int)(b1 - b0);
+  const int tile0 = (int)(b0 / GP), gp0 = (int)(b0 - (int64_t)tile0 * GP);
+  const int tile_last = (int)((b1 - 1) / GP);
+
+  const bool active = NI > 0 && c < P;
+
+  if (!active) {
+    // no work for this CTA: straight to the teardown
+  } else if (warp == kWgtWarp) {
     // ------------------------- weight producer (2-D TMA) -------------------------
     if (lane == 0) {
       const uint64_t pol = l2_evict_first_policy();
@@ -730,6 +743,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       // zero-filled.
       Ring<SB> rb;
       if (lane == 0) {
+        griddep_wait();  // the staged rows are the previous kernel's output
         for (int i = 0; i < n_items; ++i) {
           int seg, rt;
           TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
@@ -1127,8 +1141,19 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
     HN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  kern<<<e.P, kTcThreads, L::kTotal, s>>>(e);
-  HN_CUDA(cudaGetLastError());
+  // Programmatic stream serialisation: the launch may start while the
+  // previous kernel of the stream finishes (see griddep_wait in the kernel).
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)e.P);
+  cfg.blockDim = dim3((unsigned)kTcThreads);
+  cfg.dynamicSmemBytes = L::kTotal;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  HN_CUDA(cudaLaunchKernelEx(&cfg, kern, e));
   return HN_OK;
 }
 
@@ -1447,6 +1472,7 @@ static int run_moe(const MoECall& m) {
   e2.part = plan.part2;
   e2.tile_ctr = plan.ctr2;
   e2.rt_ctr = plan.rtctr;
+  e2.early = 1;
   if (combine) return launch_engine<Tr, KIND_DOWN, EPI_COMBINE>(nt, e2, m.stream);
   return launch_engine<Tr, KIND_DOWN, EPI_STORE>(nt, e2, m.stream);
 }
