@@ -168,6 +168,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   return false;
 }
 
+// Bounded wait for a partner that is usually far away (an epilogue waiting
+// for the end of a piece): poll, then sleep sleep_ns between polls, so the
+// waiting warp takes almost no issue slots from the warps of its SMSP.
+// Reads *err every 64 polls; same time limit and error reporting as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_backoff(uint32_t bar, uint32_t parity, int* err, uint32_t sleep_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (err && ld_volatile_s32(err) != 0) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+  }
+  if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);
+  return false;
+}
+
 // Programmatic dependent launch: griddepcontrol.wait blocks until the
 // preceding grid of the stream has completed and its memory is visible (it
 // returns at once when the launch had no programmatic dependency);

@@ -111,7 +111,8 @@ struct RouteArgs {
   float* out_w;
   float* out_logits;
   int seg;
-  int wbuf_off;  // byte offset of the router-weight chunk in dynamic shared memory
+  int wbuf_off;    // byte offset of the router-weight chunk in dynamic shared memory
+  int plan_here;   // 1: the last CTA builds the plan; 0: plan_kernel runs after this kernel
   Plan plan;
 };
 
@@ -359,7 +360,9 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
     if (a.out_w) a.out_w[(int64_t)t * a.K + tid] = s_w[tid];
   }
 
-  // 3. the last CTA to finish builds the plan
+  // 3. the last CTA to finish builds the plan (small routings; larger ones
+  // are planned by plan_kernel, launched after this kernel)
+  if (!a.plan_here) return;
   __threadfence();
   __syncthreads();
   if (tid == 0) s_last = (atomicAdd(a.plan.route_ctr, 1) == a.T - 1);
@@ -414,6 +417,68 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
         }
         base += __popc(bal);
       }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch plan for large routings (T*K above kPlanSmemEntries): one CTA per
+// expert e.  Each CTA histograms every expert's assignments (so no counters
+// cross CTAs), takes its offset and segment base from the prefix over the
+// experts before it, writes its segments, then lists its assignments in
+// (token, slot) order -- the order the single-CTA builder above produces --
+// with a block scan over contiguous per-thread chunks of the routing.
+// ---------------------------------------------------------------------------
+struct PlanArgs {
+  int T, K, E, seg;
+  Plan plan;
+};
+
+__global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
+  extern __shared__ int psm[];
+  int* cnt = psm;  // [E]
+  __shared__ int s_scan[256];
+  __shared__ int s_base[2];  // assignment offset, segment offset of this expert
+  const int e = blockIdx.x, tid = threadIdx.x;
+  const int64_t TK = (int64_t)a.T * a.K;
+  for (int i = tid; i < a.E; i += 256) cnt[i] = 0;
+  __syncthreads();
+  for (int64_t i = tid; i < TK; i += 256) atomicAdd(&cnt[__ldcg(a.plan.idx + i)], 1);
+  __syncthreads();
+  if (tid == 0) {
+    int o = 0, ns = 0;
+    for (int x = 0; x < e; ++x) {
+      o += cnt[x];
+      ns += (cnt[x] + a.seg - 1) / a.seg;
+    }
+    s_base[0] = o;
+    s_base[1] = ns;
+    const int m = cnt[e];
+    for (int j = 0; j < m; j += a.seg) a.plan.segs[ns++] = make_int4(e, o + j, min(a.seg, m - j), 0);
+    a.plan.counts[e] = m;
+    if (e == a.E - 1) *a.plan.n_segs = ns;
+  }
+  // this thread's chunk of the routing, in (token, slot) order
+  const int64_t per = (TK + 255) / 256, lo = min(TK, tid * per), hi = min(TK, lo + per);
+  int c = 0;
+  for (int64_t i = lo; i < hi; ++i) c += __ldcg(a.plan.idx + i) == e;
+  s_scan[tid] = c;
+  __syncthreads();
+  // exclusive scan of the 256 chunk counts (Hillis-Steele in shared memory)
+  for (int d = 1; d < 256; d <<= 1) {
+    const int v = tid >= d ? s_scan[tid - d] : 0;
+    __syncthreads();
+    s_scan[tid] += v;
+    __syncthreads();
+  }
+  int p = s_base[0] + s_scan[tid] - c;
+  for (int64_t i = lo; i < hi; ++i) {
+    if (__ldcg(a.plan.idx + i) == e) {
+      a.plan.pos[i] = p;
+      a.plan.a_tok[p] = (int)(i / a.K);
+      a.plan.a_tk[p] = (int)i;
+      a.plan.a_w[p] = __ldcg(a.plan.wts + i);
+      ++p;
     }
   }
 }
@@ -487,7 +552,7 @@ struct TileMap {
 //     (8 token rows).
 template <int N, int ST, int SB>
 struct TcSmem {
-  static constexpr int kHdr = 1024;
+  static constexpr int kHdr = N <= 32 ? 1024 : 2048;  // barriers + per-token flags of the combine
   static constexpr int kWStage = 32768;
   static constexpr int kW = ST * kWStage;
   static constexpr int kBStage = 2 * N * 128;  // a multiple of 1024: stages stay swizzle-aligned
@@ -511,16 +576,18 @@ constexpr int kTcThreads = (kTokWarp + 4) * 32;
 static_assert(kTokWarp % 4 == 0, "the four role warps must sit on the four SMSPs");
 
 // TMEM columns: SA weight stages of {A0, A1} x 64 columns (128 k as float16
-// pairs) from column 0, then two tile accumulators of {A0, A1} x N fp32
-// columns (the MMA fills one while the epilogue drains the other).
-// N = 16: 3 x 128 + 2 x 32; N = 32: 3 x 128 + 2 x 64.
+// pairs) from column 0, then SD piece accumulators of {A0, A1} x N fp32
+// columns (with two, the MMA fills one while the epilogue drains the other).
+// N = 16: 3 x 128 + 2 x 32; N = 32: 3 x 128 + 2 x 64; N = 64: 2 x 128 +
+// 2 x 128; N = 128: 2 x 128 + 1 x 256.
 template <int N>
 struct TmemPlan {
   static constexpr int kDCols = 2 * N;
-  static constexpr int kFit = (kTmemCols - 2 * kDCols) / 128;
+  static constexpr int SD = (2 * kDCols + 2 * 128 <= kTmemCols) ? 2 : 1;
+  static constexpr int kFit = (kTmemCols - SD * kDCols) / 128;
   static constexpr int SA = kFit > 4 ? 4 : kFit;
   static constexpr int kD0 = SA * 128;
-  static_assert(SA >= 2 && kD0 + 2 * kDCols <= kTmemCols, "TMEM plan exceeds 512 columns");
+  static_assert(SA >= 2 && kD0 + SD * kDCols <= kTmemCols, "TMEM plan exceeds 512 columns");
 };
 
 // Segment, row tile, token count and first assignment of a tile.
@@ -622,12 +689,13 @@ struct Ring {
 template <typename Tr, int N, int KIND, int EPI, int ST, int SB>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_constant__ EngineArgs a) {
   using L = TcSmem<N, ST, SB>;
-  constexpr int SA = TmemPlan<N>::SA, D0 = TmemPlan<N>::kD0, DC = TmemPlan<N>::kDCols;
+  constexpr int SA = TmemPlan<N>::SA, SD = TmemPlan<N>::SD, D0 = TmemPlan<N>::kD0, DC = TmemPlan<N>::kDCols;
   // The token producer signals stage k after issuing group k + LOOK (its
   // copies then had LOOK groups of time to land); issuing k + LOOK needs the
   // MMA of k + LOOK - SB to be done, so SB - LOOK groups of slack remain.
-  constexpr int LOOK = 3;
-  static_assert(LOOK >= 1 && SB - LOOK >= 4 && SA <= 4 && SB <= 16 && ST <= 8, "stage counts");
+  constexpr int LOOK = N <= 32 ? 3 : 2;
+  static_assert(LOOK >= 1 && SB - LOOK >= 2 && SA <= 4 && SB <= 16 && ST <= 8 && N % 16 == 0 && N <= 128,
+                "stage counts");
   constexpr uint32_t IDESC = umma_idesc<F16, 128, N>();
   constexpr uint32_t kDescHiSW128 = (1024u >> 4) | (1u << 14) | (2u << 29);  // SBO 1024 B, version 1, SWIZZLE_128B
   extern __shared__ uint8_t smem_raw[];
@@ -635,8 +703,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   uint64_t* a_full = bars;        // [SA][2] dequant warps of matrix j -> its MMA warp
   uint64_t* a_empty = bars + 8;   // [SA][2] MMA commit (matrix j) -> its dequant warps
-  uint64_t* d_full = bars + 16;   // [2] both MMA warps' commits at a piece end -> epilogue warps
-  uint64_t* d_empty = bars + 20;  // [2] epilogue warps -> MMA warps
+  uint64_t* d_full = bars + 16;   // [SD] both MMA warps' commits at a piece end -> epilogue warps
+  uint64_t* d_empty = bars + 20;  // [SD] epilogue warps -> MMA warps
   uint64_t* b_full = bars + 24;   // [SB] token producer -> MMA warps
   uint64_t* b_empty = bars + 40;  // [SB] both MMA warps' commits -> token producer
   uint64_t* w_full = bars + 56;   // [ST] weight TMA -> dequant warps
@@ -652,7 +720,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       mbar_init(smem_u32(&a_full[s]), 4 * kKSplit);  // the dequant warps of one matrix
       mbar_init(smem_u32(&a_empty[s]), 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < SD; ++s) {
       mbar_init(smem_u32(&d_full[s]), 2);
       mbar_init(smem_u32(&d_empty[s]), kEpiWarps);
     }
@@ -767,30 +835,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       }
       __syncwarp();
     } else {
-      // Gathered tokens: lane l copies token l of the segment with cp.async
-      // into the swizzled rows; a stage is signalled (after its copies landed
-      // and a proxy fence) LOOK groups later.
+      // Gathered tokens: lane l copies tokens l, l+32, ... of the segment with
+      // cp.async into the swizzled rows; a stage is signalled (after its
+      // copies landed and a proxy fence) LOOK groups later.
+      constexpr int TPL = (N + 31) / 32;  // tokens per lane
       Ring<SB> rb, rs;  // rb: stage being filled; rs: next stage to signal (LOOK behind)
       for (int i = 0; i < n_items; ++i) {
         int seg, rt;
         TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
         const int4 sg = a.segs[seg];
-        const uint8_t* src_tok = nullptr;
-        if (lane < sg.z) {
-          const int row = a.b_use_tok ? a.a_tok[sg.y + lane] : sg.y + lane;
-          src_tok = a.bsrc + (int64_t)row * a.b_rstride;
+        const uint8_t* src_tok[TPL];
+#pragma unroll
+        for (int q = 0; q < TPL; ++q) {
+          const int tk = lane + 32 * q;
+          src_tok[q] = nullptr;
+          if (tk < sg.z) {
+            const int row = a.b_use_tok ? a.a_tok[sg.y + tk] : sg.y + tk;
+            src_tok[q] = a.bsrc + (int64_t)row * a.b_rstride;
+          }
         }
         const int ng = min(2, a.G - 2 * gp);
         for (int gi = 0; gi < ng; ++gi, ++k) {
           const int grp = 2 * gp + gi;
           mbar_wait(smem_u32(&b_empty[rb.idx]), rb.phase ^ 1u, a.err);
-          if (src_tok) {
-            const uint32_t dst = smem_u32(bst + rb.idx * L::kBStage + lane * 128);
-            const uint8_t* src = src_tok + (int64_t)grp * kChunk;
-            const int sw = lane & 7;
 #pragma unroll
-            for (int u = 0; u < 16; ++u)
-              cp_async16(dst + (u >> 3) * (N * 128) + (((u & 7) ^ sw) << 4), src + u * 16);
+          for (int q = 0; q < TPL; ++q) {
+            if (src_tok[q]) {
+              const int tk = lane + 32 * q;
+              const uint32_t dst = smem_u32(bst + rb.idx * L::kBStage + tk * 128);
+              const uint8_t* src = src_tok[q] + (int64_t)grp * kChunk;
+              const int sw = tk & 7;
+#pragma unroll
+              for (int u = 0; u < 16; ++u)
+                cp_async16(dst + (u >> 3) * (N * 128) + (((u & 7) ^ sw) << 4), src + u * 16);
+            }
           }
           cp_async_commit();
           rb.next();
@@ -820,7 +898,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     const int mj = warp == kMmaWarp0 ? 0 : 1;
     Ring<SA> ra;
     Ring<SB> rb;
-    Ring<2> rd;
+    Ring<SD> rd;
     int gp = gp0;
     uint32_t acc = 0;  // 0: the next group starts a piece (overwrites the accumulator)
     for (int i = 0; i < n_items; ++i) {
@@ -1011,13 +1089,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         }
       }
     };
-    Ring<2> rd;
+    Ring<SD> rd;
 #pragma unroll 1
     for (int tile = tile0; tile <= tile_last; ++tile) {
       const TileInfo ti = tile_info<KIND>(a, tile, n_segs);
       const int64_t ts = (int64_t)tile * GP, te = ts + GP;
       const uint32_t dcol = tlane + D0 + rd.idx * DC;
-      mbar_wait(smem_u32(&d_full[rd.idx]), rd.phase, a.err);
+      mbar_wait_backoff(smem_u32(&d_full[rd.idx]), rd.phase, a.err, 256);
       tc_fence_after();
       bool own = true;
       if (b0 <= ts && b1 >= te) {
@@ -1110,14 +1188,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-// Tokens per segment = N of the MMA (16 or 32); 8*nt with nt in {2, 4}.
-static int pick_nt(int64_t max_tokens_per_expert) { return max_tokens_per_expert <= 16 ? 2 : 4; }
+// Tokens per segment = N of the MMA, 8*nt: 16 or 32 for decode-size steps
+// (T <= 64); for larger steps by the mean assignments per expert, T*K/E, up
+// to 128 (prefill), so each dequantised weight tile serves more tokens.
+static int pick_nt(int64_t T, int64_t K, int64_t E) {
+  if (T <= 16) return 2;
+  if (T <= 64) return 4;
+  const int64_t avg = T * K / std::max<int64_t>(E, 1);
+  if (avg >= 96) return 16;
+  if (avg >= 48) return 8;
+  return 4;
+}
 
 // Weight stages (32 KB each) and token stages per tile width N; the totals
 // stay within 227 KB of shared memory.
 template <int N>
 struct TcTune {
-  static constexpr int ST = 5, SB = 8;
+  static constexpr int ST = N <= 32 ? 5 : (N == 64 ? 4 : 3);
+  static constexpr int SB = N <= 32 ? 8 : (N == 64 ? 5 : 4);
 };
 
 static int encode_token_map(CUtensorMap* data, const void* base, int64_t rows, int64_t row_bytes, int box_rows);
@@ -1160,7 +1248,9 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
 template <typename Tr, int KIND, int EPI>
 static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
   if (nt <= 2) return launch_engine_t<Tr, 16, KIND, EPI>(a, s);
-  return launch_engine_t<Tr, 32, KIND, EPI>(a, s);
+  if (nt <= 4) return launch_engine_t<Tr, 32, KIND, EPI>(a, s);
+  if (nt <= 8) return launch_engine_t<Tr, 64, KIND, EPI>(a, s);
+  return launch_engine_t<Tr, 128, KIND, EPI>(a, s);
 }
 
 // A workspace has a counter section at its FRONT and a data section at its
@@ -1274,8 +1364,15 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   HN_REQUIRE(sm <= 227 * 1024, "router: hidden size too large for the shared-memory plan");
   if (sm > 48 * 1024)
     HN_CUDA(cudaFuncSetAttribute(route_prep_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  r.plan_here = TK <= kPlanSmemEntries;
   route_prep_kernel<Tr><<<ra.T, 256, sm, s>>>(r);
   HN_CUDA(cudaGetLastError());
+  if (!r.plan_here) {
+    HN_REQUIRE(ra.E <= kMaxExperts, "too many experts for the plan kernel");
+    PlanArgs pa{ra.T, ra.K, ra.E, ra.seg, ra.plan};
+    plan_kernel<<<ra.E, 256, (size_t)ra.E * 4, s>>>(pa);
+    HN_CUDA(cudaGetLastError());
+  }
   return HN_OK;
 }
 
@@ -1385,7 +1482,7 @@ struct MoECall {
 template <typename Tr>
 static int run_moe(const MoECall& m) {
   const int64_t TK = m.T * m.topk;
-  const int nt = pick_nt(std::min<int64_t>(m.T, TK));
+  const int nt = pick_nt(m.T, m.topk, m.E);
   const int P = grid_p(nt);
   // routed calls always scale by the routing weight and combine; the identity
   // plan of a single expert MLP stores rows directly
@@ -1501,19 +1598,19 @@ extern "C" {
 
 size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int top_k) {
   if (T < 1 || H < 128 || F < 128 || E < 1 || top_k < 1) return 0;
-  const int nt = pick_nt(std::min<int64_t>(T, T * top_k));
+  const int nt = pick_nt(T, top_k, E);
   return make_layout(T, H, E, top_k, F, H, nt, grid_p(nt), true).total() + 256;
 }
 
 size_t hn_expert_mlp_workspace_size(int64_t T, int64_t H, int64_t F) {
   if (T < 1 || H < 128 || F < 128) return 0;
-  const int nt = pick_nt(T);
+  const int nt = pick_nt(T, 1, 1);
   return make_layout(T, H, 1, 1, F, H, nt, grid_p(nt), false).total() + 256;
 }
 
 size_t hn_int4_linear_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M < 1 || N < 1 || K < 128) return 0;
-  const int nt = pick_nt(M);
+  const int nt = pick_nt(M, 1, 1);
   return make_layout(M, K, 1, 1, 0, N, nt, grid_p(nt), false).total() + 256;
 }
 
@@ -1678,7 +1775,7 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   HN_REQUIRE(((uintptr_t)w_packed & 15) == 0, "int4_linear: packed weights must be 16-byte aligned");
   HN_REQUIRE(ldx >= K && ldo >= N, "int4_linear: bad row stride");
   HN_REQUIRE(x && w_packed && w_scales && out && workspace, "int4_linear: null pointer");
-  const int nt = pick_nt(M);
+  const int nt = pick_nt(M, 1, 1);
   const int P = grid_p(nt);
   const Layout l = make_layout(M, K, 1, 1, 0, N, nt, P, false);
   int rc0 = check_ws(workspace, workspace_bytes, l);

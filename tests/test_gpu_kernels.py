@@ -2,9 +2,11 @@
 
 Contract (north star): rel-L2 <= 1e-2 against the reference's
 dequant-then-matmul path with float32 accumulation.  A tighter bound is also
-asserted: weights enter the MMA as exact integers and the group scale is
-applied in fp32, so the only sizeable error is the final rounding to the
-activation dtype (and, in the MLP, of the SiLU*up intermediate).
+asserted: weights enter the MMA as the float16 (n - 8) * scale the reference
+dequantiser produces, tokens as float16 and products accumulate in fp32, so
+the sizeable errors are the roundings of the activations to float16 and of
+the result to the activation dtype (and, in the MLP, of the SiLU*up
+intermediate, kept as float16).
 """
 
 import numpy as np
