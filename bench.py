@@ -60,6 +60,73 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+# Config 5: one GLM-4.5-Air MoE layer, prefill (tensor-core bound).
+P_T, P_H, P_F, P_E, P_K = 8192, 4096, 1408, 128, 8
+
+
+def prefill_measure(args, dev):
+    """Config 5 on this GPU: GLM-4.5-Air-shape MoE layer (H 4096, moe_ffn 1408,
+    128 experts, sigmoid top-8 with correction bias), 8192 bf16 tokens.  Device
+    time per layer step with CUDA events (eager launches; the step's prep,
+    planner and two engine launches), FLOPs 2 * T * k * 3 * H * F, against the
+    measured bf16 dense peak; per-phase times with events between phases."""
+    import torch
+    from hydranet_b200 import synth
+    from hydranet_b200.moe import MoELayerInt4
+    from hydranet_b200.packing import ExpertTable
+    from hydranet_b200.router import GLM4SigmoidRouter
+
+    shape = synth.MoEShape(P_H, P_F, P_E, P_K)
+    table = ExpertTable(synth.device_experts(4321, shape, dev))
+    r = GLM4SigmoidRouter(hidden_dim=P_H, num_experts=P_E, experts_per_token=P_K).to(dev)
+    r.set_correction_bias(torch.from_numpy(synth.host_correction_bias(3, P_E)).to(dev))
+    layer = MoELayerInt4(r, table).eval()
+    x = torch.randn(P_T, P_H, generator=torch.Generator(dev).manual_seed(5), device=dev).to(torch.bfloat16)
+    steps = max(3, min(args.steps, 20))
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            layer(x)
+        torch.cuda.synchronize(dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index or 0) as clk:
+            ev0.record(stream)
+            for _ in range(steps):
+                layer(x)
+            ev1.record(stream)
+            torch.cuda.synchronize(dev)
+        ms = ev0.elapsed_time(ev1) / steps
+        evs = []
+
+        def mark(phase):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            evs[-1].append(ev)
+
+        for _ in range(steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            evs.append([e0])
+            layer.forward_phases(x, between=mark)
+            e3 = torch.cuda.Event(enable_timing=True)
+            e3.record(stream)
+            evs[-1].append(e3)
+        torch.cuda.synchronize(dev)
+    phase = {k: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs)
+             for i, k in enumerate(("route_ms", "gateup_ms", "down_ms"))}
+    flops = 2.0 * P_T * P_K * 3 * P_H * P_F
+    _, tc_peak, peak_kind = peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    del layer, table
+    torch.cuda.empty_cache()
+    return {"workload": "glm45air_moe_layer_prefill", "tokens": P_T, "hidden": P_H, "ffn": P_F, "experts": P_E,
+            "top_k": P_K, "router": "sigmoid top-8, correction bias", "steps": steps, "warmup": args.warmup,
+            "ms_per_step": ms, "tok_s": P_T / (ms * 1e-3),
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": tc_peak, "unit": "TFLOP/s", "frac": tf / tc_peak,
+                         "peak_kind": peak_kind, "flops_per_step": flops},
+            "phases": phase, "clocks": clk.summary()}
+
+
 # DRAM bytes (read + write) of one gate/up engine launch, from the ncu capture
 # summarised in profiles/ (per launch, same workload); None where not captured.
 GATEUP_TRAFFIC = {64: 503473408}
@@ -241,6 +308,7 @@ def main():
     ap.add_argument("--sweep", type=str, default=",".join(map(str, SWEEP)),
                     help="comma-separated token batches to time (default 1,8,32,64)")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="distinct layers rotated per step")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-5 prefill measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -443,6 +511,10 @@ def main():
                "sample": f"{n} oracle layer steps at T={T} in {el:.1f}s (numpy float32 dequant-then-matmul, "
                          f"dequantisation done before timing)"}
 
+    prefill = None
+    if rank == 0 and world == 1 and not args.no_prefill:
+        prefill = prefill_measure(args, dev)
+
     if rank == 0:
         hr = results[T]
         line = {
@@ -466,6 +538,7 @@ def main():
             "gpu_launches": (3 if not ep else 5) * args.steps,
             "clocks": hr["clocks"],
             "cpu_baseline": cpu,
+            "prefill": prefill,
             "sweep": {str(t): {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items() if k != "clocks"}
                       for t, r in results.items()},
         }

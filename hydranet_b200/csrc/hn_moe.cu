@@ -56,6 +56,7 @@ struct Plan {
   float* part1;  // stream-K partial tiles, phase 1
   float* part2;  // stream-K partial tiles, phase 2
   float* R;      // [T*K][H] weighted expert outputs (EPI_COMBINE)
+  float* rlog;   // [T][E] router logits of a large batch (router_logits_kernel), or NULL
   int* ctr1;     // per phase-1 tile arrival counters
   int* ctr2;     // per phase-2 tile arrival counters
   int* rtctr;    // [row tiles][T] contributions summed into (row tile, token) so far
@@ -111,6 +112,7 @@ struct RouteArgs {
   float* out_w;
   float* out_logits;
   int seg;
+  const float* pre_logits;  // [T][E] router logits from router_logits_kernel, or NULL: computed here
   int wbuf_off;    // byte offset of the router-weight chunk in dynamic shared memory
   int plan_here;   // 1: the last CTA builds the plan; 0: plan_kernel runs after this kernel
   Plan plan;
@@ -151,7 +153,7 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   const typename Tr::T* xrow = reinterpret_cast<const typename Tr::T*>(a.x) + (int64_t)t * a.ldx;
   const int esz = route_esize(a.rw_dtype);
   const int CE = route_chunk_experts(a.H, a.E, a.rw_dtype);
-  const bool bulk = a.mode == ROUTE_COMPUTE && (reinterpret_cast<uintptr_t>(a.rw) & 15) == 0;
+  const bool bulk = a.mode == ROUTE_COMPUTE && !a.pre_logits && (reinterpret_cast<uintptr_t>(a.rw) & 15) == 0;
   uint8_t* wbuf = reinterpret_cast<uint8_t*>(rsm) + a.wbuf_off;
   if (bulk && tid == 0) {
     mbar_init(smem_u32(&s_wbar), 1);
@@ -189,8 +191,16 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
 
   // 2. routing for this token
   if (a.mode == ROUTE_COMPUTE) {
+    if (a.pre_logits) {
+      // logits of a large batch come from router_logits_kernel
+      for (int e = tid; e < a.E; e += 256) {
+        const float v = __ldg(a.pre_logits + (int64_t)t * a.E + e);
+        lg[e] = a.logits_act ? Tr::to_f(Tr::from_f(v)) : v;
+      }
+      __syncthreads();
+    }
     // router logits, one warp per expert row of the chunk in shared memory
-    for (int c0 = 0; c0 < a.E; c0 += CE) {
+    for (int c0 = 0; c0 < (a.pre_logits ? 0 : a.E); c0 += CE) {
       const int ce = min(CE, a.E - c0);
       if (bulk) mbar_wait(smem_u32(&s_wbar), (uint32_t)((c0 / CE) & 1), a.plan.err);
       for (int r = warp; r < ce; r += 8) {
@@ -417,6 +427,65 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
         }
         base += __popc(bal);
       }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Router logits of a large batch, logits[t, e] = sum_h x[t, h] * W[e, h] in
+// fp32 (the reference's `F.linear(h.float(), W.float())`, model/glm4.py:279;
+// the Mixtral gate's model-dtype rounding is applied by the prep kernel).
+// One CTA computes a 64-token x 64-expert tile, each thread 4 x 4 outputs,
+// over 32-wide chunks of h staged in shared memory; every output sums h in
+// order, so the result does not depend on the launch shape.  The per-token
+// path in route_prep_kernel reads the whole router matrix once per token,
+// which is what a batch of thousands of tokens cannot afford.
+// ---------------------------------------------------------------------------
+constexpr int kRgM = 64, kRgN = 64, kRgK = 32;
+constexpr int kRouterGemmMinT = 256;  // batches from this size route through router_logits_kernel
+
+template <typename Tr>
+__global__ void __launch_bounds__(256) router_logits_kernel(const void* x, int64_t ldx, int T, int H, int E,
+                                                            const void* rw, int rw_dtype, float* out) {
+  __shared__ __align__(16) float xs[kRgK][kRgM + 4];  // [k][token]
+  __shared__ __align__(16) float ws[kRgK][kRgN + 4];  // [k][expert]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int t0 = blockIdx.x * kRgM, e0 = blockIdx.y * kRgN;
+  const typename Tr::T* xp = reinterpret_cast<const typename Tr::T*>(x);
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < H; k0 += kRgK) {
+    for (int i = tid; i < kRgM * kRgK; i += 256) {
+      const int tt = i / kRgK, kk = i - tt * kRgK, t = t0 + tt;
+      xs[kk][tt] = t < T ? Tr::to_f(xp[(int64_t)t * ldx + k0 + kk]) : 0.f;
+    }
+    for (int i = tid; i < kRgN * kRgK; i += 256) {
+      const int ee = i / kRgK, kk = i - ee * kRgK, e = e0 + ee;
+      ws[kk][ee] = e < E ? load_any(rw, rw_dtype, (int64_t)e * H + k0 + kk) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kRgK; ++kk) {
+      const float4 av = *reinterpret_cast<const float4*>(&xs[kk][ty * 4]);
+      const float4 bv = *reinterpret_cast<const float4*>(&ws[kk][tx * 4]);
+      const float a4[4] = {av.x, av.y, av.z, av.w}, b4[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a4[i], b4[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + ty * 4 + i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e0 + tx * 4 + j;
+      if (t < T && e < E) out[(int64_t)t * E + e] = acc[i][j];
     }
   }
 }
@@ -1264,7 +1333,8 @@ static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
 // call, because another shape's data section may have covered them.
 struct Layout {
   size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
-  size_t counts, n_segs, segs, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, part1, part2, R, data;  // back (relative)
+  size_t counts, n_segs, segs, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, part1, part2, R, rlog, data;  // back (relative)
+  bool has_rlog;
   size_t total() const { return counters + data; }
 };
 
@@ -1307,6 +1377,8 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.part1 = take(F ? part : 0);
   l.part2 = take(part);
   l.R = take(combine ? (size_t)TK * N2 * 4 : 0);
+  l.has_rlog = T >= kRouterGemmMinT;
+  l.rlog = take(l.has_rlog ? (size_t)T * E * 4 : 0);
   l.data = o;
   return l;
 }
@@ -1335,6 +1407,7 @@ static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
   p.part1 = reinterpret_cast<float*>(d + l.part1);
   p.part2 = reinterpret_cast<float*>(d + l.part2);
   p.R = reinterpret_cast<float*>(d + l.R);
+  p.rlog = l.has_rlog ? reinterpret_cast<float*>(d + l.rlog) : nullptr;
   return p;
 }
 
@@ -1360,11 +1433,19 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   sm = std::max(sm, (size_t)(2 * ra.E) * 4);
   sm = (sm + 15) & ~(size_t)15;
   r.wbuf_off = (int)sm;
-  if (ra.mode == ROUTE_COMPUTE) sm += (size_t)route_chunk_experts(ra.H, ra.E, ra.rw_dtype) * ra.H * route_esize(ra.rw_dtype);
+  const bool gemm = ra.mode == ROUTE_COMPUTE && ra.T >= kRouterGemmMinT && ra.plan.rlog;
+  if (ra.mode == ROUTE_COMPUTE && !gemm)
+    sm += (size_t)route_chunk_experts(ra.H, ra.E, ra.rw_dtype) * ra.H * route_esize(ra.rw_dtype);
   HN_REQUIRE(sm <= 227 * 1024, "router: hidden size too large for the shared-memory plan");
   if (sm > 48 * 1024)
     HN_CUDA(cudaFuncSetAttribute(route_prep_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   r.plan_here = TK <= kPlanSmemEntries;
+  if (gemm) {
+    router_logits_kernel<Tr><<<dim3((unsigned)((ra.T + kRgM - 1) / kRgM), (unsigned)((ra.E + kRgN - 1) / kRgN)), 256, 0, s>>>(
+        ra.x, ra.ldx, ra.T, ra.H, ra.E, ra.rw, ra.rw_dtype, ra.plan.rlog);
+    HN_CUDA(cudaGetLastError());
+    r.pre_logits = ra.plan.rlog;
+  }
   route_prep_kernel<Tr><<<ra.T, 256, sm, s>>>(r);
   HN_CUDA(cudaGetLastError());
   if (!r.plan_here) {
