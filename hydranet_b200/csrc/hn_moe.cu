@@ -594,6 +594,7 @@ struct EngineArgs {
   int* err;
   int P;
   int early;  // KIND_DOWN after a gate/up launch: only the token producer waits for it
+  int defer_combine;  // EPI_COMBINE: leave the top-k sum to combine_kernel (large routings)
 };
 
 template <int KIND>
@@ -1241,7 +1242,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
           if (et == 0) a.tile_ctr[tile] = 0;
         }
       }
-      if (KIND == KIND_DOWN && EPI == EPI_COMBINE && own) combine(ti);
+      if (KIND == KIND_DOWN && EPI == EPI_COMBINE && own && !a.defer_combine) combine(ti);
       rd.next();
     }
   }
@@ -1251,6 +1252,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   if (warp == kMmaWarp0) {
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Top-k combine of a large routing: out[t, :] = sum over slots k, in slot
+// order, of R[t*K + k, :] (each row already scaled by its routing weight), in
+// fp32, stored in the activation dtype.  Bandwidth-bound: one pass over R.
+// Decode-size routings combine inside the down-phase epilogue instead.
+// ---------------------------------------------------------------------------
+template <typename Tr>
+__global__ void __launch_bounds__(256) combine_kernel(const float* R, int T, int K, int H, void* out, int64_t ldo) {
+  const int64_t n4 = (int64_t)T * (H / 4);
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n4; i += (int64_t)gridDim.x * 256) {
+    const int t = (int)(i / (H / 4)), h = (int)(i - (int64_t)t * (H / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < K; ++k) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(R + ((int64_t)t * K + k) * H + h));
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    typename Tr::T* o = reinterpret_cast<typename Tr::T*>(out) + (int64_t)t * ldo + h;
+    o[0] = Tr::from_f(acc.x);
+    o[1] = Tr::from_f(acc.y);
+    o[2] = Tr::from_f(acc.z);
+    o[3] = Tr::from_f(acc.w);
   }
 }
 
@@ -1651,8 +1679,17 @@ static int run_moe(const MoECall& m) {
   e2.tile_ctr = plan.ctr2;
   e2.rt_ctr = plan.rtctr;
   e2.early = 1;
-  if (combine) return launch_engine<Tr, KIND_DOWN, EPI_COMBINE>(nt, e2, m.stream);
-  return launch_engine<Tr, KIND_DOWN, EPI_STORE>(nt, e2, m.stream);
+  if (!combine) return launch_engine<Tr, KIND_DOWN, EPI_STORE>(nt, e2, m.stream);
+  // large routings: the epilogue only writes the weighted rows, one
+  // bandwidth-bound pass sums them afterwards
+  e2.defer_combine = TK > kPlanSmemEntries;
+  rc = launch_engine<Tr, KIND_DOWN, EPI_COMBINE>(nt, e2, m.stream);
+  if (rc || !e2.defer_combine) return rc;
+  const int64_t n4 = m.T * (m.H / 4);
+  const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)grid_p(nt) * 8);
+  combine_kernel<Tr><<<blocks, 256, 0, m.stream>>>(plan.R, (int)m.T, m.topk, (int)m.H, m.out, m.ldo);
+  HN_CUDA(cudaGetLastError());
+  return HN_OK;
 }
 
 static int dispatch_moe(const MoECall& m) {
