@@ -53,6 +53,7 @@ struct Plan {
   float* wts;    // [T*K] top-k weights (rounded to the activation dtype)
   uint8_t* xp;   // [T][K_in/128][kChunk]    staged activations (token-major)
   uint8_t* hp;   // [T*K][F/128][kChunk]     staged SiLU(gate)*up (assignment-major)
+  uint8_t* xs;   // [T*K][K_in/128][kChunk]  staged activations in assignment order (large routings), or NULL
   float* part1;  // stream-K partial tiles, phase 1
   float* part2;  // stream-K partial tiles, phase 2
   float* R;      // [T*K][H] weighted expert outputs (EPI_COMBINE)
@@ -503,6 +504,21 @@ struct PlanArgs {
   Plan plan;
 };
 
+// Gate/up operand of a large routing in assignment order: row p of xs is the
+// staged row of token a_tok[p], so the engine reads each segment as
+// consecutive rows (TMA boxes) instead of gathering token by token.  One
+// warp per row; 8 rows per block.
+__global__ void __launch_bounds__(256) stage_rows_kernel(const int* a_tok, int n_rows, const uint8_t* xp,
+                                                         uint8_t* xs, int64_t row_bytes) {
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= n_rows) return;
+  const int u = (int)(row_bytes / 16);
+  const uint4* src = reinterpret_cast<const uint4*>(xp + (int64_t)a_tok[r] * row_bytes);
+  uint4* dst = reinterpret_cast<uint4*>(xs + (int64_t)r * row_bytes);
+#pragma unroll 4
+  for (int w = lane; w < u; w += 32) dst[w] = __ldcg(src + w);
+}
+
 __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
   extern __shared__ int psm[];
   int* cnt = psm;  // [E]
@@ -797,7 +813,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     for (int s = 0; s < SB; ++s) {
       // KIND_DOWN fills a stage with TMA (one arrival + bytes), KIND_GATEUP
       // with per-lane cp.async (one arrival per lane)
-      mbar_init(smem_u32(&b_full[s]), KIND == KIND_DOWN ? 1 : 32);
+      mbar_init(smem_u32(&b_full[s]), (KIND == KIND_DOWN || !a.b_use_tok) ? 1 : 32);
       mbar_init(smem_u32(&b_empty[s]), 2);
     }
     for (int s = 0; s < ST; ++s) {
@@ -875,7 +891,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   } else if (warp == kTokWarp) {
     // ------------------------- token producer -------------------------
     int k = 0, tile = tile0, gp = gp0;
-    if (KIND == KIND_DOWN) {
+    if (KIND == KIND_DOWN || !a.b_use_tok) {
       // Rows of a segment are consecutive (assignment order): each k-group is
       // two TMA boxes of N rows x 128 B (128B swizzle); rows past the end are
       // zero-filled.
@@ -1315,7 +1331,7 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
   static_assert(L::kTotal <= 227 * 1024, "engine shared memory exceeds the per-CTA limit");
   auto kern = tc_engine_kernel<Tr, N, KIND, EPI, TU::ST, TU::SB>;
   EngineArgs e = a;
-  if (KIND == KIND_DOWN) {
+  if (KIND == KIND_DOWN || !e.b_use_tok) {
     const int rc = encode_token_map(&e.bmap, e.bsrc, e.b_rows, e.b_rstride, N);
     if (rc) return rc;
   }
@@ -1361,8 +1377,8 @@ static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
 // call, because another shape's data section may have covered them.
 struct Layout {
   size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
-  size_t counts, n_segs, segs, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, part1, part2, R, rlog, data;  // back (relative)
-  bool has_rlog;
+  size_t counts, n_segs, segs, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, xs, part1, part2, R, rlog, data;  // back (relative)
+  bool has_rlog, has_xs;
   size_t total() const { return counters + data; }
 };
 
@@ -1401,6 +1417,8 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.wts = take(4 * TK);
   l.xp = take((size_t)(Kin / 128) * T * kChunk);
   l.hp = take(F ? (size_t)(F / 128) * TK * kChunk : 0);
+  l.has_xs = F && combine && TK > kPlanSmemEntries;  // the plan kernel stages routed gate/up tokens in assignment order
+  l.xs = take(l.has_xs ? (size_t)(Kin / 128) * TK * kChunk : 0);
   const size_t part = (size_t)P * 2 * 8 * (8 * nt) * 32 * 4;  // [CTA][2 slots][fold warp][N][32] fp32
   l.part1 = take(F ? part : 0);
   l.part2 = take(part);
@@ -1432,6 +1450,7 @@ static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
   p.wts = reinterpret_cast<float*>(d + l.wts);
   p.xp = d + l.xp;
   p.hp = d + l.hp;
+  p.xs = l.has_xs ? d + l.xs : nullptr;
   p.part1 = reinterpret_cast<float*>(d + l.part1);
   p.part2 = reinterpret_cast<float*>(d + l.part2);
   p.R = reinterpret_cast<float*>(d + l.R);
@@ -1481,6 +1500,11 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
     PlanArgs pa{ra.T, ra.K, ra.E, ra.seg, ra.plan};
     plan_kernel<<<ra.E, 256, (size_t)ra.E * 4, s>>>(pa);
     HN_CUDA(cudaGetLastError());
+    if (ra.plan.xs) {
+      stage_rows_kernel<<<(unsigned)((TK + 7) / 8), 256, 0, s>>>(ra.plan.a_tok, (int)TK, ra.plan.xp, ra.plan.xs,
+                                                                  (int64_t)(ra.H / 128) * kChunk);
+      HN_CUDA(cudaGetLastError());
+    }
   }
   return HN_OK;
 }
@@ -1651,9 +1675,22 @@ static int run_moe(const MoECall& m) {
     rc = encode_expert_maps(&e1.single_maps, m.single, m.H, m.F);
     if (rc) return rc;
   }
-  e1.bsrc = plan.xp;
+  // gate/up tokens: gathered per token from xp, or read as consecutive rows
+  // (TMA) when they are already in assignment order -- the identity plan of
+  // a single expert, or xs staged by the plan kernel of a large routing
   e1.b_rstride = (m.H / 128) * kChunk;
-  e1.b_use_tok = 1;
+  if (m.route_mode == ROUTE_IDENTITY) {
+    e1.bsrc = plan.xp;
+    e1.b_use_tok = 0;
+    e1.b_rows = m.T;
+  } else if (plan.xs) {
+    e1.bsrc = plan.xs;
+    e1.b_use_tok = 0;
+    e1.b_rows = TK;
+  } else {
+    e1.bsrc = plan.xp;
+    e1.b_use_tok = 1;
+  }
   e1.hp = plan.hp;
   e1.hp_rstride = (m.F / 128) * kChunk;
   e1.part = plan.part1;
