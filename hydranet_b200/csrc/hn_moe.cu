@@ -611,13 +611,17 @@ struct EngineArgs {
   int P;
   int early;  // KIND_DOWN after a gate/up launch: only the token producer waits for it
   int defer_combine;  // EPI_COMBINE: leave the top-k sum to combine_kernel (large routings)
+  int allow_rr;       // whole tiles round-robin over the CTAs when there are >= 4 per CTA (prefill sizes)
 };
 
 template <int KIND>
 struct TileMap {
-  // GATEUP tiles are segment-major, DOWN tiles row-tile-major.
-  static __device__ __forceinline__ void split(int tile, int n_rt, int n_segs, int& seg, int& rt) {
-    if (KIND == KIND_GATEUP) {
+  // GATEUP tiles are segment-major; DOWN tiles row-tile-major (a row tile's
+  // segments finish together for the in-kernel combine), or segment-major
+  // when segmaj (round-robin tiles: a wave of CTAs then shares one segment's
+  // tokens and the row tiles of few experts in L2).
+  static __device__ __forceinline__ void split(int tile, int n_rt, int n_segs, int& seg, int& rt, bool segmaj) {
+    if (KIND == KIND_GATEUP || segmaj) {
       seg = tile / n_rt;
       rt = tile - seg * n_rt;
     } else {
@@ -681,18 +685,18 @@ struct TileInfo {
   int seg, rt, m, p0;
 };
 template <int KIND>
-__device__ __forceinline__ TileInfo tile_info(const EngineArgs& a, int tile, int n_segs) {
+__device__ __forceinline__ TileInfo tile_info(const EngineArgs& a, int tile, int n_segs, bool segmaj) {
   TileInfo v;
-  TileMap<KIND>::split(tile, a.n_rt, n_segs, v.seg, v.rt);
+  TileMap<KIND>::split(tile, a.n_rt, n_segs, v.seg, v.rt, segmaj);
   const int4 sg = a.segs[v.seg];
   v.m = sg.z;
   v.p0 = sg.y;
   return v;
 }
 template <int KIND>
-__device__ __forceinline__ int tile_expert(const EngineArgs& a, int tile, int n_segs) {
+__device__ __forceinline__ int tile_expert(const EngineArgs& a, int tile, int n_segs, bool segmaj) {
   int seg, rt;
-  TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+  TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt, segmaj);
   return __ldg(&a.segs[seg].x);
 }
 // Scale matrix of (expert e, matrix j) and the offset of row r's scale row in
@@ -703,9 +707,9 @@ __device__ __forceinline__ const uint16_t* scale_base(const EngineArgs& a, int e
   return KIND == KIND_GATEUP ? (j ? ep->up_scales : ep->gate_scales) : ep->down_scales;
 }
 template <int KIND>
-__device__ __forceinline__ int64_t scale_off(const EngineArgs& a, int tile, int n_segs, int j, int r) {
+__device__ __forceinline__ int64_t scale_off(const EngineArgs& a, int tile, int n_segs, int j, int r, bool segmaj) {
   int seg, rt;
-  TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+  TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt, segmaj);
   const int row = KIND == KIND_GATEUP ? rt * 128 + r : rt * 256 + j * 128 + r;
   return (int64_t)min(row, a.N - 1) * a.G;
 }
@@ -847,13 +851,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   const int64_t NI = (int64_t)n_tiles * GP;
   const int64_t P = min((int64_t)a.P, NI);
   const int64_t c = blockIdx.x;
+  // Stream-K (items [c*NI/P, (c+1)*NI/P), tiles split across CTAs and
+  // finished by the last arriver) balances a handful of tiles; with at least
+  // four tiles per CTA, whole tiles go round-robin (tile c, c+P, ...), so the
+  // CTAs of a wave work on neighbouring tiles and share their data in L2.
+  const bool rr = a.allow_rr && n_tiles >= 4 * P;
+  const int tstep = rr ? (int)P : 1;
   const int64_t b0 = c * NI / P, b1 = (c + 1) * NI / P;
   auto cta_of = [&](int64_t i) -> int64_t { return ((i + 1) * P - 1) / NI; };
   auto begin_of = [&](int64_t cc) -> int64_t { return cc * NI / P; };
   // Items are walked with 32-bit counters: (tile0, gp0) is the first item.
-  const int n_items = (int)(b1 - b0);
-  const int tile0 = (int)(b0 / GP), gp0 = (int)(b0 - (int64_t)tile0 * GP);
-  const int tile_last = (int)((b1 - 1) / GP);
+  const int rr_tiles = rr ? (int)((n_tiles - c + P - 1) / P) : 0;
+  const int n_items = rr ? rr_tiles * GP : (int)(b1 - b0);
+  const int tile0 = rr ? (int)c : (int)(b0 / GP), gp0 = rr ? 0 : (int)(b0 - (int64_t)tile0 * GP);
+  const int tile_last = rr ? (int)c + (rr_tiles - 1) * (int)P : (int)((b1 - 1) / GP);
 
   const bool active = NI > 0 && c < P;
 
@@ -867,23 +878,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       int tile = tile0, gp = gp0;
       for (int i = 0; i < n_items; ++i) {
         int seg, rt;
-        TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+        TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt, rr);
         const int e = a.segs[seg].x;
         const ExpertMaps* em = a.maps ? a.maps + e : &a.single_maps;
         mbar_wait(smem_u32(&w_empty[rw.idx]), rw.phase ^ 1u, a.err);
         const uint32_t bar = smem_u32(&w_full[rw.idx]);
         mbar_arrive_expect_tx(bar, L::kWStage);
         const uint32_t dst = smem_u32(wst + rw.idx * L::kWStage);
+        // decode streams each weight once (evict-first); round-robin tiles
+        // reuse an expert's weights across its segments (default policy)
         if (KIND == KIND_GATEUP) {
-          tma_load_2d_hint(dst, &em->gate, gp * 128, rt * 128, bar, pol);
-          tma_load_2d_hint(dst + 16384, &em->up, gp * 128, rt * 128, bar, pol);
+          if (rr) {
+            tma_load_2d(dst, &em->gate, gp * 128, rt * 128, bar);
+            tma_load_2d(dst + 16384, &em->up, gp * 128, rt * 128, bar);
+          } else {
+            tma_load_2d_hint(dst, &em->gate, gp * 128, rt * 128, bar, pol);
+            tma_load_2d_hint(dst + 16384, &em->up, gp * 128, rt * 128, bar, pol);
+          }
         } else {
-          tma_load_2d_hint(dst, &em->down, gp * 128, rt * 256, bar, pol);
+          if (rr)
+            tma_load_2d(dst, &em->down, gp * 128, rt * 256, bar);
+          else
+            tma_load_2d_hint(dst, &em->down, gp * 128, rt * 256, bar, pol);
         }
         rw.next();
         if (++gp == GP) {
           gp = 0;
-          ++tile;
+          tile += tstep;
         }
       }
     }
@@ -900,7 +921,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         griddep_wait();  // the staged rows are the previous kernel's output
         for (int i = 0; i < n_items; ++i) {
           int seg, rt;
-          TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+          TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt, rr);
           const int row0 = a.segs[seg].y;
           const int ng = min(2, a.G - 2 * gp);
           for (int gi = 0; gi < ng; ++gi, ++k) {
@@ -915,7 +936,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
           }
           if (++gp == GP) {
             gp = 0;
-            ++tile;
+            tile += tstep;
           }
         }
       }
@@ -928,7 +949,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       Ring<SB> rb, rs;  // rb: stage being filled; rs: next stage to signal (LOOK behind)
       for (int i = 0; i < n_items; ++i) {
         int seg, rt;
-        TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt);
+        TileMap<KIND>::split(tile, a.n_rt, n_segs, seg, rt, rr);
         const int4 sg = a.segs[seg];
         const uint8_t* src_tok[TPL];
 #pragma unroll
@@ -967,7 +988,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
         }
         if (++gp == GP) {
           gp = 0;
-          ++tile;
+          tile += tstep;
         }
       }
       cp_async_wait<0>();
@@ -1028,19 +1049,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     // consumed soon after it was issued.
     int ptile = tile0, pgp = gp0, pleft = n_items;
     const uint16_t* sp =
-        scale_base<KIND>(a, tile_expert<KIND>(a, ptile, n_segs), j) + scale_off<KIND>(a, ptile, n_segs, j, r);
-    const uint16_t* nb = ptile + 1 <= tile_last ? scale_base<KIND>(a, tile_expert<KIND>(a, ptile + 1, n_segs), j) : sp;
-    int nne = ptile + 2 <= tile_last ? tile_expert<KIND>(a, ptile + 2, n_segs) : 0;
+        scale_base<KIND>(a, tile_expert<KIND>(a, ptile, n_segs, rr), j) + scale_off<KIND>(a, ptile, n_segs, j, r, rr);
+    const uint16_t* nb =
+        ptile + tstep <= tile_last ? scale_base<KIND>(a, tile_expert<KIND>(a, ptile + tstep, n_segs, rr), j) : sp;
+    int nne = ptile + 2 * tstep <= tile_last ? tile_expert<KIND>(a, ptile + 2 * tstep, n_segs, rr) : 0;
     auto fetch = [&](uint32_t& s0, uint32_t& s1) {
       if (pleft <= 0) return;
       s0 = __ldg(sp + 2 * pgp);
       s1 = 2 * pgp + 1 < a.G ? __ldg(sp + 2 * pgp + 1) : 0u;
       if (--pleft > 0 && ++pgp == GP) {
         pgp = 0;
-        ++ptile;
-        sp = nb + scale_off<KIND>(a, ptile, n_segs, j, r);
-        nb = ptile + 1 <= tile_last ? scale_base<KIND>(a, nne, j) : sp;
-        nne = ptile + 2 <= tile_last ? tile_expert<KIND>(a, ptile + 2, n_segs) : 0;
+        ptile += tstep;
+        sp = nb + scale_off<KIND>(a, ptile, n_segs, j, r, rr);
+        nb = ptile + tstep <= tile_last ? scale_base<KIND>(a, nne, j) : sp;
+        nne = ptile + 2 * tstep <= tile_last ? tile_expert<KIND>(a, ptile + 2 * tstep, n_segs, rr) : 0;
       }
     };
     uint32_t sc0 = 0, sc1 = 0, n10 = 0, n11 = 0, n20 = 0, n21 = 0;  // scales of items it, it+1, it+2
@@ -1177,14 +1199,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     };
     Ring<SD> rd;
 #pragma unroll 1
-    for (int tile = tile0; tile <= tile_last; ++tile) {
-      const TileInfo ti = tile_info<KIND>(a, tile, n_segs);
+    for (int tile = tile0; tile <= tile_last; tile += tstep) {
+      const TileInfo ti = tile_info<KIND>(a, tile, n_segs, rr);
       const int64_t ts = (int64_t)tile * GP, te = ts + GP;
       const uint32_t dcol = tlane + D0 + rd.idx * DC;
       mbar_wait_backoff(smem_u32(&d_full[rd.idx]), rd.phase, a.err, 256);
       tc_fence_after();
       bool own = true;
-      if (b0 <= ts && b1 >= te) {
+      if (rr || (b0 <= ts && b1 >= te)) {
         // the whole tile ran here: epilogue straight from the accumulator
 #pragma unroll 1
         for (int hc = 0; hc < N / 16; ++hc) {
@@ -1697,6 +1719,7 @@ static int run_moe(const MoECall& m) {
   e1.tile_ctr = plan.ctr1;
   e1.err = plan.err;
   e1.P = P;
+  e1.allow_rr = nt >= 8;
   if (m.phase == 0 || m.phase == 2) rc = launch_engine<Tr, KIND_GATEUP, EPI_COMBINE>(nt, e1, m.stream);
   if (rc || m.phase == 2) return rc;
 
@@ -1978,6 +2001,7 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   e.rt_ctr = plan.rtctr;
   e.err = plan.err;
   e.P = P;
+  e.allow_rr = nt >= 8;
   int rc;
   if (dtype == HN_DTYPE_BF16) {
     rc = launch_route<BF16>(ra, s);
