@@ -445,6 +445,9 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
 constexpr int kRgM = 64, kRgN = 64, kRgK = 32;
 constexpr int kRouterGemmMinT = 256;  // batches from this size route through router_logits_kernel
 
+// Tile loads: x as one 16-byte vector (8 activations) per thread, W as one
+// 16-byte vector (4 fp32 or 8 half) per thread per 32-wide row chunk; the
+// next chunk is loaded into registers while the current one is multiplied.
 template <typename Tr>
 __global__ void __launch_bounds__(256) router_logits_kernel(const void* x, int64_t ldx, int T, int H, int E,
                                                             const void* rw, int rw_dtype, float* out) {
@@ -453,21 +456,77 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* x, int64
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int t0 = blockIdx.x * kRgM, e0 = blockIdx.y * kRgN;
   const typename Tr::T* xp = reinterpret_cast<const typename Tr::T*>(x);
+  const bool w32 = rw_dtype == HN_DTYPE_F32;
+  // this thread's loads: x row xt, k offset xk (8 values); W row(s) and k offsets
+  const int xt = tid >> 2, xk = (tid & 3) * 8;
+  const bool xok = t0 + xt < T;
+  auto load_x = [&](int k0) -> uint4 {
+    return xok ? __ldg(reinterpret_cast<const uint4*>(xp + (int64_t)(t0 + xt) * ldx + k0 + xk))
+               : make_uint4(0u, 0u, 0u, 0u);
+  };
+  // fp32 W: 2 vectors of 4 (rows tid>>3 and 32 + (tid>>3), k (tid&7)*4); 16-bit W: 1 vector of 8
+  auto load_w = [&](int k0, int q) -> uint4 {
+    int e, k;
+    if (w32) {
+      e = e0 + q * 32 + (tid >> 3);
+      k = (tid & 7) * 4;
+      return e < E ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(rw) + (int64_t)e * H + k0 + k))
+                   : make_uint4(0u, 0u, 0u, 0u);
+    }
+    e = e0 + (tid >> 2);
+    k = (tid & 3) * 8;
+    return (q == 0 && e < E)
+               ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(rw) + (int64_t)e * H + k0 + k))
+               : make_uint4(0u, 0u, 0u, 0u);
+  };
+  auto put = [&](uint4 xv, uint4 w0, uint4 w1) {
+    const typename Tr::T2* x2 = reinterpret_cast<const typename Tr::T2*>(&xv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      xs[xk + 2 * i][xt] = Tr::to_f(x2[i].x);
+      xs[xk + 2 * i + 1][xt] = Tr::to_f(x2[i].y);
+    }
+    if (w32) {
+      const float* f0 = reinterpret_cast<const float*>(&w0);
+      const float* f1 = reinterpret_cast<const float*>(&w1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ws[(tid & 7) * 4 + i][tid >> 3] = f0[i];
+        ws[(tid & 7) * 4 + i][32 + (tid >> 3)] = f1[i];
+      }
+    } else {
+      const uint32_t* h = reinterpret_cast<const uint32_t*>(&w0);
+      const bool bf = rw_dtype == HN_DTYPE_BF16;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float lo, hi;
+        if (bf) {
+          lo = __uint_as_float(h[i] << 16);
+          hi = __uint_as_float(h[i] & 0xFFFF0000u);
+        } else {
+          const __half2 hh = *reinterpret_cast<const __half2*>(&h[i]);
+          lo = __low2float(hh);
+          hi = __high2float(hh);
+        }
+        ws[(tid & 3) * 8 + 2 * i][tid >> 2] = lo;
+        ws[(tid & 3) * 8 + 2 * i + 1][tid >> 2] = hi;
+      }
+    }
+  };
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  uint4 xv = load_x(0), w0 = load_w(0, 0), w1 = load_w(0, 1);
   for (int k0 = 0; k0 < H; k0 += kRgK) {
-    for (int i = tid; i < kRgM * kRgK; i += 256) {
-      const int tt = i / kRgK, kk = i - tt * kRgK, t = t0 + tt;
-      xs[kk][tt] = t < T ? Tr::to_f(xp[(int64_t)t * ldx + k0 + kk]) : 0.f;
-    }
-    for (int i = tid; i < kRgN * kRgK; i += 256) {
-      const int ee = i / kRgK, kk = i - ee * kRgK, e = e0 + ee;
-      ws[kk][ee] = e < E ? load_any(rw, rw_dtype, (int64_t)e * H + k0 + kk) : 0.f;
-    }
+    put(xv, w0, w1);
     __syncthreads();
+    if (k0 + kRgK < H) {
+      xv = load_x(k0 + kRgK);
+      w0 = load_w(k0 + kRgK, 0);
+      w1 = load_w(k0 + kRgK, 1);
+    }
 #pragma unroll 8
     for (int kk = 0; kk < kRgK; ++kk) {
       const float4 av = *reinterpret_cast<const float4*>(&xs[kk][ty * 4]);
@@ -1140,21 +1199,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
           }
         }
       } else {
+        // rows r and r + 128 of the 256-row tile, per token
+        const int row0 = ti.rt * 256 + r;
+        const bool ok0 = row0 < a.N, ok1 = row0 + 128 < a.N;
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int row = ti.rt * 256 + jj * 128 + r;
-          if (row < a.N) {
-#pragma unroll
-            for (int n = 0; n < 16; ++n) {
-              const int tok = hc * 16 + n;
-              if (tok < ti.m) {
-                const int p = ti.p0 + tok;
-                const float v = jj ? v1[n] : v0[n];
-                if (EPI == EPI_STORE)
-                  reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)a.a_tok[p] * a.ldo + row] = Tr::from_f(v);
-                else
-                  a.R[(int64_t)a.a_tk[p] * a.N + row] = v * a.a_w[p];
-              }
+        for (int n = 0; n < 16; ++n) {
+          const int tok = hc * 16 + n;
+          if (tok < ti.m) {
+            const int p = ti.p0 + tok;
+            if (EPI == EPI_STORE) {
+              typename Tr::T* o = reinterpret_cast<typename Tr::T*>(a.out) + (int64_t)a.a_tok[p] * a.ldo + row0;
+              if (ok0) o[0] = Tr::from_f(v0[n]);
+              if (ok1) o[128] = Tr::from_f(v1[n]);
+            } else {
+              const float w = a.a_w[p];
+              float* o = a.R + (int64_t)a.a_tk[p] * a.N + row0;
+              if (ok0) o[0] = v0[n] * w;
+              if (ok1) o[128] = v1[n] * w;
             }
           }
         }
@@ -1502,7 +1563,9 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   sm = std::max(sm, (size_t)(2 * ra.E) * 4);
   sm = (sm + 15) & ~(size_t)15;
   r.wbuf_off = (int)sm;
-  const bool gemm = ra.mode == ROUTE_COMPUTE && ra.T >= kRouterGemmMinT && ra.plan.rlog;
+  // the GEMM's 16-byte vector loads need aligned rows of x and of the router matrix
+  const bool gemm = ra.mode == ROUTE_COMPUTE && ra.T >= kRouterGemmMinT && ra.plan.rlog &&
+                    ((uintptr_t)ra.x & 15) == 0 && ra.ldx % 8 == 0 && ((uintptr_t)ra.rw & 15) == 0;
   if (ra.mode == ROUTE_COMPUTE && !gemm)
     sm += (size_t)route_chunk_experts(ra.H, ra.E, ra.rw_dtype) * ra.H * route_esize(ra.rw_dtype);
   HN_REQUIRE(sm <= 227 * 1024, "router: hidden size too large for the shared-memory plan");
