@@ -1128,48 +1128,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     fetch(sc0, sc1);
     fetch(n10, n11);
     fetch(n20, n21);
-    int gp = gp0;
+    // Per-thread constants: swizzled offsets of this row's 16-byte chunks for
+    // the two groups of a weight stage, this matrix's A-stage barriers (stage
+    // sa at +16*sa bytes) and TMEM column.
+    int choff[2][kC];
+#pragma unroll
+    for (int g = 0; g < 2; ++g)
+#pragma unroll
+      for (int i = 0; i < kC; ++i) choff[g][i] = ((g * 4 + h * kC + i) ^ swz) << 4;
+    const uint32_t afull_j = smem_u32(&a_full[j]), aempty_j = smem_u32(&a_empty[j]);
+    const uint32_t tcol_j = tlane + j * 64 + h * (16 * kC);
     Ring<ST> rw;
     Ring<SA> ra;
+    // One group: load this thread's chunks, wait for the A stage, dequantise
+    // into TMEM, wait for the stores, signal (and release the weight stage
+    // after the item's last group: the refill is an async-proxy write that is
+    // not ordered after shared loads still in flight).
+    auto group = [&](const uint8_t* wrow_p, int gi, uint32_t sv, bool last, uint32_t wempty) {
+      const int sa = ra.idx;
+      uint4 W[kC];
+#pragma unroll
+      for (int i = 0; i < kC; ++i) W[i] = *reinterpret_cast<const uint4*>(wrow_p + choff[gi][i]);
+      const uint32_t s2 = __byte_perm(sv, sv, 0x1010);
+      mbar_wait(aempty_j + 16 * sa, ra.phase ^ 1u, a.err);
+      tc_fence_after();
+      const uint32_t acol = tcol_j + sa * 128;
+#pragma unroll
+      for (int i = 0; i < kC; ++i) {
+        uint32_t o[16];
+        dequant_word_f16(W[i].x, s2, o + 0);
+        dequant_word_f16(W[i].y, s2, o + 4);
+        dequant_word_f16(W[i].z, s2, o + 8);
+        dequant_word_f16(W[i].w, s2, o + 12);
+        tmem_st16(acol + 16 * i, o);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      mbar_arrive_elect(afull_j + 16 * sa);
+      if (last) mbar_arrive_elect(wempty);
+      ra.next();
+    };
+    int gp = gp0;
 #pragma unroll 1
     for (int it = 0; it < n_items; ++it) {
       const int ng = min(2, a.G - 2 * gp);
       const int ws = rw.idx;
       mbar_wait(smem_u32(&w_full[ws]), rw.phase, a.err);
       const uint8_t* wrow_p = wrow + ws * L::kWStage;
-#pragma unroll 1
-      for (int gi = 0; gi < ng; ++gi) {
-        const int sa = ra.idx;
-        uint4 W[kC];
-#pragma unroll
-        for (int i = 0; i < kC; ++i)
-          W[i] = *reinterpret_cast<const uint4*>(wrow_p + (((gi * 4 + h * kC + i) ^ swz) << 4));
-        const uint32_t sv = gi ? sc1 : sc0;
-        const uint32_t s2 = sv | (sv << 16);
-        mbar_wait(smem_u32(&a_empty[2 * sa + j]), ra.phase ^ 1u, a.err);
-        tc_fence_after();
-        const uint32_t acol = tlane + sa * 128 + j * 64 + h * (16 * kC);
-#pragma unroll
-        for (int i = 0; i < kC; ++i) {
-          uint32_t o[16];
-          dequant_word_f16(W[i].x, s2, o + 0);
-          dequant_word_f16(W[i].y, s2, o + 4);
-          dequant_word_f16(W[i].z, s2, o + 8);
-          dequant_word_f16(W[i].w, s2, o + 12);
-          tmem_st16(acol + 16 * i, o);
-        }
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(smem_u32(&a_full[2 * sa + j]));
-          // The weight stage is released only after every lane consumed its
-          // shared loads (the dequant above read W): the refill is an
-          // async-proxy write that is not ordered after loads still in flight.
-          if (gi == ng - 1) mbar_arrive(smem_u32(&w_empty[ws]));
-        }
-        ra.next();
-      }
+      const uint32_t wempty = smem_u32(&w_empty[ws]);
+      group(wrow_p, 0, sc0, ng == 1, wempty);
+      if (ng == 2) group(wrow_p, 1, sc1, true, wempty);
       rw.next();
       if (++gp == GP) gp = 0;
       sc0 = n10;
