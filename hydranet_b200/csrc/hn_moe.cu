@@ -1065,32 +1065,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
     Ring<SA> ra;
     Ring<SB> rb;
     Ring<SD> rd;
-    int gp = gp0;
+    // per-warp constants: barrier addresses (stage s at +8*s, A stages at
+    // +16*s for this matrix), the B ring's descriptor start, TMEM columns
+    const uint32_t afull_m = smem_u32(&a_full[mj]), aempty_m = smem_u32(&a_empty[mj]);
+    const uint32_t bfull0 = smem_u32(&b_full[0]), bempty0 = smem_u32(&b_empty[0]);
+    const uint32_t dfull0 = smem_u32(&d_full[0]), dempty0 = smem_u32(&d_empty[0]);
+    // B descriptor (32-bit halves): K-major SW128 tile (start, LBO ignored =
+    // 1, SBO 1024 B, layout SWIZZLE_128B); stage sb starts kBStage/16 units on
+    constexpr uint32_t kBStep = L::kBStage >> 4;
+    const uint32_t b_lo0 = ((smem_u32(bst) >> 4) & 0x3FFFu) | (1u << 16);
+    const uint32_t a_col = tbase + mj * 64, d_col = tbase + D0 + mj * N;
     uint32_t acc = 0;  // 0: the next group starts a piece (overwrites the accumulator)
+    auto group = [&](bool end) {
+      const int sa = ra.idx, sb = rb.idx;
+      if (acc == 0) mbar_wait(dempty0 + 8 * rd.idx, rd.phase ^ 1u, a.err);
+      mbar_wait(bfull0 + 8 * sb, rb.phase, a.err);
+      mbar_wait(afull_m + 16 * sa, ra.phase, a.err);
+      tc_fence_after();
+      umma_group8_sw128<N>(d_col + rd.idx * DC, a_col + sa * 128, b_lo0 + sb * kBStep, kDescHiSW128, IDESC, acc);
+      umma_commit_elect(aempty_m + 16 * sa);
+      umma_commit_elect(bempty0 + 8 * sb);
+      if (end) {
+        umma_commit_elect(dfull0 + 8 * rd.idx);
+        rd.next();
+      }
+      acc = end ? 0u : 1u;
+      ra.next();
+      rb.next();
+    };
+    int gp = gp0;
     for (int i = 0; i < n_items; ++i) {
       const int ng = min(2, a.G - 2 * gp);
-      for (int gi = 0; gi < ng; ++gi) {
-        const int sa = ra.idx, sb = rb.idx;
-        if (acc == 0) mbar_wait(smem_u32(&d_empty[rd.idx]), rd.phase ^ 1u, a.err);
-        mbar_wait(smem_u32(&b_full[sb]), rb.phase, a.err);
-        mbar_wait(smem_u32(&a_full[2 * sa + mj]), ra.phase, a.err);
-        tc_fence_after();
-        // B descriptor (32-bit halves): K-major SW128 tile (start, LBO ignored
-        // = 1, SBO 1024 B, layout SWIZZLE_128B)
-        const uint32_t b_lo = ((smem_u32(bst + sb * L::kBStage) >> 4) & 0x3FFFu) | (1u << 16);
-        umma_group8_sw128<N>(tbase + D0 + rd.idx * DC + mj * N, tbase + sa * 128 + mj * 64, b_lo, kDescHiSW128,
-                             IDESC, acc);
-        umma_commit_elect(smem_u32(&a_empty[2 * sa + mj]));
-        umma_commit_elect(smem_u32(&b_empty[sb]));
-        const bool end = (2 * gp + gi == a.G - 1) || (i == n_items - 1 && gi == ng - 1);
-        if (end) {
-          umma_commit_elect(smem_u32(&d_full[rd.idx]));
-          rd.next();
-        }
-        acc = end ? 0u : 1u;
-        ra.next();
-        rb.next();
-      }
+      const bool last_item = i == n_items - 1;
+      group((2 * gp == a.G - 1) || (last_item && ng == 1));
+      if (ng == 2) group((2 * gp + 1 == a.G - 1) || last_item);
       if (++gp == GP) gp = 0;
     }
     __syncwarp();
