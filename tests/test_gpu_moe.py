@@ -206,3 +206,9 @@ def test_phase_split_equals_one_call(lib):
     with pytest.raises(_lib.HydraNetError):
         _lib.check(_lib.load().hn_moe_layer_int4_phase(4, None, 2, 1, 1024, 768, 8, None, None, None, None, None,
                                                        None, None, None, 0, None))
+
+
+def test_driver_smoke_entry(lib):
+    """The driver's smoke() (one small layer on cuda:0 against the oracle) runs clean."""
+    import __graft_entry__
+    __graft_entry__.smoke()
