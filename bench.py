@@ -129,7 +129,7 @@ def prefill_measure(args, dev):
 
 # DRAM bytes (read + write) of one gate/up engine launch, from the ncu capture
 # summarised in profiles/ (per launch, same workload); None where not captured.
-GATEUP_TRAFFIC = {64: 503473408}
+GATEUP_TRAFFIC = {64: 493565952}
 
 
 def blob_bytes(h, f, g=128):
