@@ -20,6 +20,12 @@ void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int check_cuda(cudaError_t e, const char* what);
 int sm_count_current();
+// hn_int4_linear and its workspace size with segments of at most 8*max_nt
+// tokens (hn_int4_linear itself allows 128).
+size_t int4_linear_workspace_nt(int64_t M, int64_t N, int64_t K, int max_nt);
+int int4_linear_nt(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, const uint8_t* w_packed,
+                   const uint16_t* w_scales, int64_t N, int group_size, void* out, int64_t ldo, void* workspace,
+                   size_t workspace_bytes, void* stream, int max_nt);
 
 #define HN_REQUIRE(cond, msg)                                  \
   do {                                                         \

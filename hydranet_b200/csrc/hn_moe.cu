@@ -1867,9 +1867,7 @@ size_t hn_expert_mlp_workspace_size(int64_t T, int64_t H, int64_t F) {
 }
 
 size_t hn_int4_linear_workspace_size(int64_t M, int64_t N, int64_t K) {
-  if (M < 1 || N < 1 || K < 128) return 0;
-  const int nt = pick_nt(M, 1, 1);
-  return make_layout(M, K, 1, 1, 0, N, nt, grid_p(nt), false).total() + 256;
+  return hn::int4_linear_workspace_nt(M, N, K, 16);
 }
 
 static int moe_layer_call(int phase, const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
@@ -2027,13 +2025,32 @@ int hn_expert_mlp_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F
 int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, const uint8_t* w_packed,
                    const uint16_t* w_scales, int64_t N, int group_size, void* out, int64_t ldo, void* workspace,
                    size_t workspace_bytes, void* stream) {
+  return hn::int4_linear_nt(x, ldx, dtype, M, K, w_packed, w_scales, N, group_size, out, ldo, workspace,
+                            workspace_bytes, stream, 16);
+}
+
+}  // extern "C"
+
+namespace hn {
+
+size_t int4_linear_workspace_nt(int64_t M, int64_t N, int64_t K, int max_nt) {
+  if (M < 1 || N < 1 || K < 128) return 0;
+  const int nt = std::min(pick_nt(M, 1, 1), max_nt);
+  return make_layout(M, K, 1, 1, 0, N, nt, grid_p(nt), false).total() + 256;
+}
+
+// hn_int4_linear with segments of at most 8*max_nt tokens (the static-scratch
+// entry caps them at 32, which keeps its stream-K partials small).
+int int4_linear_nt(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, const uint8_t* w_packed,
+                   const uint16_t* w_scales, int64_t N, int group_size, void* out, int64_t ldo, void* workspace,
+                   size_t workspace_bytes, void* stream, int max_nt) {
   HN_REQUIRE_SUPPORTED(group_size == 128, "only group_size 128 is implemented");
   HN_REQUIRE(M >= 1 && N >= 1 && K >= 128 && K % 128 == 0, "int4_linear: need M, N >= 1 and K a multiple of 128");
   HN_REQUIRE(M <= (1 << 20) && N <= (1 << 20) && K <= 32768, "int4_linear: dims too large");
   HN_REQUIRE(((uintptr_t)w_packed & 15) == 0, "int4_linear: packed weights must be 16-byte aligned");
   HN_REQUIRE(ldx >= K && ldo >= N, "int4_linear: bad row stride");
   HN_REQUIRE(x && w_packed && w_scales && out && workspace, "int4_linear: null pointer");
-  const int nt = pick_nt(M, 1, 1);
+  const int nt = std::min(pick_nt(M, 1, 1), max_nt);
   const int P = grid_p(nt);
   const Layout l = make_layout(M, K, 1, 1, 0, N, nt, P, false);
   int rc0 = check_ws(workspace, workspace_bytes, l);
@@ -2094,6 +2111,10 @@ int hn_int4_linear(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   }
   return rc;
 }
+
+}  // namespace hn
+
+extern "C" {
 
 size_t hn_expert_maps_bytes(void) { return sizeof(ExpertMaps); }
 

@@ -15,6 +15,10 @@ namespace hn {
 namespace {
 
 constexpr size_t kStaticScratchBytes = HN_INT4_LINEAR_STATIC_SCRATCH_BYTES;
+// Token segments of at most 32 rows keep the stream-K partials within the
+// scratch; the 64- and 128-row segments hn_int4_linear uses above M = 64
+// need 19-39 MiB of partials alone.
+constexpr int kStaticMaxNt = 4;
 static_assert(kStaticScratchBytes % 256 == 0, "static scratch size must keep 256-byte granularity");
 
 __device__ __align__(256) unsigned char g_linear_scratch[kStaticScratchBytes];
@@ -46,7 +50,7 @@ int static_scratch(void** out) {
 extern "C" int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K,
                                      const uint8_t* w_packed, const uint16_t* w_scales, int64_t N, int group_size,
                                      void* out, int64_t ldo, void* stream) {
-  const size_t need = hn_int4_linear_workspace_size(M, N, K);
+  const size_t need = hn::int4_linear_workspace_nt(M, N, K, hn::kStaticMaxNt);
   if (need == 0) return hn::fail(HN_ERR_INVALID, "int4_linear_static: need M, N >= 1 and K >= 128");
   if (need > hn::kStaticScratchBytes)
     return hn::fail(HN_ERR_WORKSPACE, "int4_linear_static: M=" + std::to_string(M) + " N=" + std::to_string(N) +
@@ -57,6 +61,6 @@ extern "C" int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int6
   void* ws = nullptr;
   const int rc = hn::static_scratch(&ws);
   if (rc) return rc;
-  return hn_int4_linear(x, ldx, dtype, M, K, w_packed, w_scales, N, group_size, out, ldo, ws,
-                        hn::kStaticScratchBytes, stream);
+  return hn::int4_linear_nt(x, ldx, dtype, M, K, w_packed, w_scales, N, group_size, out, ldo, ws,
+                            hn::kStaticScratchBytes, stream, hn::kStaticMaxNt);
 }

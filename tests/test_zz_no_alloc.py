@@ -36,7 +36,8 @@ def weights(seed, n, k):
 
 
 @pytest.mark.parametrize("M,N,K,dtype", [(1, 14336, 4096, "bf16"), (17, 1024, 512, "f16"),
-                                         (64, 4096, 14336, "bf16"), (40, 2048, 1024, "bf16")])
+                                         (64, 4096, 14336, "bf16"), (40, 2048, 1024, "bf16"),
+                                         (80, 2048, 1024, "bf16"), (300, 1024, 512, "f16")])
 def test_static_matches_workspace_entry_point(lib, M, N, K, dtype):
     p, s, pd, sd = weights(M + N + K, N, K)
     x = act(np.random.default_rng(M).standard_normal((M, K), dtype=np.float32), dtype)
