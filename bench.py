@@ -119,12 +119,18 @@ def prefill_measure(args, dev):
     tf = flops / (ms * 1e-3) / 1e12
     del layer, table
     torch.cuda.empty_cache()
+    cpu = None
+    if not args.no_cpu_baseline:
+        v, n, el, nt, ne = prefill_cpu_time()
+        cpu = {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"{n} oracle steps of {nt} tokens, sigmoid top-{P_K} over {ne} experts (eight expert "
+                         f"MLPs per token as in config 5), numpy float32 dequant-then-matmul, {el:.1f}s"}
     return {"workload": "glm45air_moe_layer_prefill", "tokens": P_T, "hidden": P_H, "ffn": P_F, "experts": P_E,
             "top_k": P_K, "router": "sigmoid top-8, correction bias", "steps": steps, "warmup": args.warmup,
             "ms_per_step": ms, "tok_s": P_T / (ms * 1e-3),
             "roofline": {"bound": "tensor", "achieved": tf, "peak": tc_peak, "unit": "TFLOP/s", "frac": tf / tc_peak,
                          "peak_kind": peak_kind, "flops_per_step": flops},
-            "phases": phase, "clocks": clk.summary()}
+            "phases": phase, "clocks": clk.summary(), "cpu_baseline": cpu}
 
 
 # DRAM bytes (read + write) of one gate/up engine launch, from the ncu capture
@@ -258,6 +264,44 @@ def cpu_oracle_time(T: int, budget_s: float = 15.0, max_steps: int = 50):
         if el > budget_s or steps >= max_steps:
             break
     return T * steps / el, steps, el
+
+
+def prefill_cpu_time(budget_s: float = 10.0, n_tok: int = 256, n_exp: int = 16):
+    """tok/s of the oracle's prefill layer (GLM-4.5-Air shapes, sigmoid top-8,
+    dequant-then-matmul in numpy float32) on the host cores, over a bounded
+    sample: n_tok tokens routed over n_exp experts, so each token still runs
+    eight expert MLPs (the per-token work of config 5) with fewer weights in
+    host memory."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import int4_ref as R
+    from hydranet_b200 import synth
+
+    def make(e):
+        rng = np.random.default_rng(2000 + e)
+        mats = []
+        for n, k in ((P_F, P_H), (P_F, P_H), (P_H, P_F)):
+            mats += [rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8),
+                     (rng.random((n, k // 128), dtype=np.float32) * np.float32(0.005)).astype(np.float16)]
+        return R.DequantExpert.from_packed(*mats)
+
+    with ThreadPoolExecutor(max_workers=min(8, cpu_threads())) as ex:
+        experts = dict(enumerate(ex.map(make, range(n_exp))))
+    rw = synth.host_normal(98, (n_exp, P_H), 0.02)
+    x = R.round_to_bf16(np.random.default_rng(1).standard_normal((n_tok, P_H), dtype=np.float32))
+
+    def step():
+        idx, w, _ = R.sigmoid_topk_router_ref(x, rw, P_K, "f32")
+        return R.moe_combine_ref(x, idx, w, experts)
+
+    step()
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        steps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or steps >= 20:
+            break
+    return n_tok * steps / el, steps, el, n_tok, n_exp
 
 
 def cpu_threads():

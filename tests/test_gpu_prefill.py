@@ -33,21 +33,27 @@ def _check_indices(idx, ref_idx, ref_scores, k, ulp_rel):
     return len(mism)
 
 
-@pytest.mark.parametrize("T,E,k,H,F", [
-    (1280, 16, 4, 1024, 512),   # T*K = 5120 > 4096: plan kernel; 320 per expert: N = 128
-    (2200, 64, 2, 512, 256),    # plan kernel; ~69 per expert: N = 64
-    (1280, 32, 2, 512, 384),    # prep-kernel plan; 80 per expert: N = 64
+@pytest.mark.parametrize("T,E,k,H,F,bias", [
+    (1280, 16, 4, 1024, 512, False),  # T*K = 5120 > 4096: plan kernel; 320 per expert: N = 128
+    (1280, 16, 4, 1024, 512, True),   # the same with a selection-only correction bias (GLM-4.5)
+    (2200, 64, 2, 512, 256, False),   # plan kernel; ~69 per expert: N = 64
+    (1280, 32, 2, 512, 384, False),   # prep-kernel plan; 80 per expert: N = 64
 ])
-def test_prefill_sigmoid_layer(lib, T, E, k, H, F):
+def test_prefill_sigmoid_layer(lib, T, E, k, H, F, bias):
     shape = synth.MoEShape(H, F, E, k)
     table, packed = host_moe(shape, 500 + E)
     x = torch.randn(T, H, generator=torch.Generator("cuda").manual_seed(T), device="cuda").to(torch.bfloat16)
     r = GLM4SigmoidRouter(hidden_dim=H, num_experts=E, experts_per_token=k).cuda()
+    cb = torch.from_numpy(synth.host_correction_bias(9, E)).cuda() if bias else None
+    if bias:
+        r.set_correction_bias(cb)
     layer = MoELayerInt4(r, table)
     out, ro = layer(x, return_routing=True)
     xi, wi = to_np32(x), to_np32(r.weight)
-    idx, w, logits = R.sigmoid_topk_router_ref(xi, wi, k, "bf16")
-    n_tie = _check_indices(ro.expert_indices.cpu().numpy(), idx, 1 / (1 + np.exp(-logits)), k, 2 ** -22)
+    cbn = None if cb is None else to_np32(cb)
+    idx, w, logits = R.sigmoid_topk_router_ref(xi, wi, k, "bf16", correction_bias=cbn)
+    sel = 1 / (1 + np.exp(-logits)) + (0 if cbn is None else cbn[None, :])
+    n_tie = _check_indices(ro.expert_indices.cpu().numpy(), idx, sel, k, 2 ** -22)
     assert n_tie == 0
     ref = R.moe_combine_ref(xi, idx, w, oracle_experts(packed))
     err = rel_l2(to_np32(out), ref)
