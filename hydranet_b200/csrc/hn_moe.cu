@@ -45,6 +45,9 @@ struct Plan {
   int* counts;   // [E]
   int* n_segs;   // [1]
   int4* segs;    // [max_segs] {expert, first assignment, tokens, 0}
+  int* n_segs2;  // [1] a second cut of the same lists into seg2-token segments (down phase), or NULL
+  int4* segs2;   // [max_segs2]
+  int seg2;      // 0: no second cut
   int* a_tok;    // [T*K] token of assignment p
   int* a_tk;     // [T*K] t*K + slot of assignment p (inverse of pos)
   float* a_w;    // [T*K] routing weight of assignment p
@@ -397,15 +400,19 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   for (int i = tid; i < TK; i += 256) atomicAdd(&cnt[in_smem ? pidx[i] : __ldcg(a.plan.idx + i)], 1);
   __syncthreads();
   if (tid == 0) {
-    int o = 0, ns = 0;
+    int o = 0, ns = 0, ns2 = 0;
     for (int e = 0; e < a.E; ++e) {
       off[e] = o;
       const int m = cnt[e];
       for (int j = 0; j < m; j += a.seg) a.plan.segs[ns++] = make_int4(e, o + j, min(a.seg, m - j), 0);
+      if (a.plan.seg2)
+        for (int j = 0; j < m; j += a.plan.seg2)
+          a.plan.segs2[ns2++] = make_int4(e, o + j, min(a.plan.seg2, m - j), 0);
       o += m;
       a.plan.counts[e] = m;
     }
     *a.plan.n_segs = ns;
+    if (a.plan.seg2) *a.plan.n_segs2 = ns2;
     *a.plan.route_ctr = 0;
   }
   __syncthreads();
@@ -590,17 +597,24 @@ __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
   for (int64_t i = tid; i < TK; i += 256) atomicAdd(&cnt[__ldcg(a.plan.idx + i)], 1);
   __syncthreads();
   if (tid == 0) {
-    int o = 0, ns = 0;
+    const int s2 = a.plan.seg2;
+    int o = 0, ns = 0, ns2 = 0;
     for (int x = 0; x < e; ++x) {
       o += cnt[x];
       ns += (cnt[x] + a.seg - 1) / a.seg;
+      if (s2) ns2 += (cnt[x] + s2 - 1) / s2;
     }
     s_base[0] = o;
     s_base[1] = ns;
     const int m = cnt[e];
     for (int j = 0; j < m; j += a.seg) a.plan.segs[ns++] = make_int4(e, o + j, min(a.seg, m - j), 0);
+    if (s2)
+      for (int j = 0; j < m; j += s2) a.plan.segs2[ns2++] = make_int4(e, o + j, min(s2, m - j), 0);
     a.plan.counts[e] = m;
-    if (e == a.E - 1) *a.plan.n_segs = ns;
+    if (e == a.E - 1) {
+      *a.plan.n_segs = ns;
+      if (s2) *a.plan.n_segs2 = ns2;
+    }
   }
   // this thread's chunk of the routing, in (token, slot) order
   const int64_t per = (TK + 255) / 256, lo = min(TK, tid * per), hi = min(TK, lo + per);
@@ -1477,8 +1491,10 @@ static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
 // call, because another shape's data section may have covered them.
 struct Layout {
   size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
-  size_t counts, n_segs, segs, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, xs, part1, part2, R, rlog, data;  // back (relative)
+  size_t counts, n_segs, segs, n_segs2, segs2, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, xs, part1, part2, R, rlog,
+      data;  // back (relative)
   bool has_rlog, has_xs;
+  int seg2;  // second segment cut for the down phase (0: none)
   size_t total() const { return counters + data; }
 };
 
@@ -1509,6 +1525,12 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.counts = take(4 * E);
   l.n_segs = take(4);
   l.segs = take(16 * max_segs);
+  // 128-token segments of a routed layer: the down phase runs 64-token tiles
+  // (two accumulator stages), cut from the same assignment lists
+  l.seg2 = (F && nt >= 16) ? seg_tokens(8) : 0;
+  const int64_t max_segs2 = l.seg2 ? std::min<int64_t>(E, TK) + (TK + l.seg2 - 1) / l.seg2 : 0;
+  l.n_segs2 = take(4);
+  l.segs2 = take(16 * max_segs2);
   l.a_tok = take(4 * TK);
   l.a_tk = take(4 * TK);
   l.a_w = take(4 * TK);
@@ -1542,6 +1564,9 @@ static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
   p.counts = reinterpret_cast<int*>(d + l.counts);
   p.n_segs = reinterpret_cast<int*>(d + l.n_segs);
   p.segs = reinterpret_cast<int4*>(d + l.segs);
+  p.seg2 = l.seg2;
+  p.n_segs2 = l.seg2 ? reinterpret_cast<int*>(d + l.n_segs2) : nullptr;
+  p.segs2 = l.seg2 ? reinterpret_cast<int4*>(d + l.segs2) : nullptr;
   p.a_tok = reinterpret_cast<int*>(d + l.a_tok);
   p.a_tk = reinterpret_cast<int*>(d + l.a_tk);
   p.a_w = reinterpret_cast<float*>(d + l.a_w);
@@ -1819,11 +1844,19 @@ static int run_moe(const MoECall& m) {
   e2.tile_ctr = plan.ctr2;
   e2.rt_ctr = plan.rtctr;
   e2.early = 1;
-  if (!combine) return launch_engine<Tr, KIND_DOWN, EPI_STORE>(nt, e2, m.stream);
+  int nt2 = nt;
+  if (plan.seg2) {
+    // 64-token tiles for the down phase: two accumulator stages instead of one
+    e2.segs = plan.segs2;
+    e2.n_segs = plan.n_segs2;
+    nt2 = plan.seg2 / 8;
+    e2.allow_rr = nt2 >= 8;
+  }
+  if (!combine) return launch_engine<Tr, KIND_DOWN, EPI_STORE>(nt2, e2, m.stream);
   // large routings: the epilogue only writes the weighted rows, one
   // bandwidth-bound pass sums them afterwards
   e2.defer_combine = TK > kPlanSmemEntries;
-  rc = launch_engine<Tr, KIND_DOWN, EPI_COMBINE>(nt, e2, m.stream);
+  rc = launch_engine<Tr, KIND_DOWN, EPI_COMBINE>(nt2, e2, m.stream);
   if (rc || !e2.defer_combine) return rc;
   const int64_t n4 = m.T * (m.H / 4);
   const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)grid_p(nt) * 8);

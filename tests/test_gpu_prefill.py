@@ -103,7 +103,7 @@ def test_given_routing_plan_kernel_with_duplicates(lib, k):
 @pytest.mark.parametrize("M,N,K", [(70, 512, 1024), (300, 384, 512), (1000, 256, 256)])
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 def test_int4_linear_wide_segments(lib, M, N, K, dtype):
-    """int4_linear with M >= 48 rows per call uses 64- or 128-token segments."""
+    """int4_linear with more than 64 rows per call uses 64- or 128-token segments."""
     rng = np.random.default_rng(M)
     p, s = R.quantize_tensor(rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
     xt = act(rng.standard_normal((M, K), dtype=np.float32), dtype)
