@@ -588,7 +588,6 @@ __global__ void __launch_bounds__(256) stage_rows_kernel(const int* a_tok, int n
 __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
   extern __shared__ int psm[];
   int* cnt = psm;  // [E]
-  __shared__ int s_scan[256];
   __shared__ int s_base[2];  // assignment offset, segment offset of this expert
   const int e = blockIdx.x, tid = threadIdx.x;
   const int64_t TK = (int64_t)a.T * a.K;
@@ -616,28 +615,34 @@ __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
       if (s2) *a.plan.n_segs2 = ns2;
     }
   }
-  // this thread's chunk of the routing, in (token, slot) order
-  const int64_t per = (TK + 255) / 256, lo = min(TK, tid * per), hi = min(TK, lo + per);
-  int c = 0;
-  for (int64_t i = lo; i < hi; ++i) c += __ldcg(a.plan.idx + i) == e;
-  s_scan[tid] = c;
+  // this expert's assignments in (token, slot) order: coalesced rounds of
+  // 256 routing entries, a ballot per warp and a prefix over the 8 warps
+  __shared__ int s_wcnt[8];
   __syncthreads();
-  // exclusive scan of the 256 chunk counts (Hillis-Steele in shared memory)
-  for (int d = 1; d < 256; d <<= 1) {
-    const int v = tid >= d ? s_scan[tid - d] : 0;
+  const int lane = tid & 31, wid = tid >> 5;
+  int base = s_base[0];
+  for (int64_t r0 = 0; r0 < TK; r0 += 256) {
+    const int64_t i = r0 + tid;
+    const bool hit = i < TK && __ldcg(a.plan.idx + i) == e;
+    const unsigned bal = __ballot_sync(0xffffffffu, hit);
+    if (lane == 0) s_wcnt[wid] = __popc(bal);
     __syncthreads();
-    s_scan[tid] += v;
-    __syncthreads();
-  }
-  int p = s_base[0] + s_scan[tid] - c;
-  for (int64_t i = lo; i < hi; ++i) {
-    if (__ldcg(a.plan.idx + i) == e) {
+    int before = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const int cw = s_wcnt[w];
+      before += w < wid ? cw : 0;
+      total += cw;
+    }
+    if (hit) {
+      const int p = base + before + __popc(bal & ((1u << lane) - 1u));
       a.plan.pos[i] = p;
       a.plan.a_tok[p] = (int)(i / a.K);
       a.plan.a_tk[p] = (int)i;
       a.plan.a_w[p] = __ldcg(a.plan.wts + i);
-      ++p;
     }
+    base += total;
+    __syncthreads();  // s_wcnt is rewritten by the next round
   }
 }
 
