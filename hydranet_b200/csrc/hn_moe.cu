@@ -377,12 +377,19 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   // 3. the last CTA to finish builds the plan (small routings; larger ones
   // are planned by plan_kernel, launched after this kernel)
   if (!a.plan_here) return;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = (atomicAdd(a.plan.route_ctr, 1) == a.T - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
+  // A single token's CTA holds the whole routing already: no election, and
+  // the plan reads it from shared memory instead of back from global memory.
+  const bool solo = gridDim.x == 1;
+  if (solo) {
+    __syncthreads();
+  } else {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(a.plan.route_ctr, 1) == a.T - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+  }
   int* cnt = reinterpret_cast<int*>(rsm);  // reuse (>= E ints available: H >= 128 floats)
   int* off = cnt + a.E;
   const int TK = a.T * a.K;
@@ -393,8 +400,8 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   for (int e = tid; e < a.E; e += 256) cnt[e] = 0;
   if (in_smem)
     for (int i = tid; i < TK; i += 256) {
-      pidx[i] = __ldcg(a.plan.idx + i);
-      pwts[i] = __ldcg(a.plan.wts + i);
+      pidx[i] = solo ? s_idx[i] : __ldcg(a.plan.idx + i);
+      pwts[i] = solo ? s_w[i] : __ldcg(a.plan.wts + i);
     }
   __syncthreads();
   for (int i = tid; i < TK; i += 256) atomicAdd(&cnt[in_smem ? pidx[i] : __ldcg(a.plan.idx + i)], 1);
