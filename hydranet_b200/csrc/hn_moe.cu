@@ -1551,7 +1551,10 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.wts = take(4 * TK);
   l.xp = take((size_t)(Kin / 128) * T * kChunk);
   l.hp = take(F ? (size_t)(F / 128) * TK * kChunk : 0);
-  l.has_xs = F && combine && TK > kPlanSmemEntries;  // the plan kernel stages routed gate/up tokens in assignment order
+  // routed gate/up tokens staged in assignment order, read by TMA instead of
+  // gathered token by token: pays for its extra copy from a mean of 12
+  // assignments per expert (e.g. Mixtral at 64 tokens) and 32-token segments
+  l.has_xs = F && combine && nt >= 4 && TK >= 12 * E;
   l.xs = take(l.has_xs ? (size_t)(Kin / 128) * TK * kChunk : 0);
   const size_t part = (size_t)P * 2 * 8 * (8 * nt) * 32 * 4;  // [CTA][2 slots][fold warp][N][32] fp32
   l.part1 = take(F ? part : 0);
@@ -1639,11 +1642,11 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
     PlanArgs pa{ra.T, ra.K, ra.E, ra.seg, ra.plan};
     plan_kernel<<<ra.E, 256, (size_t)ra.E * 4, s>>>(pa);
     HN_CUDA(cudaGetLastError());
-    if (ra.plan.xs) {
-      stage_rows_kernel<<<(unsigned)((TK + 7) / 8), 256, 0, s>>>(ra.plan.a_tok, (int)TK, ra.plan.xp, ra.plan.xs,
-                                                                  (int64_t)(ra.H / 128) * kChunk);
-      HN_CUDA(cudaGetLastError());
-    }
+  }
+  if (ra.plan.xs) {
+    stage_rows_kernel<<<(unsigned)((TK + 7) / 8), 256, 0, s>>>(ra.plan.a_tok, (int)TK, ra.plan.xp, ra.plan.xs,
+                                                                (int64_t)(ra.H / 128) * kChunk);
+    HN_CUDA(cudaGetLastError());
   }
   return HN_OK;
 }
