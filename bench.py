@@ -135,7 +135,7 @@ def prefill_measure(args, dev):
 
 # DRAM bytes (read + write) of one gate/up engine launch, from the ncu capture
 # summarised in profiles/ (per launch, same workload); None where not captured.
-GATEUP_TRAFFIC = {64: 493565952}
+GATEUP_TRAFFIC = {64: 493860096}
 
 
 def blob_bytes(h, f, g=128):
@@ -264,6 +264,19 @@ def cpu_oracle_time(T: int, budget_s: float = 15.0, max_steps: int = 50):
         if el > budget_s or steps >= max_steps:
             break
     return T * steps / el, steps, el
+
+
+def decode_launches(T: int) -> int:
+    """Kernels one layer step launches at config 2, mirroring the library's
+    choices: prep, gate/up and down, plus the router GEMM from 256 tokens,
+    the multi-CTA planner and the combine pass above 4096 assignments, and the
+    assignment-ordered token copy from 12 assignments per expert (T > 16)."""
+    tk = T * TOPK
+    n = 3
+    n += T >= 256
+    n += 2 * (tk > 4096)
+    n += T > 16 and tk >= 12 * E
+    return int(n)
 
 
 def prefill_cpu_time(budget_s: float = 10.0, n_tok: int = 256, n_exp: int = 16):
@@ -579,7 +592,7 @@ def main():
                           "kernel": "expert-parallel layer step per rank (route, all-to-all, experts, all-to-all)"}),
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e_ms},
-            "gpu_launches": (3 if not ep else 5) * args.steps,
+            "gpu_launches": (decode_launches(T) if not ep else 5) * args.steps,
             "clocks": hr["clocks"],
             "cpu_baseline": cpu,
             "prefill": prefill,
