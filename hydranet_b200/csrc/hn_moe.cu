@@ -353,13 +353,23 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   } else if (tid == 0) {
     for (int k = 0; k < a.K; ++k) {
       if (a.mode == ROUTE_GIVEN) {
+        // -1 marks an unused slot: a token with only unused slots is left out
+        // of the plan; unused slots next to real picks are weight-0 picks
+        int n_unused = 0;
+        for (int kk = 0; kk < a.K; ++kk) n_unused += a.given_idx[(int64_t)t * a.K + kk] == -1;
         int e = a.given_idx[(int64_t)t * a.K + k];
-        if (e < 0 || e >= a.E) {
+        float w = a.given_w[(int64_t)t * a.K + k];
+        if (e == -1) {
+          if (n_unused < a.K) {
+            e = 0;
+            w = 0.f;
+          }
+        } else if (e < 0 || e >= a.E) {
           atomicExch(a.plan.err, DEV_ERR_BAD_INDEX);
           e = 0;
         }
         s_idx[k] = e;
-        s_w[k] = a.given_w[(int64_t)t * a.K + k];
+        s_w[k] = w;
       } else {
         s_idx[k] = 0;
         s_w[k] = 1.0f;
@@ -404,7 +414,10 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
       pwts[i] = solo ? s_w[i] : __ldcg(a.plan.wts + i);
     }
   __syncthreads();
-  for (int i = tid; i < TK; i += 256) atomicAdd(&cnt[in_smem ? pidx[i] : __ldcg(a.plan.idx + i)], 1);
+  for (int i = tid; i < TK; i += 256) {
+    const int e = in_smem ? pidx[i] : __ldcg(a.plan.idx + i);
+    if (e >= 0) atomicAdd(&cnt[e], 1);  // -1: a skipped token's slot
+  }
   __syncthreads();
   if (tid == 0) {
     int o = 0, ns = 0, ns2 = 0;
@@ -421,8 +434,12 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
     *a.plan.n_segs = ns;
     if (a.plan.seg2) *a.plan.n_segs2 = ns2;
     *a.plan.route_ctr = 0;
+    s_idx[0] = o;  // assignments planned (skipped tokens' slots excluded)
   }
   __syncthreads();
+  // positions past the planned assignments (left by skipped tokens) name
+  // token 0, so a copy over all T*K positions stays in bounds
+  for (int p = s_idx[0] + tid; p < TK; p += 256) a.plan.a_tok[p] = 0;
   // per-expert assignment order: by token, then by top-k slot (ballot over 32
   // tokens at a time); a token listing the same expert twice gets two slots
   for (int e = warp; e < a.E; e += 8) {
@@ -600,7 +617,10 @@ __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
   const int64_t TK = (int64_t)a.T * a.K;
   for (int i = tid; i < a.E; i += 256) cnt[i] = 0;
   __syncthreads();
-  for (int64_t i = tid; i < TK; i += 256) atomicAdd(&cnt[__ldcg(a.plan.idx + i)], 1);
+  for (int64_t i = tid; i < TK; i += 256) {
+    const int x = __ldcg(a.plan.idx + i);
+    if (x >= 0) atomicAdd(&cnt[x], 1);  // -1: a skipped token's slot
+  }
   __syncthreads();
   if (tid == 0) {
     const int s2 = a.plan.seg2;
@@ -620,6 +640,9 @@ __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
     if (e == a.E - 1) {
       *a.plan.n_segs = ns;
       if (s2) *a.plan.n_segs2 = ns2;
+      // positions past the planned assignments (skipped tokens' slots) name
+      // token 0, so a copy over all T*K positions stays in bounds
+      for (int64_t q = o + m; q < TK; ++q) a.plan.a_tok[q] = 0;
     }
   }
   // this expert's assignments in (token, slot) order: coalesced rounds of

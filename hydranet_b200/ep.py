@@ -2,24 +2,29 @@
 
 Experts are partitioned in contiguous blocks: rank ``r`` of ``W`` owns experts
 ``[r*E/W, (r+1)*E/W)`` (GLM-4.5-Air: 64/32/16 experts per GPU at 2/4/8).
-Each rank routes its own tokens, then per layer:
+Each rank routes its own tokens, then per layer, all on the device (no
+host synchronisation, so the host keeps queueing work):
 
-1. ``all_to_all_single`` of per-destination assignment counts (int64), read
-   back to size the exchange;
-2. one variable-split ``all_to_all_single`` of byte rows, each the routed
-   token's activations followed by its (local expert, routing weight) pair;
-3. the rank's grouped kernel over what it received, with caller-supplied
-   routing (``hn_moe_experts_int4``: each received row is one assignment,
-   top-1 with its routing weight, so the kernel returns weight * MLP_e(x));
-4. the mirror ``all_to_all_single`` of the weighted rows back to their source
-   ranks, summed per token in float32 and cast to the activation dtype.
+1. the T*k assignments are grouped by owner rank and placed into a send
+   buffer of W blocks of C = T*k fixed slots (any split of the assignments
+   fits), one byte row per slot: the token's activations, its global expert
+   id (int32, -1 in an unused slot) and its routing weight (float32);
+2. one ``all_to_all_single`` with equal splits delivers block r to rank r;
+3. the rank's grouped kernel runs over the W*C received rows with
+   caller-supplied routing (``hn_moe_experts_int4``: top-1 per row with its
+   routing weight, so it returns weight * MLP_e(x); rows whose id is -1 are
+   skipped and cost no expert work);
+4. the mirror ``all_to_all_single`` returns the rows to their source ranks,
+   which sum the k rows of each token in slot order in float32 and cast to
+   the activation dtype.
 
 The reference runs experts one at a time in Python on one GPU
-(``model/glm4.py:375-473``, ``model/mixtral.py:282-370``); the exchange is the
+(``model/mixtral.py:282-370``, ``model/glm4.py:375-473``); the exchange is the
 standard expert-parallel dispatch/combine.  One row is sent per (token, slot)
-assignment, which keeps the combine order fixed (slot order), so results do
-not depend on the number of ranks beyond fp32 summation of the k partial
-outputs.
+assignment and the combine order is the slot order, so results do not depend
+on the number of ranks beyond fp32 summation of the k partial outputs.  The
+fixed slots trade a few MB of padding per step (W*T*k rows, mostly empty) for
+split sizes that never have to be read back to the host.
 
 ``local_fn`` computes step 3 and defaults to the CUDA grouped kernel; tests
 on CPU ranks (gloo) pass a reference implementation to check the exchange
@@ -46,33 +51,6 @@ def owner_of(expert: torch.Tensor, num_experts: int, world: int) -> torch.Tensor
     return torch.div(expert, num_experts // world, rounding_mode="floor")
 
 
-class DispatchPlan:
-    """Host-free bookkeeping of one exchange (all tensors stay on the device).
-
-    ``order``     assignment ids (t*k + slot) sorted by destination rank, stable;
-    ``send``      rows sent to each rank; ``recv`` rows received from each rank.
-    """
-
-    def __init__(self, idx: torch.Tensor, num_experts: int, world: int, group=None):
-        T, k = idx.shape
-        dest = owner_of(idx.reshape(-1), num_experts, world)
-        self.order = torch.sort(dest, stable=True).indices
-        self.send = torch.bincount(dest, minlength=world).to(torch.int64)
-        self.recv = torch.empty_like(self.send)
-        dist.all_to_all_single(self.recv, self.send, group=group)
-        # split sizes must be host ints for all_to_all_single: one device->host read
-        self.send_splits, self.recv_splits = torch.stack([self.send, self.recv]).tolist()
-        self.T, self.k = T, k
-
-
-def exchange(t: torch.Tensor, plan: DispatchPlan, forward: bool, group=None) -> torch.Tensor:
-    """Variable-split all-to-all of rows of ``t`` (dispatch if ``forward``, else combine)."""
-    ins, outs = (plan.send_splits, plan.recv_splits) if forward else (plan.recv_splits, plan.send_splits)
-    out = torch.empty((sum(outs),) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-    dist.all_to_all_single(out, t.contiguous(), output_split_sizes=outs, input_split_sizes=ins, group=group)
-    return out
-
-
 def ep_moe_forward(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_experts: int,
                    local_fn: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor],
                    group=None) -> torch.Tensor:
@@ -80,31 +58,46 @@ def ep_moe_forward(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_expe
 
     x [T, H] (this rank's tokens), idx [T, k] global expert ids, w [T, k]
     routing weights.  ``local_fn(rows [n, H], local_expert [n], weight [n])``
-    returns weight * MLP_e(row) for each received row (activation dtype).
+    returns weight * MLP_e(row) for each received row whose local expert is
+    >= 0 (activation dtype); rows with local expert -1 are unused slots and
+    their outputs are ignored.
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     T, H = x.shape
     k = idx.shape[1]
+    dev = x.device
     first, _ = expert_range(num_experts, rank, world)
-    plan = DispatchPlan(idx, num_experts, world, group)
-    tok = torch.div(plan.order, k, rounding_mode="floor")
-    # one byte row per assignment: the token's activations, then the local
-    # expert id (int32) and the routing weight (float32), so the dispatch is a
-    # single all-to-all
+    n = T * k
+    C = n  # slots per destination block
+    flat = idx.reshape(-1)
+    dest = owner_of(flat, num_experts, world)
+    order = torch.sort(dest, stable=True).indices  # assignments grouped by destination, slot order kept
+    d_sorted = dest.index_select(0, order)
+    counts = torch.bincount(dest, minlength=world)
+    starts = torch.cumsum(counts, 0) - counts
+    row = d_sorted * C + (torch.arange(n, device=dev) - starts.index_select(0, d_sorted))
+    tok = torch.div(order, k, rounding_mode="floor")
     rb = H * x.element_size()
-    packed = torch.empty(tok.numel(), rb + 8, dtype=torch.uint8, device=x.device)
+    # send buffer: W blocks of C rows; unused rows carry expert id -1 (0xFF bytes)
+    send = torch.zeros(world * C, rb + 8, dtype=torch.uint8, device=dev)
+    send[:, rb:rb + 4] = 255
+    packed = torch.empty(n, rb + 8, dtype=torch.uint8, device=dev)
     packed[:, :rb] = x.index_select(0, tok).view(torch.uint8).view(-1, rb)
-    packed[:, rb:rb + 4] = idx.reshape(-1).index_select(0, plan.order).to(torch.int32).view(-1, 1).view(torch.uint8)
-    packed[:, rb + 4:] = w.reshape(-1).index_select(0, plan.order).to(torch.float32).view(-1, 1).view(torch.uint8)
-    recv = exchange(packed, plan, True, group)
+    packed[:, rb:rb + 4] = flat.index_select(0, order).to(torch.int32).view(-1, 1).view(torch.uint8)
+    packed[:, rb + 4:] = w.reshape(-1).index_select(0, order).to(torch.float32).view(-1, 1).view(torch.uint8)
+    send.index_copy_(0, row, packed)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
     r_rows = recv[:, :rb].contiguous().view(x.dtype).view(-1, H)
-    local = recv[:, rb:rb + 4].contiguous().view(torch.int32).view(-1) - first  # global id -> this rank's
+    g = recv[:, rb:rb + 4].contiguous().view(torch.int32).view(-1)
+    local = torch.where(g >= 0, g - first, g)  # global id -> this rank's; -1 stays
     r_w = recv[:, rb + 4:].contiguous().view(torch.float32).view(-1)
-    y = local_fn(r_rows, local, r_w) if r_rows.shape[0] else r_rows.new_zeros((0, H))
-    back = exchange(y, plan, False, group)
-    out = torch.zeros(T, H, dtype=torch.float32, device=x.device)
-    out.index_add_(0, tok, back.to(torch.float32))
+    y = local_fn(r_rows, local, r_w)
+    back = torch.empty_like(y)
+    dist.all_to_all_single(back, y.contiguous(), group=group)
+    out = torch.zeros(T, H, dtype=torch.float32, device=dev)
+    out.index_add_(0, tok, back.index_select(0, row).to(torch.float32))
     return out.to(x.dtype)
 
 
@@ -114,6 +107,7 @@ def cuda_local_fn(table):
     from .moe import moe_experts
 
     def fn(rows: torch.Tensor, local_expert: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+        # local expert -1 (an unused slot) is skipped by the kernel
         return moe_experts(rows, local_expert.view(-1, 1).to(torch.int32), weight.view(-1, 1), table)
 
     return fn

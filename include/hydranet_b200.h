@@ -185,7 +185,12 @@ HN_API int hn_moe_layer_int4_phase(int phase, const void* x, int dtype, int64_t 
 
 /* Same as hn_moe_layer_int4 but with routing supplied by the caller
  * (topk_idx int32 [T, k], topk_w float32 [T, k]); used for expert-parallel
- * shards and for callers that route on their own. */
+ * shards and for callers that route on their own.  An index of -1 marks an
+ * unused slot: a token whose k slots are all -1 is skipped (no expert work;
+ * its output row is left unspecified), and -1 slots of a token with other
+ * picks count as weight-0 picks.  Other indices outside [0, E) are read as
+ * expert 0 and set error code 2 in the workspace's error word
+ * (hn_workspace_error). */
 HN_API int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
                         int top_k, const int32_t* topk_idx, const float* topk_w,
                         const hn_expert_ptrs* experts, const void* expert_maps, void* out,

@@ -56,6 +56,8 @@ def worker(rank, world, port, T, force_idx, results):
             rr = rows.numpy().astype(np.float32)
             out = np.zeros_like(rr)
             for i in range(rr.shape[0]):
+                if int(local_e[i]) < 0:
+                    continue  # an unused slot of the fixed-size exchange
                 e = first + int(local_e[i])
                 assert first <= e < last
                 out[i] = float(weight[i]) * experts[e](rr[i:i + 1])[0]

@@ -212,3 +212,31 @@ def test_driver_smoke_entry(lib):
     """The driver's smoke() (one small layer on cuda:0 against the oracle) runs clean."""
     import __graft_entry__
     __graft_entry__.smoke()
+
+
+@pytest.mark.parametrize("T,k,E", [(37, 2, 6), (100, 1, 4), (5000, 1, 4)])
+def test_given_routing_unused_slots(lib, T, k, E):
+    """Index -1 marks an unused slot (the expert-parallel exchange pads with
+    them): tokens whose slots are all -1 are skipped, -1 next to real picks
+    counts as a weight-0 pick; the other tokens match the oracle.  Sizes cover
+    the gathered and the assignment-ordered token paths and the multi-CTA
+    planner (T*k > 4096)."""
+    shape = synth.MoEShape(256, 256, E, k)
+    table, packed = host_moe(shape, 70 + T)
+    rng = np.random.default_rng(T)
+    idx = rng.integers(0, E, size=(T, k)).astype(np.int32)
+    w = rng.random((T, k)).astype(np.float32)
+    skip = rng.random(T) < 0.4
+    idx[skip] = -1
+    if k > 1:
+        part = (~skip) & (rng.random(T) < 0.3)
+        idx[part, 0] = -1
+    x = act(rng.standard_normal((T, 256), dtype=np.float32), "bf16")
+    out = moe_experts(x, torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), table)
+    keep = ~skip
+    ref_idx = np.where(idx < 0, 0, idx).astype(np.int64)
+    ref_w = np.where(idx < 0, 0.0, w).astype(np.float32)
+    ref = R.moe_combine_ref(to_np32(x)[keep], ref_idx[keep], ref_w[keep], oracle_experts(packed))
+    assert rel_l2(to_np32(out)[keep], ref) <= TIGHT
+    for ws in _lib.workspaces.all():
+        assert _lib.workspace_error(ws) == 0
