@@ -74,7 +74,8 @@ def ep_moe_forward(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_expe
     dest = owner_of(flat, num_experts, world)
     order = torch.sort(dest, stable=True).indices  # assignments grouped by destination, slot order kept
     d_sorted = dest.index_select(0, order)
-    counts = torch.bincount(dest, minlength=world)
+    # per-destination counts without torch.bincount (which reads its maximum back to the host)
+    counts = torch.zeros(world, dtype=dest.dtype, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
     starts = torch.cumsum(counts, 0) - counts
     row = d_sorted * C + (torch.arange(n, device=dev) - starts.index_select(0, d_sorted))
     tok = torch.div(order, k, rounding_mode="floor")
