@@ -441,10 +441,43 @@ def main():
                 touched.append(int(torch.unique(idx).numel()))
         algo_bytes = statistics.mean(touched) * blob_bytes(H, F) + 2 * T * H * 2 + E * H * 2
         if ep:
-            # eager steps (the exchange sizes its all-to-all splits on the host)
+            # The exchange never reads back to the host, so each layer's step
+            # (route, all-to-all, local experts, all-to-all, combine) is
+            # captured in a CUDA graph; every rank must capture for any to
+            # replay (a MIN over ranks), otherwise all ranks time eager steps.
+            graphs, note = None, None
             with torch.no_grad():
+                try:
+                    s = torch.cuda.Stream(dev)
+                    s.wait_stream(torch.cuda.current_stream(dev))
+                    with torch.cuda.stream(s):
+                        for li, layer in enumerate(layers):
+                            layer(xs[li])  # warm-up on the capture stream (workspaces, communicators)
+                        torch.cuda.synchronize(dev)
+                        graphs = []
+                        for li, layer in enumerate(layers):
+                            g = torch.cuda.CUDAGraph()
+                            with torch.cuda.graph(g, stream=s):
+                                layer(xs[li])
+                            graphs.append(g)
+                    torch.cuda.current_stream(dev).wait_stream(s)
+                    torch.cuda.synchronize(dev)
+                except Exception as exc:  # noqa: BLE001 - any capture failure falls back to eager steps
+                    graphs, note = None, repr(exc)[:200]
+                    torch.cuda.synchronize(dev)
+                ok = torch.tensor([1 if graphs else 0], device=dev, dtype=torch.int32)
+                dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+                if int(ok.item()) == 0:
+                    graphs = None
+
+                def step(i):
+                    if graphs:
+                        graphs[i % n_layers].replay()
+                    else:
+                        layers[i % n_layers](xs[i % n_layers])
+
                 for i in range(args.warmup):
-                    layers[i % n_layers](xs[i % n_layers])
+                    step(i)
                 torch.cuda.synchronize(dev)
                 barrier()
                 torch.cuda.synchronize(dev)
@@ -452,15 +485,25 @@ def main():
                 with ClockSampler(local) as clk:
                     ev0.record()
                     for i in range(args.steps):
-                        layers[i % n_layers](xs[i % n_layers])
+                        step(i)
                     ev1.record()
                     torch.cuda.synchronize(dev)
             ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
             barrier()
             results[T] = {"ms_per_step": ms, "tok_s": world * T / (ms * 1e-3),
                           "touched_experts": statistics.mean(touched), "algo_bytes": algo_bytes,
-                          "gbs": algo_bytes / (ms * 1e-3) / 1e9, "clocks": clk.summary()}
+                          "gbs": algo_bytes / (ms * 1e-3) / 1e9, "clocks": clk.summary(),
+                          "cuda_graph": bool(graphs)}
+            if note and rank == 0:
+                results[T]["graph_note"] = note
             results[T]["frac"] = results[T]["gbs"] / hbm_peak
+            # graphs holding NCCL work are released before the process group
+            # goes (every reference: the list and the capture loop's variable),
+            # or its teardown waits for good
+            for gr in graphs or []:
+                gr.reset()
+            graphs, g, gr = None, None, None
+            torch.cuda.synchronize(dev)
             continue
         # capture one graph per layer (warm up on a side stream first)
         s = torch.cuda.Stream(dev)
@@ -580,7 +623,7 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, weights ~N(0,0.02) INT4 g128)",
             "config": {"workload": WORKLOAD, "tokens": T, "hidden": H, "ffn": F, "experts": E, "top_k": TOPK,
                        "group_size": 128, "layers_rotated": n_layers, "l2": "weights per step > L2 (126 MB), "
-                       f"{n_layers} distinct layers rotated", "cuda_graph": True,
+                       f"{n_layers} distinct layers rotated", "cuda_graph": bool(hr.get("cuda_graph", True)),
                        "parallelism": f"ep{world} (experts sharded, NCCL all-to-all)" if ep else "single"},
             "roofline": ({"bound": "hbm", "achieved": gu_bytes / (gu_ms * 1e-3) / 1e9, "peak": hbm_peak,
                           "unit": "GB/s", "frac": gu_bytes / (gu_ms * 1e-3) / 1e9 / hbm_peak,

@@ -77,7 +77,9 @@ class TopKRouter(nn.Module):
         bonus = self.bonus_vector(x.device) if apply_affinity else None
         idx, w, logits = ops.moe_route(x, self.params(top_k, bonus), self.num_experts, keep_refs=(bonus,))
         if not self.training:
-            self.usage_counts += torch.bincount(idx.reshape(-1).long(), minlength=self.num_experts)
+            # scatter_add_, not torch.bincount: bincount reads its maximum back to the host
+            flat = idx.reshape(-1).long()
+            self.usage_counts.scatter_add_(0, flat, torch.ones_like(flat))
         return RouterOutput(idx.long().view(b, s, top_k), w.to(hidden_states.dtype).view(b, s, top_k),
                             logits.view(b, s, self.num_experts))
 

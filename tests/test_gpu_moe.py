@@ -191,6 +191,28 @@ def test_cuda_graph_capture(lib):
     assert torch.equal(y, ref)
 
 
+def test_router_usage_counts_capturable(lib):
+    """``usage_counts`` (``model/router.py:177-182``) counts every pick, and a
+    router call has no host read, so it can be captured in a graph."""
+    r = TopKRouter(hidden_dim=512, num_experts=8, experts_per_token=2).cuda().to(torch.bfloat16).eval()
+    x = torch.randn(1, 40, 512, device="cuda", dtype=torch.bfloat16)
+    ro = r(x)
+    want = torch.bincount(ro.expert_indices.reshape(-1), minlength=8)
+    assert torch.equal(r.usage_counts, want)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        r(x)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            r(x)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(r.usage_counts, 3 * want)  # first call, side-stream call, replay (capture runs nothing)
+
+
 def test_phase_split_equals_one_call(lib):
     """hn_moe_layer_int4_phase 1, 2, 3 in order == one hn_moe_layer_int4 call, bit for bit."""
     shape = synth.MoEShape(1024, 768, 8, 2)
