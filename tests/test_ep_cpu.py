@@ -1,4 +1,4 @@
-"""Expert-parallel dispatch/combine bookkeeping on CPU ranks (gloo, world size 2).
+"""Expert-parallel dispatch/combine bookkeeping on CPU ranks (gloo, world sizes 2 and 4).
 
 Each rank routes its own tokens with the oracle router, exchanges rows with
 ``hydranet_b200.ep.ep_moe_forward`` and runs its share of the experts with a
@@ -95,6 +95,13 @@ def test_ep_uneven_and_empty_splits_and_duplicates():
     f0 = np.array([[5, 5, 7], [6, 4, 5], [7, 7, 7]], dtype=np.int64)
     f1 = np.array([[0, 1, 2], [3, 3, 0], [1, 2, 3]], dtype=np.int64)
     errs = run(2, 3, force_idx={0: f0, 1: f1})
+    assert max(errs) < 1e-5, errs
+
+
+def test_ep_four_ranks():
+    """Four ranks, two experts each (the layout of the 4-GPU bench run);
+    token counts differ per rank only through routing, as in the bench."""
+    errs = run(4, 6)
     assert max(errs) < 1e-5, errs
 
 
