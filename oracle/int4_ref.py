@@ -92,6 +92,32 @@ def dequantize_tensor(packed: np.ndarray, scales: np.ndarray, group_size: int = 
     return (qg * scales.astype(np.float32)[:, :, None]).astype(np.float16).reshape(out_f, in_f)
 
 
+def int4linear_quantize_ref(w: np.ndarray, group_size: int = 128):
+    """Quantiser of the non-expert ``Int4Linear`` (``kernels/int4_linear.py:69-103``).
+
+    Differs from the expert packer: the group absmax is clamped to 1e-8 first
+    (``:90``), the stored scale is ``absmax / 7`` cast to float16 (``:92``), and
+    the integer is ``round_half_even(w / absmax * 7)`` (``:95``), two roundings
+    in ``w.dtype``.  Same nibble order (even column in the low nibble, ``:103``).
+    float32 and float16 inputs; an all-zero float16 group is left undefined,
+    as in the reference (0/0 cast to int8).
+    """
+    out_f, in_f = w.shape
+    if in_f % group_size != 0:
+        raise ValueError(f"in_features {in_f} must be divisible by group_size {group_size}")
+    dt = w.dtype
+    if dt not in (np.float32, np.float16):
+        raise TypeError(f"unsupported weight dtype {dt}")
+    g = w.reshape(out_f, in_f // group_size, group_size)
+    absmax = np.maximum(np.abs(g).max(axis=-1, keepdims=True), dt.type(1e-8)).astype(dt)
+    scales = (absmax / dt.type(7.0)).astype(dt).astype(np.float16)[:, :, 0]
+    ratio = (g / absmax).astype(dt)
+    q = np.clip(np.rint((ratio * dt.type(7.0)).astype(dt)), -8, 7).astype(np.int8)
+    u = (q.astype(np.int16) + 8).astype(np.uint8).reshape(out_f, in_f)
+    packed = ((u[:, 1::2] << 4) | u[:, 0::2]).astype(np.uint8)
+    return np.ascontiguousarray(packed), np.ascontiguousarray(scales)
+
+
 @dataclass
 class BlobLayout:
     """Byte offsets of the six tensors inside one expert blob.

@@ -3,7 +3,8 @@
 
 This script imports HydraNet itself (read-only) and records what the
 reference computes on seeded synthetic inputs: its packer, its dequantiser,
-its two routers and its MoE layers in dequant mode.  The fixtures pin the
+the non-expert ``Int4Linear`` quantiser, its two routers and its MoE
+layers in dequant mode.  The fixtures pin the
 numpy oracle under ``oracle/``; the GPU box never runs this script (the
 reference is not there), it only reads the committed ``.npz`` files.
 
@@ -87,6 +88,37 @@ def pack_cases(torch, ExpertWeightPacker, QuantConfig):
     e[4] *= 1e-30
     e[5] = -np.abs(e[5])
     add("edge_f32", e.astype(np.float32))
+    return cases
+
+
+def int4linear_cases(torch, Int4Linear):
+    """The non-expert ``Int4Linear`` quantiser (``kernels/int4_linear.py:69-103``)
+    and ``from_float``'s group-size choice (``:121-131``)."""
+    cases = {}
+
+    def add(name, w, gs):
+        p, s = Int4Linear.quantize_weight(torch.from_numpy(w.copy()), gs)
+        cases[name + "/w"] = w
+        cases[name + "/packed"] = p.numpy()
+        cases[name + "/scales"] = s.numpy()
+        cases[name + "/group_size"] = np.int64(gs)
+
+    add("rand_f32", synth.host_normal(21, (32, 512), 0.02), 128)
+    add("rand_f16", synth.host_normal(22, (48, 256), 0.05).astype(np.float16), 128)
+    add("g64_f32", synth.host_normal(23, (16, 192), 0.1), 64)
+    e = synth.host_normal(24, (6, 256), 1.0)
+    e[0, :128] = 0.0                                    # all-zero group: absmax clamps to 1e-8
+    e[1, :128] = np.float32(3.5) * (np.arange(128, dtype=np.float32) % 3 - 1)  # w/absmax*7 = -7, 0, 7
+    e[1, 128:142] = np.array([0.5, 1.5, 2.5, -0.5, -1.5, -2.5, 3.5, -3.5, 4.5, -4.5, 5.5, -5.5, 6.5, -6.5],
+                             dtype=np.float32)
+    e[1, 142] = 7.0                                     # absmax 7: halves above are exact ties
+    e[2] *= 1e4
+    e[3] *= 1e-20
+    e[4] = -np.abs(e[4])
+    add("edge_f32", e.astype(np.float32), 128)
+    for n_in in (256, 192, 96):
+        m = Int4Linear.from_float(torch.nn.Linear(n_in, 8), group_size=128)
+        cases[f"from_float_group/{n_in}"] = np.int64(m.group_size)
     return cases
 
 
@@ -239,10 +271,15 @@ def glm_router(torch, base_seed, shape, tokens, dtype):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--only", default=None, help="write only this fixture (file stem)")
     args = ap.parse_args()
     ref = import_reference(args.reference.resolve())
     import torch
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    from hydranet.kernels.int4_linear import Int4Linear
+    np.savez_compressed(HERE / "int4linear_quant.npz", **int4linear_cases(torch, Int4Linear))
+    if args.only == "int4linear_quant":
+        return
     from hydranet.preprocess.pack_weights import ExpertWeightPacker, QuantConfig
 
     np.savez_compressed(HERE / "pack_cases.npz", **pack_cases(torch, ExpertWeightPacker, QuantConfig))

@@ -56,6 +56,27 @@ def test_int4_linear_3d_and_strided(lib):
     assert rel_l2(to_np32(out.reshape(6, 384)), ref) <= TIGHT["bf16"]
 
 
+@pytest.mark.parametrize("dtype,bias", [("f16", True), ("f16", False), ("bf16", True)])
+def test_int4linear_module(lib, dtype, bias):
+    """``Int4Linear.from_float`` and its forward (``kernels/int4_linear.py:105-168``):
+    the engine's output plus the float16 bias, with the reference's type
+    promotion (a bf16 input plus the float16 bias gives float32)."""
+    from hydranet_b200.kernels import Int4Linear
+    torch.manual_seed(3)
+    lin = torch.nn.Linear(1024, 384, bias=bias)
+    m = Int4Linear.from_float(lin, device=torch.device("cuda"))
+    p, s = R.int4linear_quantize_ref(lin.weight.detach().numpy())
+    assert np.array_equal(m.weight_packed.cpu().numpy(), p)
+    x = act(np.random.default_rng(4).standard_normal((14, 1024), dtype=np.float32), dtype).view(2, 7, 1024)
+    y = m(x)
+    want_dtype = x.dtype if (not bias or dtype == "f16") else torch.float32
+    assert y.shape == (2, 7, 384) and y.dtype == want_dtype
+    ref = R.int4_linear_ref(to_np32(x.reshape(14, 1024)), p, s)
+    if bias:
+        ref = ref + lin.bias.detach().numpy().astype(np.float16).astype(np.float32)
+    assert rel_l2(to_np32(y.reshape(14, 384)), ref) <= TIGHT[dtype]
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 def test_silu_mul(lib, dtype):
     g = act(np.random.default_rng(0).standard_normal((7, 1000), dtype=np.float32) * 3, dtype)
