@@ -156,6 +156,12 @@ class _Workspaces:
         with self._lock:
             buf = self._ws.get(key)
             if buf is None or buf.numel() < nbytes:
+                if torch.cuda.is_current_stream_capturing():
+                    # a buffer made during capture is only zeroed when the graph
+                    # replays, so eager calls would find its counters unset
+                    raise RuntimeError(
+                        f"hydranet_b200: the workspace of this stream needs {nbytes} bytes; make one call of "
+                        "the same shape on this stream outside CUDA-graph capture before capturing")
                 size = max(nbytes, 1 << 20)
                 if buf is not None:
                     size = max(size, buf.numel() * 2)

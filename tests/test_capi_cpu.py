@@ -3,6 +3,7 @@
 * the library loads and exports every entry point ``include/hydranet_b200.h`` declares;
 * the ctypes table in ``hydranet_b200/_lib.py`` binds exactly those;
 * workspace-size queries behave; ops refuse CPU tensors (no CPU fallback);
+* the workspace cache refuses to allocate during CUDA-graph capture;
 * the packed-format helpers agree with the reference layout.
 """
 
@@ -122,3 +123,14 @@ def test_expert_slot_views_are_aligned():
     for t in s.tensors():
         assert t.data_ptr() % 16 == 0
     ExpertTable([s, ExpertSlot(4096, 1408, 128, device="cpu")])
+
+
+def test_workspace_not_made_during_graph_capture(monkeypatch):
+    """A workspace allocated inside CUDA-graph capture would only be zeroed
+    when the graph replays, so the cache refuses to make or grow one then."""
+    ws = _lib._Workspaces()
+    monkeypatch.setattr(_lib, "stream_ptr", lambda device=None: 1234)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    with pytest.raises(RuntimeError, match="outside CUDA-graph capture"):
+        ws.get(4096, torch.device("cuda:0"))
+    assert ws.all() == []
