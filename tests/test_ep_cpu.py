@@ -1,4 +1,4 @@
-"""Expert-parallel dispatch/combine bookkeeping on CPU ranks (gloo, world sizes 2 and 4).
+"""Expert-parallel dispatch/combine bookkeeping on CPU ranks (gloo, world sizes 2 and 4; Mixtral and GLM-4.5 routing).
 
 Each rank routes its own tokens with the oracle router, exchanges rows with
 ``hydranet_b200.ep.ep_moe_forward`` and runs its share of the experts with a
@@ -20,6 +20,7 @@ from hydranet_b200 import synth
 from oracle import int4_ref as R
 
 H, F, E, K = 256, 256, 8, 3
+GLM = dict(E=16, K=8, router="sigmoid")  # GLM-4.5 layout at a small size
 
 
 def free_port():
@@ -30,26 +31,29 @@ def free_port():
     return port
 
 
-def experts_oracle():
-    shape = synth.MoEShape(H, F, E, K)
+def experts_oracle(n_exp=E, k=K):
+    shape = synth.MoEShape(H, F, n_exp, k)
     out = {}
-    for e in range(E):
+    for e in range(n_exp):
         g, u, d = synth.host_expert_weights(7, shape, e)
         out[e] = R.DequantExpert.from_packed(*R.quantize_tensor(g), *R.quantize_tensor(u), *R.quantize_tensor(d))
     return out
 
 
-def worker(rank, world, port, T, force_idx, results):
+def worker(rank, world, port, T, force_idx, results, n_exp=E, k=K, router="softmax"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from hydranet_b200.ep import ep_moe_forward, expert_range
-        experts = experts_oracle()
-        first, last = expert_range(E, rank, world)
+        experts = experts_oracle(n_exp, k)
+        first, last = expert_range(n_exp, rank, world)
         x = synth.host_activations(100 + rank, T, H)
-        rw = synth.host_normal(5, (E, H), 0.02)
-        idx, w, _ = R.softmax_topk_router_ref(x, rw, K, "f32")
+        rw = synth.host_normal(5, (n_exp, H), 0.02)
+        if router == "sigmoid":
+            idx, w, _ = R.sigmoid_topk_router_ref(x, rw, k, "f32", correction_bias=synth.host_correction_bias(3, n_exp))
+        else:
+            idx, w, _ = R.softmax_topk_router_ref(x, rw, k, "f32")
         if force_idx is not None:
             idx = force_idx[rank].copy()
         def local_fn(rows, local_e, weight):
@@ -63,7 +67,7 @@ def worker(rank, world, port, T, force_idx, results):
                 out[i] = float(weight[i]) * experts[e](rr[i:i + 1])[0]
             return torch.from_numpy(out)
         y = ep_moe_forward(torch.from_numpy(x), torch.from_numpy(idx.astype(np.int64)), torch.from_numpy(w),
-                           E, local_fn)
+                           n_exp, local_fn)
         ref = R.moe_combine_ref(x, idx, w, experts)
         err = float(np.abs(y.numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
         results[rank] = err
@@ -71,11 +75,13 @@ def worker(rank, world, port, T, force_idx, results):
         dist.destroy_process_group()
 
 
-def run(world, T, force_idx=None):
+def run(world, T, force_idx=None, **layout):
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
     port = free_port()
-    procs = [ctx.Process(target=worker, args=(r, world, port, T, force_idx, results)) for r in range(world)]
+    procs = [ctx.Process(target=worker, args=(r, world, port, T, force_idx, results),
+                         kwargs={"n_exp": layout.get("E", E), "k": layout.get("K", K),
+                                 "router": layout.get("router", "softmax")}) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -102,6 +108,13 @@ def test_ep_four_ranks():
     """Four ranks, two experts each (the layout of the 4-GPU bench run);
     token counts differ per rank only through routing, as in the bench."""
     errs = run(4, 6)
+    assert max(errs) < 1e-5, errs
+
+
+def test_ep_glm_layout_four_ranks():
+    """Sigmoid top-8 with a correction bias over 16 experts, 4 experts per
+    rank: every token reaches several ranks, some more than once."""
+    errs = run(4, 5, **GLM)
     assert max(errs) < 1e-5, errs
 
 
