@@ -66,6 +66,7 @@ SIGNATURES = {
     "hn_workspace_error": (c_int, [c_void_p, c_size_t, ctypes.POINTER(c_int), c_void_p]),
     "hn_int4_linear_static": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64,
                                       c_int, c_void_p, c_int64, c_void_p]),
+    "hn_selftest_wait_timeout": (c_int, [c_void_p, c_size_t, c_int, c_void_p]),
 }
 
 _lib = None

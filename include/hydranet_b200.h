@@ -241,6 +241,14 @@ HN_API int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int64_t 
  * Copies 4 bytes device->host on 'stream' and synchronises that stream. */
 HN_API int hn_workspace_error(const void* workspace, size_t workspace_bytes, int* error_code, void* stream);
 
+/* Self-test of the failure path (no reference counterpart).  Launches one CTA
+ * whose bounded waits wait on a barrier that nothing arrives at (mode 0: the
+ * engine's polling wait and its backoff wait; mode 1: two backoff waits).
+ * After the wait limit (2 s) the kernel records the timeout (error code 1)
+ * in the workspace's error word and ends; hn_workspace_error then reports it.
+ * Needs a workspace of >= 512 bytes whose first 4 bytes are zero. */
+HN_API int hn_selftest_wait_timeout(void* workspace, size_t workspace_bytes, int mode, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
