@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from hydranet_b200 import _lib, ops, synth
+from hydranet_b200 import _lib, synth
 from hydranet_b200.moe import MoELayerInt4, moe_experts
 from hydranet_b200.router import GLM4SigmoidRouter, TopKRouter
 from oracle import int4_ref as R
