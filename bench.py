@@ -251,7 +251,7 @@ class OracleLayer:
         return self.R.moe_combine_ref(self.x, idx, w, self.experts)
 
 
-def cpu_oracle_time(T: int, budget_s: float = 15.0, max_steps: int = 50):
+def cpu_oracle_time(T: int, budget_s: float = 15.0, max_steps: int = 400):
     """tok/s of the oracle MoE layer on the host cores over a bounded sample."""
     layer = OracleLayer(T)
     layer.step()  # warm-up
