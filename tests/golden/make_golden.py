@@ -3,8 +3,8 @@
 
 This script imports HydraNet itself (read-only) and records what the
 reference computes on seeded synthetic inputs: its packer, its dequantiser,
-the non-expert ``Int4Linear`` quantiser, its two routers and its MoE
-layers in dequant mode.  The fixtures pin the
+the non-expert ``Int4Linear`` quantiser, its group-by-expert gatherer, its
+two routers and its MoE layers in dequant mode.  The fixtures pin the
 numpy oracle under ``oracle/``; the GPU box never runs this script (the
 reference is not there), it only reads the committed ``.npz`` files.
 
@@ -119,6 +119,44 @@ def int4linear_cases(torch, Int4Linear):
     for n_in in (256, 192, 96):
         m = Int4Linear.from_float(torch.nn.Linear(n_in, 8), group_size=128)
         cases[f"from_float_group/{n_in}"] = np.int64(m.group_size)
+    return cases
+
+
+def gatherer_cases(torch, GroupByExpertGatherer):
+    """The reference's group-by-expert gather and scatter
+    (``scheduler/continuous_batch.py:281-381``) on CPU tensors.  Each expert's
+    output is a fixed function of its gathered rows, ``rows * (e + 1) - e``."""
+    cases = {}
+
+    def add(name, T, k, E, H, dtype, dup=False):
+        rng = np.random.default_rng(T * 31 + k)
+        idx = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int64)
+        if dup:
+            idx[::3, 1] = idx[::3, 0]                     # some tokens pick an expert twice
+        idx[:, :][idx == 2] = 3                            # expert 2 unused
+        hid = rng.standard_normal((T, H)).astype(np.float32)
+        w = rng.random((T, k)).astype(np.float32)
+        g = GroupByExpertGatherer(device=torch.device("cpu"))
+        tdt = getattr(torch, dtype)
+        got = g.gather(torch.from_numpy(hid).to(tdt), torch.from_numpy(idx), torch.from_numpy(w).to(tdt), 5)
+        outs = [(x, x.hidden_states * (x.expert_idx + 1) - x.expert_idx) for x in got]
+        y = g.scatter(outs, (T, H))
+        cases[name + "/hidden"] = hid
+        cases[name + "/idx"] = idx
+        cases[name + "/w"] = w
+        cases[name + "/dtype"] = np.array(dtype)
+        cases[name + "/experts"] = np.array([x.expert_idx for x in got], dtype=np.int64)
+        cases[name + "/counts"] = np.array([x.num_tokens for x in got], dtype=np.int64)
+        cases[name + "/layer"] = np.array([x.layer_idx for x in got], dtype=np.int64)
+        cases[name + "/tokens"] = torch.cat([x.token_indices for x in got]).numpy()
+        cases[name + "/weights"] = torch.cat([x.routing_weights for x in got]).float().numpy()
+        cases[name + "/rows"] = torch.cat([x.hidden_states for x in got]).float().numpy()
+        cases[name + "/scatter"] = y.float().numpy()
+        cases[name + "/scatter_dtype"] = np.array(str(y.dtype))
+
+    add("f32", 37, 3, 8, 16, "float32")
+    add("f32_dup", 25, 4, 6, 8, "float32", dup=True)
+    add("f16", 19, 2, 8, 8, "float16")
     return cases
 
 
@@ -277,8 +315,13 @@ def main():
     import torch
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     from hydranet.kernels.int4_linear import Int4Linear
-    np.savez_compressed(HERE / "int4linear_quant.npz", **int4linear_cases(torch, Int4Linear))
-    if args.only == "int4linear_quant":
+    from hydranet.scheduler.continuous_batch import GroupByExpertGatherer
+    light = {"int4linear_quant": lambda: int4linear_cases(torch, Int4Linear),
+             "gatherer": lambda: gatherer_cases(torch, GroupByExpertGatherer)}
+    for stem, make in light.items():
+        if args.only in (None, stem):
+            np.savez_compressed(HERE / f"{stem}.npz", **make())
+    if args.only in light:
         return
     from hydranet.preprocess.pack_weights import ExpertWeightPacker, QuantConfig
 
