@@ -266,16 +266,14 @@ def cpu_oracle_time(T: int, budget_s: float = 15.0, max_steps: int = 400):
 
 
 def decode_launches(T: int) -> int:
-    """Kernels one layer step launches at config 2, mirroring the library's
-    choices: prep, gate/up and down, plus the router GEMM from 256 tokens,
-    the multi-CTA planner and the combine pass above 4096 assignments, and the
-    assignment-ordered token copy from 12 assignments per expert (T > 16)."""
-    tk = T * TOPK
-    n = 3
-    n += T >= 256
-    n += 2 * (tk > 4096)
-    n += T > 16 and tk >= 12 * E
-    return int(n)
+    """Kernels one layer step launches at config 2, as the library itself
+    reports them (``hn_moe_layer_launches``, computed from the same layout
+    decisions its launch code takes): prep, gate/up and down, plus the router
+    GEMM from 256 tokens, the assignment-ordered token copy from 12
+    assignments per expert, and the multi-CTA planner and the combine pass
+    above 4096 assignments."""
+    from hydranet_b200 import _lib
+    return int(_lib.load().hn_moe_layer_launches(T, H, F, E, TOPK))
 
 
 def prefill_cpu_time(budget_s: float = 10.0, n_tok: int = 256, n_exp: int = 16):

@@ -1931,6 +1931,19 @@ size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int top
   return make_layout(T, H, E, top_k, F, H, nt, grid_p(nt), true).total() + 256;
 }
 
+int hn_moe_layer_launches(int64_t T, int64_t H, int64_t F, int64_t E, int top_k) {
+  if (T < 1 || H < 128 || F < 128 || E < 1 || top_k < 1) return 0;
+  const int nt = pick_nt(T, top_k, E);
+  const Layout l = make_layout(T, H, E, top_k, F, H, nt, grid_p(nt), true);
+  const bool big = T * top_k > kPlanSmemEntries;
+  int n = 3;       // route_prep_kernel, the gate/up engine, the down engine
+  n += l.has_rlog;  // router_logits_kernel (taken when x and the router rows are 16-byte aligned)
+  n += big;         // plan_kernel
+  n += l.has_xs;    // stage_rows_kernel
+  n += big;         // combine_kernel
+  return n;
+}
+
 size_t hn_expert_mlp_workspace_size(int64_t T, int64_t H, int64_t F) {
   if (T < 1 || H < 128 || F < 128) return 0;
   const int nt = pick_nt(T, 1, 1);

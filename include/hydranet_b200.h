@@ -149,6 +149,14 @@ typedef struct hn_router_params {
 
 HN_API size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int top_k);
 
+/* Number of kernel launches one hn_moe_layer_int4 call of this shape makes
+ * (host-only query, no GPU needed; 0 for invalid sizes).  Three always (the
+ * route/plan kernel, gate/up, down), plus the router GEMM from 256 tokens
+ * (when x and the router rows are 16-byte aligned), the assignment-ordered
+ * token copy when experts get >= 12 assignments on average, and the
+ * multi-CTA planner and the combine pass above 4096 (token, slot) pairs. */
+HN_API int hn_moe_layer_launches(int64_t T, int64_t H, int64_t F, int64_t E, int top_k);
+
 /* TMA descriptors of an expert table (what the grouped ops stream weights
  * with): hn_expert_maps_bytes() bytes per expert (384).  hn_expert_maps_encode
  * fills a 64-byte aligned HOST buffer of E entries from a HOST copy of the

@@ -134,3 +134,16 @@ def test_workspace_not_made_during_graph_capture(monkeypatch):
     with pytest.raises(RuntimeError, match="outside CUDA-graph capture"):
         ws.get(4096, torch.device("cuda:0"))
     assert ws.all() == []
+
+
+def test_moe_layer_launch_count_query():
+    """``hn_moe_layer_launches`` (host-only) at config 2 across the batch sizes
+    where the library adds kernels, at the GLM prefill shape, and for sizes
+    the layer rejects."""
+    lib = _lib.load()
+    want = {1: 3, 16: 3, 32: 3, 64: 4, 255: 4, 256: 5, 2048: 5, 2049: 7, 8192: 7}
+    assert {T: lib.hn_moe_layer_launches(T, 4096, 14336, 8, 2) for T in want} == want
+    assert lib.hn_moe_layer_launches(8192, 4096, 1408, 128, 8) == 7
+    assert lib.hn_moe_layer_launches(32, 4096, 1408, 128, 8) == 3
+    assert lib.hn_moe_layer_launches(0, 4096, 14336, 8, 2) == 0
+    assert lib.hn_moe_layer_launches(4, 64, 14336, 8, 2) == 0
