@@ -1816,6 +1816,9 @@ static int run_moe(const MoECall& m) {
   ra.out_logits = m.out_logits;
   ra.seg = seg_tokens(nt);
   ra.plan = plan;
+  // a route-only call (hn_moe_route) runs no expert phase, so nothing would
+  // read the assignment-ordered copy of the tokens: skip making it
+  if (!m.run_experts) ra.plan.xs = nullptr;
   int rc = HN_OK;
   if (m.phase == 0 || m.phase == 1) rc = launch_route<Tr>(ra, m.stream);
   if (rc || !m.run_experts || m.phase == 1) return rc;
