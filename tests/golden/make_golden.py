@@ -3,9 +3,9 @@
 
 This script imports HydraNet itself (read-only) and records what the
 reference computes on seeded synthetic inputs: its packer, its dequantiser,
-the non-expert ``Int4Linear`` quantiser, its group-by-expert gatherer, its
-two routers and its MoE layers in dequant mode.  The fixtures pin the
-numpy oracle under ``oracle/``; the GPU box never runs this script (the
+the non-expert ``Int4Linear`` quantiser, its group-by-expert gatherer, a
+packed store written by its own test helper, its two routers and its MoE
+layers in dequant mode.  The fixtures pin the numpy oracle under ``oracle/``; the GPU box never runs this script (the
 reference is not there), it only reads the committed ``.npz`` files.
 
 Usage (from the repository root)::
@@ -158,6 +158,23 @@ def gatherer_cases(torch, GroupByExpertGatherer):
     add("f32_dup", 25, 4, 6, 8, "float32", dup=True)
     add("f16", 19, 2, 8, 8, "float16")
     return cases
+
+
+def store_case(ref: Path):
+    """A packed store written by the reference's own test helper
+    (``tests/test_int4_loader.py:28-119``: 2 layers x 2 experts, H 256, F 512,
+    weights from ``torch.manual_seed(42)``): its index JSON and the SHA-256 of
+    its ``experts.bin`` (the bytes themselves are regenerated by the test)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("ref_test_int4_loader", ref / "tests" / "test_int4_loader.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    out = Path(tempfile.mkdtemp(prefix="hnstore_"))
+    mod.create_synthetic_packed_store(out, num_layers=2, num_experts=2, hidden_dim=256, intermediate_dim=512)
+    data = (out / "experts.bin").read_bytes()
+    return {"idx_json": np.array((out / "experts.idx").read_text()),
+            "bin_sha256": np.array(hashlib.sha256(data).hexdigest()),
+            "bin_size": np.int64(len(data))}
 
 
 # ---------------------------------------------------------------------------
@@ -317,7 +334,8 @@ def main():
     from hydranet.kernels.int4_linear import Int4Linear
     from hydranet.scheduler.continuous_batch import GroupByExpertGatherer
     light = {"int4linear_quant": lambda: int4linear_cases(torch, Int4Linear),
-             "gatherer": lambda: gatherer_cases(torch, GroupByExpertGatherer)}
+             "gatherer": lambda: gatherer_cases(torch, GroupByExpertGatherer),
+             "reference_store": lambda: store_case(args.reference.resolve())}
     for stem, make in light.items():
         if args.only in (None, stem):
             np.savez_compressed(HERE / f"{stem}.npz", **make())
