@@ -18,6 +18,7 @@ LIB_PATH = HERE / "libhydranet_b200.so"
 HN_OK, HN_ERR_INVALID, HN_ERR_UNSUPPORTED, HN_ERR_CUDA, HN_ERR_WORKSPACE = range(5)
 HN_DTYPE_F32, HN_DTYPE_F16, HN_DTYPE_BF16 = range(3)
 HN_ROUTER_SOFTMAX_TOPK, HN_ROUTER_SIGMOID_TOPK = range(2)
+HN_ENGINE_AUTO, HN_ENGINE_TCGEN05 = range(2)
 
 c_void_p, c_int, c_int64, c_size_t, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_float
 
@@ -68,6 +69,9 @@ SIGNATURES = {
     "hn_int4_linear_static": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64,
                                       c_int, c_void_p, c_int64, c_void_p]),
     "hn_selftest_wait_timeout": (c_int, [c_void_p, c_size_t, c_int, c_void_p]),
+    "hn_set_decode_engine": (c_int, [c_int]),
+    "hn_int4_linear_static_scratch_size": (c_size_t, [c_int64, c_int64, c_int64]),
+    "hn_int4_linear_static_error": (c_int, [ctypes.POINTER(c_int), c_void_p]),
 }
 
 _lib = None
@@ -139,16 +143,26 @@ def require_cuda(*tensors):
             raise ValueError("hydranet_b200 ops take CUDA tensors (no CPU fallback)")
 
 
+class DeviceError(HydraNetError):
+    """A bounded device wait timed out, or caller-given routing named an
+    expert outside the table, in an earlier call on this stream: the results
+    of that call (and of calls issued before this one noticed) are invalid."""
+
+
 class _Workspaces:
     """One zero-filled workspace per (device, stream), grown on demand.
 
     The library keeps a workspace's counter section zero between calls, so one
     buffer serves every call shape on its stream (see the header comment of
-    ``include/hydranet_b200.h``).
+    ``include/hydranet_b200.h``).  Each workspace also names a pinned host
+    word (bytes 8..15) into which the kernels copy any device error they
+    record; ``get`` reads that word -- a plain host read, no synchronisation --
+    and raises ``DeviceError`` for an error an earlier call left there.
     """
 
     def __init__(self):
         self._ws = {}
+        self._mirror = {}
         self._lock = threading.Lock()
 
     def get(self, nbytes: int, device):
@@ -157,6 +171,13 @@ class _Workspaces:
         key = (dev.index if dev.index is not None else torch.cuda.current_device(), stream_ptr(dev))
         with self._lock:
             buf = self._ws.get(key)
+            mirror = self._mirror.get(key)
+            if mirror is not None and int(mirror[0]) != 0:
+                code = int(mirror[0])
+                mirror.zero_()
+                buf[:4].zero_()  # the device word, cleared in stream order
+                raise DeviceError(code, f"device error {code} ({DEVICE_ERRORS.get(code, 'unknown')}) recorded by "
+                                        "an earlier call on this stream; its results are invalid")
             if buf is None or buf.numel() < nbytes:
                 if torch.cuda.is_current_stream_capturing():
                     # a buffer made during capture is only zeroed when the graph
@@ -168,17 +189,30 @@ class _Workspaces:
                 if buf is not None:
                     size = max(size, buf.numel() * 2)
                 buf = torch.zeros(size, dtype=torch.uint8, device=dev)
+                if mirror is None:
+                    mirror = torch.zeros(1, dtype=torch.int32).pin_memory()
+                    self._mirror[key] = mirror
+                buf[8:16].view(torch.int64).fill_(mirror.data_ptr())
                 self._ws[key] = buf
             return buf
 
     def all(self):
         return list(self._ws.values())
 
+    def clear_mirror(self, ws):
+        for key, buf in self._ws.items():
+            if buf.data_ptr() == ws.data_ptr():
+                self._mirror[key].zero_()
+
+
+DEVICE_ERRORS = {1: "a bounded device wait timed out", 2: "a routing index outside [0, E)"}
 
 workspaces = _Workspaces()
 
 
 def workspace_error(ws) -> int:
+    """Read and clear a workspace's device error word (synchronises its stream)."""
     code = c_int(0)
     check(load().hn_workspace_error(ws.data_ptr(), ws.numel(), ctypes.byref(code), stream_ptr(ws.device)))
+    workspaces.clear_mirror(ws)
     return code.value

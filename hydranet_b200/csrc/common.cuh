@@ -23,6 +23,8 @@ int sm_count_current();
 // hn_int4_linear and its workspace size with segments of at most 8*max_nt
 // tokens (hn_int4_linear itself allows 128).
 size_t int4_linear_workspace_nt(int64_t M, int64_t N, int64_t K, int max_nt);
+// Address of hn_int4_linear_static's scratch array on the current device.
+int static_scratch_address(void** out);
 int int4_linear_nt(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, const uint8_t* w_packed,
                    const uint16_t* w_scales, int64_t N, int group_size, void* out, int64_t ldo, void* workspace,
                    size_t workspace_bytes, void* stream, int max_nt);
@@ -157,6 +159,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // recorded an error every other wait gives up within a few milliseconds, and
 // a failing launch finishes within about one wait limit.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Records a device error code in the workspace's error word and, when bytes
+// 8..15 of the workspace hold the address of a host-mapped int32 (pinned
+// host memory; NULL: none), in that word too, so the host can see the error
+// with a plain memory read, without synchronising.  Only failure paths call
+// this.
+__device__ __forceinline__ void record_error(int* err, int code) {
+  if (!err) return;
+  atomicExch(err, code);
+  int* mirror = *reinterpret_cast<int* volatile*>(reinterpret_cast<char*>(err) + 8);
+  if (mirror) {
+    *reinterpret_cast<volatile int*>(mirror) = code;
+    __threadfence_system();
+  }
+}
 constexpr int kQuietPolls = 16;
 __device__ __forceinline__ int ld_volatile_s32(const int* p) {
   int v;
@@ -177,7 +194,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
       if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
-  if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);
+  record_error(err, DEV_ERR_WAIT_TIMEOUT);
   return false;
 }
 
@@ -196,7 +213,7 @@ __device__ __forceinline__ bool mbar_wait_backoff(uint32_t bar, uint32_t parity,
       if (globaltimer_ns() - t0 > kWaitLimitNs) break;
     }
   }
-  if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);
+  record_error(err, DEV_ERR_WAIT_TIMEOUT);
   return false;
 }
 

@@ -22,6 +22,8 @@
 // tcgen05.mma (M = 128 weight rows), the tokens are the B operand (N = 16 or
 // 32) in shared memory, and each piece of a tile accumulates in TMEM.
 #include <algorithm>
+#include <atomic>
+#include <type_traits>
 #include <cstring>
 #include <string>
 #include <cuda.h>
@@ -365,7 +367,7 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
             w = 0.f;
           }
         } else if (e < 0 || e >= a.E) {
-          atomicExch(a.plan.err, DEV_ERR_BAD_INDEX);
+          record_error(a.plan.err, DEV_ERR_BAD_INDEX);
           e = 0;
         }
         s_idx[k] = e;
@@ -582,6 +584,114 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* x, int64
 }
 
 // ---------------------------------------------------------------------------
+// Router logits of a small batch whose router matrix spans several of the
+// prep kernel's 64 KB chunks (GLM-4.5: 128 experts x 4096 fp32 = 2 MB): the
+// per-token prep CTA would stream the whole matrix chunk by chunk, one round
+// trip each.  Here CTA b stages kRgvE expert rows in shared memory (as fp32)
+// and each warp dots them with one token's activations at a time; a lane
+// sums h = 8*lane + 256*i in order and the warp reduces by xor-shuffle, so
+// the result does not depend on the launch shape.  logits[t, e] is fp32 (the
+// prep kernel applies the Mixtral gate's model-dtype rounding).
+// ---------------------------------------------------------------------------
+constexpr int kRgvE = 2;
+// Taken when the router has more than 32 Ki weights (64 KB at 16 bits):
+// decided on the weight count, not on the dtype, so a host-only query can
+// tell without knowing the router's dtype.
+__host__ __device__ inline bool router_gemv_wanted(int64_t H, int64_t E) {
+  return E * H * 2 > (int64_t)kRouteChunkBytes;
+}
+template <typename Tr>
+__global__ void __launch_bounds__(256) router_gemv_kernel(const void* x, int64_t ldx, int T, int H, int E,
+                                                          const void* rw, int rw_dtype, float* out) {
+  extern __shared__ __align__(16) float wsm[];  // [kRgvE][H]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int e0 = blockIdx.x * kRgvE, ne = min(kRgvE, E - e0);
+  // the rows in 16-byte vectors, four loads in flight per thread before any store
+  const int n = ne * H;
+  if (rw_dtype == HN_DTYPE_F32 && (reinterpret_cast<uintptr_t>(rw) & 15) == 0) {
+    const float4* src = reinterpret_cast<const float4*>(rw) + (int64_t)e0 * H / 4;
+    for (int i0 = tid; i0 < n / 4; i0 += 4 * 256) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * 256 < n / 4) v[u] = __ldg(src + i0 + u * 256);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * 256 < n / 4) reinterpret_cast<float4*>(wsm)[i0 + u * 256] = v[u];
+    }
+  } else if (rw_dtype != HN_DTYPE_F32 && (reinterpret_cast<uintptr_t>(rw) & 15) == 0) {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(rw) + (int64_t)e0 * H);
+    const bool bf = rw_dtype == HN_DTYPE_BF16;
+    for (int i0 = tid; i0 < n / 8; i0 += 4 * 256) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * 256 < n / 8) v[u] = __ldg(src + i0 + u * 256);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (i0 + u * 256 >= n / 8) continue;
+        const uint32_t q[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        float* d = wsm + (i0 + u * 256) * 8;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (bf) {
+            d[2 * c] = __uint_as_float(q[c] << 16);
+            d[2 * c + 1] = __uint_as_float(q[c] & 0xFFFF0000u);
+          } else {
+            const __half2 hh = *reinterpret_cast<const __half2*>(&q[c]);
+            d[2 * c] = __low2float(hh);
+            d[2 * c + 1] = __high2float(hh);
+          }
+        }
+      }
+    }
+  } else {
+    for (int i = tid; i < n; i += 256) wsm[i] = load_any(rw, rw_dtype, (int64_t)e0 * H + i);
+  }
+  __syncthreads();
+  const typename Tr::T* xp = reinterpret_cast<const typename Tr::T*>(x);
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 8 == 0);
+  for (int t = warp; t < T; t += 8) {
+    float acc[kRgvE];
+#pragma unroll
+    for (int e = 0; e < kRgvE; ++e) acc[e] = 0.f;
+    const typename Tr::T* xr = xp + (int64_t)t * ldx;
+    for (int h = lane * 8; h < H; h += 256) {
+      float xv[8];
+      if (vec) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + h));
+        const typename Tr::T2* h2 = reinterpret_cast<const typename Tr::T2*>(&v);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          xv[2 * u] = Tr::to_f(h2[u].x);
+          xv[2 * u + 1] = Tr::to_f(h2[u].y);
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) xv[u] = Tr::to_f(xr[h + u]);
+      }
+#pragma unroll
+      for (int e = 0; e < kRgvE; ++e) {
+        const float4 w0 = *reinterpret_cast<const float4*>(wsm + e * H + h);
+        const float4 w1 = *reinterpret_cast<const float4*>(wsm + e * H + h + 4);
+        acc[e] = fmaf(xv[0], w0.x, acc[e]);
+        acc[e] = fmaf(xv[1], w0.y, acc[e]);
+        acc[e] = fmaf(xv[2], w0.z, acc[e]);
+        acc[e] = fmaf(xv[3], w0.w, acc[e]);
+        acc[e] = fmaf(xv[4], w1.x, acc[e]);
+        acc[e] = fmaf(xv[5], w1.y, acc[e]);
+        acc[e] = fmaf(xv[6], w1.z, acc[e]);
+        acc[e] = fmaf(xv[7], w1.w, acc[e]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kRgvE; ++e)
+      for (int o = 16; o; o >>= 1) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+    if (lane < ne) out[(int64_t)t * E + e0 + lane] = lane == 0 ? acc[0] : acc[kRgvE > 1 ? 1 : 0];
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Dispatch plan for large routings (T*K above kPlanSmemEntries): one CTA per
 // expert e.  Each CTA histograms every expert's assignments (so no counters
 // cross CTAs), takes its offset and segment base from the prefix over the
@@ -720,6 +830,8 @@ struct EngineArgs {
   int early;  // KIND_DOWN after a gate/up launch: only the token producer waits for it
   int defer_combine;  // EPI_COMBINE: leave the top-k sum to combine_kernel (large routings)
   int allow_rr;       // whole tiles round-robin over the CTAs when there are >= 4 per CTA (prefill sizes)
+  int64_t max_segs;   // segments the plan can hold (bounds the tiles of an mma.sync engine CTA)
+  int max_nt;         // tokens per segment / 8
 };
 
 template <int KIND>
@@ -1420,6 +1532,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
   }
 }
 
+#include "hn_gv.cuh"
+
 // ---------------------------------------------------------------------------
 // Top-k combine of a large routing: out[t, :] = sum over slots k, in slot
 // order, of R[t*K + k, :] (each row already scaled by its routing weight), in
@@ -1454,8 +1568,13 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* R, int T, int
 // (T <= 64); for larger steps by the mean assignments per expert, T*K/E, up
 // to 128 (prefill), so each dequantised weight tile serves more tokens.
 static int pick_nt(int64_t T, int64_t K, int64_t E) {
-  if (T <= 16) return 2;
-  if (T <= 64) return 4;
+  if (T <= 8) return 1;
+  if (T <= 64) {
+    // decode: 16-token segments while experts get at most 4 assignments on
+    // average (few experts ever reach 16), else 16 (T <= 16) or 32 tokens
+    const int64_t avg = T * K / std::max<int64_t>(E, 1);
+    return (avg <= 4 || T <= 16) ? 2 : 4;
+  }
   const int64_t avg = T * K / std::max<int64_t>(E, 1);
   if (avg >= 96) return 16;
   if (avg >= 48) return 8;
@@ -1471,6 +1590,102 @@ struct TcTune {
 };
 
 static int encode_token_map(CUtensorMap* data, const void* base, int64_t rows, int64_t row_bytes, int box_rows);
+
+// Which engine runs a phase: segments of at most 16 tokens go to the
+// register-dequant mma.sync engine (gv_kernel) unless hn_set_decode_engine
+// chose the tcgen05 engine; larger segments always run on tcgen05, whose
+// tensor pipe is four times wider (at 24-32 tokens per segment the mma.sync
+// pipe, not HBM, would bound the phase).
+static std::atomic<int> g_decode_engine{HN_ENGINE_AUTO};
+static int gv_nt(int nt) { return nt <= 1 ? 1 : 2; }
+// CTAs of an mma.sync engine launch (two per SM)
+static int gv_grid(int nt) {
+  const int sms = sm_count_current();
+  (void)nt;
+  return (sms > 0 ? sms : 148) * GvCfg<1>::kCtasPerSm;
+}
+static int gv_warps(int nt) {
+  (void)nt;
+  return GvCfg<1>::W;
+}
+// Tiles one CTA's step range can touch at most: the engine caches their
+// metadata in shared memory (kGvMaxTiles entries).
+static bool gv_fits(int nt, int64_t max_segs, int64_t rows, bool gateup) {
+  const int64_t tile_rows = (gateup ? 16 : 32) * (int64_t)gv_warps(nt);
+  const int64_t tiles = max_segs * ((rows + tile_rows - 1) / tile_rows);
+  return tiles / gv_grid(nt) + 3 <= kGvMaxTiles;
+}
+static bool use_gv(int nt) { return nt <= 2 && g_decode_engine.load(std::memory_order_relaxed) != HN_ENGINE_TCGEN05; }
+// Bytes of stream-K partials an mma.sync engine launch may write.
+static size_t gv_part_bytes(int nt) {
+  return (size_t)gv_grid(nt) * 2 * gv_warps(nt) * 2 * gv_nt(nt) * 32 * 16;
+}
+
+template <typename Tr, int NT, int KIND, int EPI>
+static int launch_gv_t(const GvArgs& a, cudaStream_t s) {
+  using C = GvCfg<NT>;
+  auto kern = gv_kernel<Tr, NT, KIND, EPI>;
+  static std::atomic<bool> attr_set[64] = {};  // per instantiation and device; setting it twice is harmless
+  int dev = 0;
+  HN_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
+    HN_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kTotal));
+    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)gv_grid(NT));
+  cfg.blockDim = dim3((unsigned)C::kThreads);
+  cfg.dynamicSmemBytes = C::kTotal;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  HN_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  return HN_OK;
+}
+
+template <typename Tr, int KIND, int EPI>
+static int launch_gv(int nt, const GvArgs& a, cudaStream_t s) {
+  if (nt <= 1) return launch_gv_t<Tr, 1, KIND, EPI>(a, s);
+  return launch_gv_t<Tr, 2, KIND, EPI>(a, s);
+}
+
+// The mma.sync engine's arguments for the phase the tcgen05 engine's
+// arguments describe (same plan, same staged rows, same outputs).
+static GvArgs gv_args(const EngineArgs& e, int KIND) {
+  GvArgs g{};
+  g.K = e.K;
+  g.G = e.G;
+  g.rows = e.N;
+  const int tile_rows = (KIND == KIND_GATEUP ? 16 : 32) * gv_warps(gv_nt(e.max_nt));
+  g.tps = (e.N + tile_rows - 1) / tile_rows;
+  g.T = e.T;
+  g.topk = e.topk;
+  g.segs = e.segs;
+  g.n_segs = e.n_segs;
+  g.a_tok = e.a_tok;
+  g.a_tk = e.a_tk;
+  g.a_w = e.a_w;
+  g.table = e.table;
+  g.single = e.single;
+  g.bsrc = e.bsrc;
+  g.b_rstride = e.b_rstride;
+  g.b_by_token = KIND == KIND_GATEUP ? 1 : e.b_use_tok;  // gate/up reads x by token (xp), down its own rows
+  g.hp = e.hp;
+  g.hp_rstride = e.hp_rstride;
+  g.R = e.R;
+  g.out = e.out;
+  g.ldo = e.ldo;
+  g.part = e.part;
+  g.tile_ctr = e.tile_ctr;
+  g.rt_ctr = e.rt_ctr;
+  g.defer_combine = e.defer_combine;
+  g.early = e.early;
+  g.P = e.P;
+  return g;
+}
 
 template <typename Tr, int N, int KIND, int EPI>
 static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
@@ -1509,6 +1724,8 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
 
 template <typename Tr, int KIND, int EPI>
 static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
+  if (use_gv(nt) && gv_fits(nt, a.max_segs, a.N, KIND == KIND_GATEUP))
+    return launch_gv<Tr, KIND, EPI>(nt, gv_args(a, KIND), s);
   if (nt <= 2) return launch_engine_t<Tr, 16, KIND, EPI>(a, s);
   if (nt <= 4) return launch_engine_t<Tr, 32, KIND, EPI>(a, s);
   if (nt <= 8) return launch_engine_t<Tr, 64, KIND, EPI>(a, s);
@@ -1529,7 +1746,8 @@ struct Layout {
   size_t counts, n_segs, segs, n_segs2, segs2, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, xs, part1, part2, R, rlog,
       data;  // back (relative)
   bool has_rlog, has_xs;
-  int seg2;  // second segment cut for the down phase (0: none)
+  int seg2;          // second segment cut for the down phase (0: none)
+  int64_t max_segs;  // segments the plan can hold
   size_t total() const { return counters + data; }
 };
 
@@ -1543,6 +1761,7 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   const int64_t TK = T * topk;
   const int64_t seg = seg_tokens(nt);
   const int64_t max_segs = std::min<int64_t>(E, TK) + (TK + seg - 1) / seg;
+  l.max_segs = max_segs;
   const int64_t n_rt2 = (N2 + 255) / 256;
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -1577,13 +1796,19 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   // routed gate/up tokens staged in assignment order, read by TMA instead of
   // gathered token by token: pays for its extra copy from a mean of 12
   // assignments per expert (e.g. Mixtral at 64 tokens) and 32-token segments
-  l.has_xs = F && combine && nt >= 4 && TK >= 12 * E;
+  const bool gv_gateup = F && use_gv(nt) && gv_fits(nt, max_segs, F, true);
+  l.has_xs = F && combine && nt >= 4 && TK >= 12 * E && !gv_gateup;
   l.xs = take(l.has_xs ? (size_t)(Kin / 128) * TK * kChunk : 0);
-  const size_t part = (size_t)P * 2 * 8 * (8 * nt) * 32 * 4;  // [CTA][2 slots][fold warp][N][32] fp32
+  // tcgen05 engine: [CTA][2 slots][fold warp][N][32] fp32 with N >= 16; the
+  // mma.sync engine: [CTA][2 slots][warp][2 MMA tiles][NT][32 lanes][4] fp32
+  size_t part = (size_t)P * 2 * 8 * (8 * std::max(nt, 2)) * 32 * 4;
+  if (use_gv(nt)) part = std::max(part, gv_part_bytes(nt));
   l.part1 = take(F ? part : 0);
   l.part2 = take(part);
   l.R = take(combine ? (size_t)TK * N2 * 4 : 0);
-  l.has_rlog = T >= kRouterGemmMinT;
+  // router logits from router_logits_kernel (T >= kRouterGemmMinT) or from
+  // router_gemv_kernel (routers of more than one prep chunk): T*E floats
+  l.has_rlog = true;
   l.rlog = take(l.has_rlog ? (size_t)T * E * 4 : 0);
   l.data = o;
   return l;
@@ -1646,7 +1871,9 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   // the GEMM's 16-byte vector loads need aligned rows of x and of the router matrix
   const bool gemm = ra.mode == ROUTE_COMPUTE && ra.T >= kRouterGemmMinT && ra.plan.rlog &&
                     ((uintptr_t)ra.x & 15) == 0 && ra.ldx % 8 == 0 && ((uintptr_t)ra.rw & 15) == 0;
-  if (ra.mode == ROUTE_COMPUTE && !gemm)
+  // small batches whose router matrix spans several prep chunks: logits by router_gemv_kernel
+  const bool gemv = ra.mode == ROUTE_COMPUTE && !gemm && ra.plan.rlog && router_gemv_wanted(ra.H, ra.E);
+  if (ra.mode == ROUTE_COMPUTE && !gemm && !gemv)
     sm += (size_t)route_chunk_experts(ra.H, ra.E, ra.rw_dtype) * ra.H * route_esize(ra.rw_dtype);
   HN_REQUIRE(sm <= 227 * 1024, "router: hidden size too large for the shared-memory plan");
   if (sm > 48 * 1024)
@@ -1655,6 +1882,15 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   if (gemm) {
     router_logits_kernel<Tr><<<dim3((unsigned)((ra.T + kRgM - 1) / kRgM), (unsigned)((ra.E + kRgN - 1) / kRgN)), 256, 0, s>>>(
         ra.x, ra.ldx, ra.T, ra.H, ra.E, ra.rw, ra.rw_dtype, ra.plan.rlog);
+    HN_CUDA(cudaGetLastError());
+    r.pre_logits = ra.plan.rlog;
+  } else if (gemv) {
+    const size_t gsm = (size_t)kRgvE * ra.H * 4;
+    HN_REQUIRE(gsm <= 227 * 1024, "router: hidden size too large for the router GEMV");
+    if (gsm > 48 * 1024)
+      HN_CUDA(cudaFuncSetAttribute(router_gemv_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
+    router_gemv_kernel<Tr><<<(unsigned)((ra.E + kRgvE - 1) / kRgvE), 256, gsm, s>>>(ra.x, ra.ldx, ra.T, ra.H, ra.E,
+                                                                                  ra.rw, ra.rw_dtype, ra.plan.rlog);
     HN_CUDA(cudaGetLastError());
     r.pre_logits = ra.plan.rlog;
   }
@@ -1692,18 +1928,16 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  // looked up once, thread-safely (a function-local static's initialiser runs once)
+  static const EncodeTiledFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-    else
-      cudaGetLastError();
-  }
+      return reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
   return fn;
 }
 
@@ -1866,6 +2100,8 @@ static int run_moe(const MoECall& m) {
   e1.err = plan.err;
   e1.P = P;
   e1.allow_rr = nt >= 8;
+  e1.max_segs = l.max_segs;
+  e1.max_nt = nt;
   if (m.phase == 0 || m.phase == 2) rc = launch_engine<Tr, KIND_GATEUP, EPI_COMBINE>(nt, e1, m.stream);
   if (rc || m.phase == 2) return rc;
 
@@ -1939,8 +2175,10 @@ int hn_moe_layer_launches(int64_t T, int64_t H, int64_t F, int64_t E, int top_k)
   const int nt = pick_nt(T, top_k, E);
   const Layout l = make_layout(T, H, E, top_k, F, H, nt, grid_p(nt), true);
   const bool big = T * top_k > kPlanSmemEntries;
-  int n = 3;       // route_prep_kernel, the gate/up engine, the down engine
-  n += l.has_rlog;  // router_logits_kernel (taken when x and the router rows are 16-byte aligned)
+  int n = 3;  // route_prep_kernel, the gate/up engine, the down engine
+  // router_logits_kernel (from kRouterGemmMinT tokens, when x and the router
+  // rows are 16-byte aligned) or router_gemv_kernel (routers of more than 32 Ki weights)
+  n += T >= kRouterGemmMinT || router_gemv_wanted(H, E);
   n += big;         // plan_kernel
   n += l.has_xs;    // stage_rows_kernel
   n += big;         // combine_kernel
@@ -2186,6 +2424,8 @@ int int4_linear_nt(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   e.err = plan.err;
   e.P = P;
   e.allow_rr = nt >= 8;
+  e.max_segs = l.max_segs;
+  e.max_nt = nt;
   int rc;
   if (dtype == HN_DTYPE_BF16) {
     rc = launch_route<BF16>(ra, s);
@@ -2215,6 +2455,14 @@ int hn_expert_maps_encode(const hn_expert_ptrs* host_table, int64_t E, int64_t H
     if (rc) return rc;
   }
   return HN_OK;
+}
+
+int hn_set_decode_engine(int engine) {
+  if (engine != HN_ENGINE_AUTO && engine != HN_ENGINE_TCGEN05) {
+    fail(HN_ERR_INVALID, "hn_set_decode_engine: unknown engine " + std::to_string(engine));
+    return -1;
+  }
+  return g_decode_engine.exchange(engine);
 }
 
 int hn_workspace_error(const void* workspace, size_t workspace_bytes, int* error_code, void* stream) {

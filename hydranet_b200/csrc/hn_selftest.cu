@@ -4,7 +4,8 @@
 // (mbar_wait, mbar_wait_backoff).  The first wait to pass the time limit
 // records DEV_ERR_WAIT_TIMEOUT in the workspace's error word; the other sees
 // the word and gives up; the launch ends, and the context stays usable.  A
-// test reads the word back with hn_workspace_error.
+// test reads the word back with hn_workspace_error (or, when the self-test ran
+// on hn_int4_linear_static's array, with hn_int4_linear_static_error).
 #include "common.cuh"
 
 namespace hn {
@@ -30,8 +31,14 @@ __global__ void __launch_bounds__(64) wait_timeout_kernel(int* err, int mode) {
 }  // namespace hn
 
 extern "C" int hn_selftest_wait_timeout(void* workspace, size_t workspace_bytes, int mode, void* stream) {
-  HN_REQUIRE(workspace && workspace_bytes >= 512, "hn_selftest_wait_timeout: need a workspace of >= 512 bytes");
   HN_REQUIRE(mode == 0 || mode == 1, "hn_selftest_wait_timeout: mode is 0 or 1");
+  if (!workspace) {
+    // the error word of hn_int4_linear_static's array
+    const int rc = hn::static_scratch_address(&workspace);
+    if (rc) return rc;
+    workspace_bytes = HN_INT4_LINEAR_STATIC_SCRATCH_BYTES;
+  }
+  HN_REQUIRE(workspace_bytes >= 512, "hn_selftest_wait_timeout: need a workspace of >= 512 bytes");
   hn::wait_timeout_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(reinterpret_cast<int*>(workspace), mode);
   HN_CUDA(cudaGetLastError());
   return HN_OK;

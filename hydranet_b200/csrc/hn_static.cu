@@ -3,10 +3,12 @@
 //
 // The array is a file-scope __device__ variable, so the CUDA runtime creates
 // one zero-filled copy per device when it loads this module there; nothing is
-// allocated at call time.  Its address on the current device is looked up once
-// (cudaGetSymbolAddress) and cached.  The computation is the unchanged
-// hn_int4_linear entry point, given that array as its workspace.
-#include <mutex>
+// allocated at call time.  Host code cannot use the array's name as a device
+// address: every call looks the address up for the current device and
+// context (cudaGetSymbolAddress, a host-side table lookup once the module is
+// loaded), so a context that was reset or replaced never leaves a stale
+// address behind.  The computation is the unchanged hn_int4_linear entry
+// point, given that array as its workspace.
 #include <string>
 
 #include "common.cuh"
@@ -23,29 +25,22 @@ static_assert(kStaticScratchBytes % 256 == 0, "static scratch size must keep 256
 
 __device__ __align__(256) unsigned char g_linear_scratch[kStaticScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+}  // namespace
 
-// Address of the current device's copy of g_linear_scratch.  The first call on
-// a device may load the module onto it; later calls only read the cache.
-int static_scratch(void** out) {
-  int dev = -1;
-  HN_CUDA(cudaGetDevice(&dev));
-  HN_REQUIRE(dev >= 0 && dev < kMaxDevices, "int4_linear_static: device ordinal beyond the library's table of 64");
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    HN_CUDA(cudaGetSymbolAddress(&p, g_linear_scratch));
-    HN_REQUIRE(p && ((uintptr_t)p & 255) == 0, "int4_linear_static: static scratch is not 256-byte aligned");
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+// Address of the current device's copy of g_linear_scratch.
+int static_scratch_address(void** out) {
+  void* p = nullptr;
+  HN_CUDA(cudaGetSymbolAddress(&p, g_linear_scratch));
+  HN_REQUIRE(p && ((uintptr_t)p & 255) == 0, "int4_linear_static: static scratch is not 256-byte aligned");
+  *out = p;
   return HN_OK;
 }
 
-}  // namespace
 }  // namespace hn
+
+extern "C" size_t hn_int4_linear_static_scratch_size(int64_t M, int64_t N, int64_t K) {
+  return hn::int4_linear_workspace_nt(M, N, K, hn::kStaticMaxNt);
+}
 
 extern "C" int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K,
                                      const uint8_t* w_packed, const uint16_t* w_scales, int64_t N, int group_size,
@@ -59,8 +54,17 @@ extern "C" int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int6
                                           std::to_string(hn::kStaticScratchBytes) +
                                           " bytes compiled into the library; call hn_int4_linear with a workspace");
   void* ws = nullptr;
-  const int rc = hn::static_scratch(&ws);
+  const int rc = hn::static_scratch_address(&ws);
   if (rc) return rc;
   return hn::int4_linear_nt(x, ldx, dtype, M, K, w_packed, w_scales, N, group_size, out, ldo, ws,
                             hn::kStaticScratchBytes, stream, hn::kStaticMaxNt);
+}
+
+// The array's error word (its first 4 bytes), read on 'stream' and cleared.
+extern "C" int hn_int4_linear_static_error(int* error_code, void* stream) {
+  HN_REQUIRE(error_code, "hn_int4_linear_static_error: error_code is NULL");
+  void* ws = nullptr;
+  const int rc = hn::static_scratch_address(&ws);
+  if (rc) return rc;
+  return hn_workspace_error(ws, hn::kStaticScratchBytes, error_code, stream);
 }

@@ -207,6 +207,12 @@ def load_store(index_path: Path, layer_idx: int, device="cuda") -> ExpertTable:
     entries = sorted((e for e in idx["experts"] if e["layer_idx"] == layer_idx), key=lambda e: e["expert_idx"])
     if not entries:
         raise ValueError(f"layer {layer_idx} not in index")
+    # the table is indexed by expert id: the layer must list each of 0..E-1 exactly once
+    ids = [e["expert_idx"] for e in entries]
+    n_exp = mc.get("num_experts", len(ids))
+    if ids != list(range(n_exp)):
+        raise ValueError(f"layer {layer_idx} of the index lists experts {ids[:8]}{'...' if len(ids) > 8 else ''}, "
+                         f"not each of 0..{n_exp - 1} once")
     data = np.memmap(index_path.parent / "experts.bin", dtype=np.uint8, mode="r")
     slots = []
     for e in entries:

@@ -8,7 +8,11 @@
  * *_workspace_size() query (query on the device that will run the call).
  * A workspace must be 256-byte aligned, and its first 512 bytes (an error
  * word and an arrival counter) must be zero before its first use; zero-filling
- * the whole buffer once when it is allocated is enough.  The kernels leave it
+ * the whole buffer once when it is allocated is enough.  Bytes 8..15 may then
+ * be set to the address of a host-mapped int32 (pinned host memory, which the
+ * device reaches at the same address): a device error recorded in the error
+ * word is copied there as well, so the host can notice it with a plain read
+ * instead of hn_workspace_error's synchronising copy.  The kernels leave it
  * re-usable: the two words stay zero unless a bounded wait failed (see
  * hn_workspace_error), every other counter is zeroed by each call itself, so
  * one workspace may serve calls of any shape whose size query it satisfies.
@@ -151,10 +155,12 @@ HN_API size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, 
 
 /* Number of kernel launches one hn_moe_layer_int4 call of this shape makes
  * (host-only query, no GPU needed; 0 for invalid sizes).  Three always (the
- * route/plan kernel, gate/up, down), plus the router GEMM from 256 tokens
- * (when x and the router rows are 16-byte aligned), the assignment-ordered
- * token copy when experts get >= 12 assignments on average, and the
- * multi-CTA planner and the combine pass above 4096 (token, slot) pairs. */
+ * route/plan kernel, gate/up, down), plus one router-logits kernel from 256
+ * tokens (when x and the router rows are 16-byte aligned) or when the router
+ * has more than 32 Ki weights (E * H > 32768, e.g. GLM-4.5's 128 x 4096), the
+ * assignment-ordered token copy when experts get >= 12 assignments on average
+ * on the tcgen05 engine, and the multi-CTA planner and the combine pass above
+ * 4096 (token, slot) pairs. */
 HN_API int hn_moe_layer_launches(int64_t T, int64_t H, int64_t F, int64_t E, int top_k);
 
 /* TMA descriptors of an expert table (what the grouped ops stream weights
@@ -223,17 +229,21 @@ HN_API int hn_moe_route(const void* x, int dtype, int64_t T, int64_t H, int64_t 
  * serving runtime that has given all free HBM to its caches, so that a
  * cudaMalloc on the decode path would fail or wait for the whole device.
  *
- *  - Shapes whose hn_int4_linear_workspace_size(M, N, K) is larger than the
- *    array are refused with HN_ERR_WORKSPACE (for example M = 64 with
- *    K = 14336 fits; M = 4096 with K = 14336 does not).
- *  - The first call on each device, made with that device current, looks up
- *    the array's address (cudaGetSymbolAddress, which may load the module onto
- *    the device) and caches it; make that first call before any stream
+ *  - Shapes whose hn_int4_linear_static_scratch_size(M, N, K) is larger than
+ *    the array are refused with HN_ERR_WORKSPACE (for example M = 64 with
+ *    K = 14336 fits; M = 4096 with K = 14336 does not).  The query is
+ *    host-only and needs no GPU.
+ *  - Every call looks up the array's address on the current device and
+ *    context (cudaGetSymbolAddress; host code cannot use the array's name as
+ *    a device address).  The first lookup on a device may load the library's
+ *    module there, so make the first call on each device before any stream
  *    capture.  A failure there is returned as HN_ERR_CUDA.
  *  - What must be zero: the array's first 512 bytes (an error word and an
  *    arrival counter) when a call starts.  They are zero after loading and
- *    stay zero unless a bounded device wait times out; after that, results of
- *    later calls on that device are undefined.
+ *    stay zero unless a bounded device wait of a call timed out (calls of up
+ *    to 32 rows per token segment, which is all of them by default, contain
+ *    no such wait).  hn_int4_linear_static_error reads the error word and
+ *    clears it; results of calls issued while it was set are undefined.
  *  - There is ONE array per device, shared by every caller of this function.
  *    Two calls that may overlap on the device (streams with no ordering
  *    between them, or host threads racing on different streams) overwrite
@@ -244,6 +254,27 @@ HN_API int hn_moe_route(const void* x, int dtype, int64_t T, int64_t H, int64_t 
 HN_API int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K,
                                  const uint8_t* w_packed, const uint16_t* w_scales, int64_t N, int group_size,
                                  void* out, int64_t ldo, void* stream);
+/* Scratch bytes hn_int4_linear_static needs for this shape (0 for invalid
+ * sizes); calls whose need exceeds HN_INT4_LINEAR_STATIC_SCRATCH_BYTES are
+ * refused.  Host-only. */
+HN_API size_t hn_int4_linear_static_scratch_size(int64_t M, int64_t N, int64_t K);
+/* The static array's device error word on the current device: copies 4 bytes
+ * device->host on 'stream', synchronises that stream, and clears the word if
+ * it was set (as hn_workspace_error does for a workspace). */
+HN_API int hn_int4_linear_static_error(int* error_code, void* stream);
+
+/* Engine for segments of at most 32 tokens per expert (decode sizes).  No
+ * counterpart in the reference.  HN_ENGINE_AUTO (the default) runs them on
+ * the register-dequant mma.sync engine; HN_ENGINE_TCGEN05 runs them on the
+ * tcgen05 engine that larger segments always use.  Both compute the same
+ * function (fp32 accumulation of float16 tokens times exact n - 8 weights;
+ * they differ only in where the group scale is applied), so the switch exists
+ * for side-by-side measurement and parity tests.  Process-wide; applies to
+ * calls issued after it returns, including the workspace-size and launch
+ * queries.  Returns the previous engine, or -1 with HN_ERR_INVALID recorded
+ * in hn_last_error for an unknown value. */
+enum hn_engine { HN_ENGINE_AUTO = 0, HN_ENGINE_TCGEN05 = 1 };
+HN_API int hn_set_decode_engine(int engine);
 
 /* Device-side error word of a workspace (bounded waits that timed out set it).
  * Copies 4 bytes device->host on 'stream' and synchronises that stream. */
@@ -254,7 +285,9 @@ HN_API int hn_workspace_error(const void* workspace, size_t workspace_bytes, int
  * engine's polling wait and its backoff wait; mode 1: two backoff waits).
  * After the wait limit (2 s) the kernel records the timeout (error code 1)
  * in the workspace's error word and ends; hn_workspace_error then reports it.
- * Needs a workspace of >= 512 bytes whose first 4 bytes are zero. */
+ * Needs a workspace of >= 512 bytes whose first 4 bytes are zero.  With
+ * workspace NULL it uses the error word of hn_int4_linear_static's array on
+ * the current device instead (read back with hn_int4_linear_static_error). */
 HN_API int hn_selftest_wait_timeout(void* workspace, size_t workspace_bytes, int mode, void* stream);
 
 #ifdef __cplusplus

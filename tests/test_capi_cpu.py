@@ -143,7 +143,14 @@ def test_moe_layer_launch_count_query():
     lib = _lib.load()
     want = {1: 3, 16: 3, 32: 3, 64: 4, 255: 4, 256: 5, 2048: 5, 2049: 7, 8192: 7}
     assert {T: lib.hn_moe_layer_launches(T, 4096, 14336, 8, 2) for T in want} == want
+    # the engine choice does not change the count at decode sizes
+    prev = lib.hn_set_decode_engine(_lib.HN_ENGINE_TCGEN05)
+    try:
+        assert lib.hn_moe_layer_launches(8, 4096, 14336, 8, 2) == 3
+    finally:
+        lib.hn_set_decode_engine(prev)
+    assert lib.hn_set_decode_engine(7) == -1
     assert lib.hn_moe_layer_launches(8192, 4096, 1408, 128, 8) == 7
-    assert lib.hn_moe_layer_launches(32, 4096, 1408, 128, 8) == 3
+    assert lib.hn_moe_layer_launches(32, 4096, 1408, 128, 8) == 4  # + the router GEMV (128 x 4096 router)
     assert lib.hn_moe_layer_launches(0, 4096, 14336, 8, 2) == 0
     assert lib.hn_moe_layer_launches(4, 64, 14336, 8, 2) == 0

@@ -6,6 +6,8 @@ through the C ABI and compares both results with ``hn_int4_linear`` (through
 ``kernels.int4_gemm.int4_linear``) and with the oracle.
 """
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -52,7 +54,10 @@ def test_static_matches_workspace_entry_point(lib, M, N, K, dtype):
 
 def test_static_refuses_shapes_beyond_its_scratch(lib):
     M, N, K = 4096, 4096, 14336
-    assert lib.hn_int4_linear_workspace_size(M, N, K) > STATIC_BYTES
+    assert lib.hn_int4_linear_static_scratch_size(M, N, K) > STATIC_BYTES
+    # the shapes the matching test accepts fit by the same rule
+    for m, n, k in [(1, 14336, 4096), (64, 4096, 14336), (80, 2048, 1024), (300, 1024, 512)]:
+        assert 0 < lib.hn_int4_linear_static_scratch_size(m, n, k) <= STATIC_BYTES
     x = torch.zeros(M, K, device="cuda", dtype=torch.bfloat16)
     pd = torch.zeros(N, K // 2, device="cuda", dtype=torch.uint8)
     sd = torch.zeros(N, K // 128, device="cuda", dtype=torch.float16)
@@ -60,3 +65,24 @@ def test_static_refuses_shapes_beyond_its_scratch(lib):
         call_static(lib, x, pd, sd, N)
     assert e.value.code == _lib.HN_ERR_WORKSPACE
     assert "hn_int4_linear with a workspace" in str(e.value)
+
+
+def test_static_error_word_is_reported_and_cleared(lib):
+    """The array's error word is reachable: the bounded-wait self-test run on
+    the static array (workspace NULL) sets it, hn_int4_linear_static_error
+    reports it and clears it, and the next static call is correct."""
+    code = ctypes.c_int(-1)
+    stream = _lib.stream_ptr(torch.device("cuda"))
+    _lib.check(lib.hn_int4_linear_static_error(ctypes.byref(code), stream))
+    assert code.value == 0
+    _lib.check(lib.hn_selftest_wait_timeout(None, 0, 1, stream))
+    torch.cuda.synchronize()
+    _lib.check(lib.hn_int4_linear_static_error(ctypes.byref(code), stream))
+    assert code.value == 1                      # DEV_ERR_WAIT_TIMEOUT, seen through the static entry's query
+    _lib.check(lib.hn_int4_linear_static_error(ctypes.byref(code), stream))
+    assert code.value == 0                      # read and cleared
+    p, s, pd, sd = weights(5, 512, 1024)
+    x = act(np.random.default_rng(6).standard_normal((3, 1024), dtype=np.float32), "bf16")
+    got = call_static(lib, x, pd, sd, 512)
+    torch.cuda.synchronize()
+    assert rel_l2(to_np32(got), R.int4_linear_ref(to_np32(x), p, s)) <= TIGHT["bf16"]
