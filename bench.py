@@ -21,10 +21,16 @@ decode tokens.  T is swept over 1/8/32/64; the headline line is T=64.
 the reference itself is Python + Triton and is not installed on the GPU box)
 on the same config and prints the same JSON line with ``"impl": "reference"``.
 
-With ``--gpus N`` (under torchrun) the layer runs expert-parallel: each rank
-owns E/N experts and T tokens of its own (weak scaling), routes them, sends
-token rows to the experts' owners and gets the weighted rows back with NCCL
-all-to-alls (``hydranet_b200/ep.py``); the time is the max over ranks.
+Config 4 (``glm_c4``): one GLM-4.5-Air MoE layer (H 4096, 128 experts of
+moe_ffn 1408, sigmoid top-8 with correction bias) decoding a continuous batch
+of 32 sequences per GPU.  At N = 1 it is measured beside the headline; with
+``--gpus N`` (under torchrun) it IS the headline: each rank owns 128/N
+experts and 32 tokens of its own (weak scaling), sends each token at most once
+to every rank holding one of its picks and gets the partial outputs back with
+NCCL all-to-alls (``hydranet_b200/ep.py``); the whole step is one CUDA graph
+per layer, the time is the max over ranks, and rank 0 checks its output
+against the single-GPU layer holding all 128 experts (``parity_rel_l2``,
+``index_match``).  Scaling is read from ``glm_c4`` at every N (N = 1 included).
 """
 
 from __future__ import annotations
@@ -49,6 +55,10 @@ HEADLINE_T = 64
 N_LAYERS = 4
 METRIC = "INT4 MoE decode tok/s & achieved HBM GB/s vs ~8 TB/s at 1/2/4/8 B200"
 WORKLOAD = "mixtral8x7b_moe_layer_decode"
+# Config 4: GLM-4.5-Air MoE layer decode, 32 sequences per GPU, expert-parallel at N > 1
+G_H, G_F, G_E, G_K, G_T = 4096, 1408, 128, 8, 32
+G_WORKLOAD = "glm45air_moe_layer_decode_ep"
+G_LAYERS = 2  # distinct layers rotated: at N = 8 one rank's 16 experts (143 MB) alone would nearly fit L2
 
 
 def peaks():
@@ -265,6 +275,12 @@ def cpu_oracle_time(T: int, budget_s: float = 15.0, max_steps: int = 400):
     return T * steps / el, steps, el
 
 
+def decode_engine(T: int) -> str:
+    """Engine of the config-2 decode phases at batch T: the mma.sync engine runs
+    segments of up to 16 tokens (8 * pick_nt), tcgen05 the larger ones."""
+    return "mma.sync" if T <= 16 else "tcgen05"
+
+
 def decode_launches(T: int) -> int:
     """Kernels one layer step launches at config 2, as the library itself
     reports them (``hn_moe_layer_launches``, computed from the same layout
@@ -322,8 +338,24 @@ def cpu_threads():
 
 
 def run_reference(args):
+    """The reference's CPU algorithm (the oracle port) on this host's cores, on
+    the GPU arm's workload: config 2 at N = 1, config 4 under --gpus N > 1
+    (rank 0 alone; its step is the whole job's layer step of N x 32 tokens,
+    timed from a bounded sample)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.gpus > 1:
+        v1, ms1, sample = glm_cpu_time(budget_s=max(2.0, min(args.ref_budget, 10.0)))
+        line = {"impl": "reference", "metric": METRIC, "value": v1, "unit": "tok/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms1, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": G_WORKLOAD, "tokens_per_gpu": G_T, "hidden": G_H, "moe_ffn": G_F,
+                           "experts": G_E, "top_k": G_K, "group_size": 128},
+                "cpu_baseline": {"value": v1, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": v1, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     T = args.tokens
     layer = OracleLayer(T)
@@ -344,6 +376,209 @@ def run_reference(args):
                                        f"dequant-then-matmul, weights dequantised before timing)"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def glm_cpu_time(budget_s: float = 10.0, n_exp: int = 16, tok_per_exp: int = 2):
+    """Host-core time of one config-4 layer step (32 tokens, sigmoid top-8 over
+    128 experts) by the oracle's dequant-then-matmul path, from a bounded
+    sample: n_exp expert MLPs at tok_per_exp tokens each (the mean tokens per
+    expert at config 4) are timed and the layer time is that times the
+    experts the step touches (115, the mean over seeded routings) / n_exp;
+    the router (2 MB of fp32 weights) is timed whole.  Returns (tok/s, ms per
+    layer, sample description)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import int4_ref as R
+    from hydranet_b200 import synth
+
+    def make(e):
+        rng = np.random.default_rng(3000 + e)
+        mats = []
+        for n, k in ((G_F, G_H), (G_F, G_H), (G_H, G_F)):
+            mats += [rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8),
+                     (rng.random((n, k // 128), dtype=np.float32) * np.float32(0.005)).astype(np.float16)]
+        return R.DequantExpert.from_packed(*mats)
+
+    with ThreadPoolExecutor(max_workers=min(8, cpu_threads())) as ex:
+        experts = list(ex.map(make, range(n_exp)))
+    rw = synth.host_normal(97, (G_E, G_H), 0.02)
+    x = R.round_to_bf16(np.random.default_rng(2).standard_normal((G_T, G_H), dtype=np.float32))
+    xe = x[:tok_per_exp]
+
+    def step():
+        R.sigmoid_topk_router_ref(x, rw, G_K, "f32")
+        t_r = time.perf_counter()
+        for e in experts:
+            e(xe)
+        return time.perf_counter() - t_r
+
+    step()
+    steps, t0, t_exp = 0, time.perf_counter(), 0.0
+    while True:
+        t_exp += step()
+        steps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or steps >= 50:
+            break
+    per_step = el / steps
+    t_router = per_step - t_exp / steps
+    layer_s = t_router + (t_exp / steps) * 115.0 / n_exp
+    return G_T / layer_s, layer_s * 1e3, (f"{steps} samples of {n_exp} expert MLPs at {tok_per_exp} tokens each "
+                                          f"plus the router over {G_T} tokens (numpy float32 dequant-then-matmul); "
+                                          f"layer time = router + expert time x 115/{n_exp} touched experts")
+
+
+def glm_c4(args, dev, world, rank, barrier, max_over_ranks):
+    """Config 4 on `world` GPUs (expert-parallel when world > 1): device time per
+    layer step (CUDA graph replay, max over ranks), tok/s of the whole job
+    (world * 32 / step), the parity self-check on rank 0, per-rank algorithmic
+    HBM bytes (the rank's touched experts + activations) / step time, and the
+    end-to-end rate through the public module with host copies."""
+    import torch
+    import torch.distributed as dist
+    from hydranet_b200 import ops, synth
+    from hydranet_b200.ep import ExpertParallelMoE
+    from hydranet_b200.moe import MoELayerInt4
+    from hydranet_b200.packing import ExpertTable
+    from hydranet_b200.router import GLM4SigmoidRouter
+
+    per = G_E // world
+    shape = synth.MoEShape(G_H, G_F, G_E, G_K)
+    layers, full_tables, routers = [], [], []
+    for li in range(G_LAYERS):
+        slots = synth.device_experts(7000 + li, shape, dev)  # every rank builds the same 128 experts
+        r = GLM4SigmoidRouter(hidden_dim=G_H, num_experts=G_E, experts_per_token=G_K).to(dev)
+        with torch.no_grad():
+            r.weight.copy_(torch.randn(G_E, G_H, generator=torch.Generator(dev).manual_seed(31 + li), device=dev)
+                           * 0.02)
+        r.set_correction_bias(torch.from_numpy(synth.host_correction_bias(41 + li, G_E)).to(dev))
+        routers.append(r)
+        if world > 1:
+            layers.append(ExpertParallelMoE(r, ExpertTable(slots[rank * per:(rank + 1) * per]), G_E).eval())
+            full_tables.append(ExpertTable(slots) if rank == 0 and li == 0 else None)
+        else:
+            layers.append(MoELayerInt4(r, ExpertTable(slots)).eval())
+            full_tables.append(None)
+        del slots
+    xs = [torch.randn(G_T, G_H, generator=torch.Generator(dev).manual_seed(500 + 10 * rank + li), device=dev)
+          .to(torch.bfloat16) for li in range(G_LAYERS)]
+    # touched experts of this rank (any rank's tokens) -> algorithmic bytes per step
+    touched = []
+    with torch.no_grad():
+        for li in range(G_LAYERS):
+            idx, _, _ = ops.moe_route(xs[li], routers[li].params(), G_E, want_logits=False)
+            if world > 1:
+                allidx = [torch.empty_like(idx) for _ in range(world)]
+                dist.all_gather(allidx, idx)
+                idx = torch.cat(allidx)
+                idx = idx[(idx >= rank * per) & (idx < (rank + 1) * per)]
+            touched.append(int(torch.unique(idx).numel()))
+    algo = statistics.mean(touched) * blob_bytes(G_H, G_F) + 2 * G_T * G_H * 2 + G_E * G_H * 4
+    # parity self-check on rank 0: the expert-parallel output against one GPU holding all experts
+    parity, index_match = None, None
+    with torch.no_grad():
+        y = layers[0](xs[0])
+        if rank == 0:
+            if world > 1:
+                ref_layer = MoELayerInt4(routers[0], full_tables[0]).eval()
+                ref, ro = ref_layer(xs[0], return_routing=True)
+                idx_ep, _, _ = ops.moe_route(xs[0], routers[0].params(), G_E, want_logits=False)
+                index_match = bool(torch.equal(idx_ep.long(), ro.expert_indices))
+                parity = float((y.float() - ref.float()).norm() / ref.float().norm())
+                del ref_layer
+            else:
+                index_match, parity = True, 0.0
+    full_tables = None
+    torch.cuda.synchronize(dev)
+    barrier()
+    graphs, note = None, None
+    with torch.no_grad():
+        try:
+            st = torch.cuda.Stream(dev)
+            st.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(st):
+                for li in range(G_LAYERS):
+                    layers[li](xs[li])  # warm-up on the capture stream (workspaces, communicators)
+                torch.cuda.synchronize(dev)
+                graphs = []
+                for li in range(G_LAYERS):
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=st):
+                        layers[li](xs[li])
+                    graphs.append(g)
+            torch.cuda.current_stream(dev).wait_stream(st)
+            torch.cuda.synchronize(dev)
+        except Exception as exc:  # noqa: BLE001 - a capture failure falls back to eager steps
+            graphs, note = None, repr(exc)[:200]
+            torch.cuda.synchronize(dev)
+        ok = torch.tensor([1 if graphs else 0], device=dev, dtype=torch.int32)
+        if world > 1:
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0:
+            graphs = None
+
+        def step(i):
+            if graphs:
+                graphs[i % G_LAYERS].replay()
+            else:
+                layers[i % G_LAYERS](xs[i % G_LAYERS])
+
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index or 0) as clk:
+            ev0.record()
+            for i in range(args.steps):
+                step(i)
+            ev1.record()
+            torch.cuda.synchronize(dev)
+        ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+        barrier()
+        captured = bool(graphs)
+        # graphs holding NCCL work are released before the process group goes
+        for gr in graphs or []:
+            gr.reset()
+        graphs, g, gr = None, None, None
+        torch.cuda.synchronize(dev)
+        # end to end through the public module: pinned host input -> device -> layer -> host
+        x_host = [xs[li].cpu().pin_memory() for li in range(G_LAYERS)]
+        x_dev = torch.empty(G_T, G_H, device=dev, dtype=torch.bfloat16)
+        out_host = torch.empty(G_T, G_H, dtype=torch.bfloat16).pin_memory()
+        for i in range(args.warmup):
+            x_dev.copy_(x_host[i % G_LAYERS], non_blocking=True)
+            out_host.copy_(layers[i % G_LAYERS](x_dev), non_blocking=True)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            x_dev.copy_(x_host[i % G_LAYERS], non_blocking=True)
+            out_host.copy_(layers[i % G_LAYERS](x_dev), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        barrier()
+    hbm_peak, _, peak_kind = peaks()
+    gbs = algo / (ms * 1e-3) / 1e9
+    res = {"workload": G_WORKLOAD, "n_gpus": world, "tokens_per_gpu": G_T, "hidden": G_H, "moe_ffn": G_F,
+           "experts": G_E, "experts_per_gpu": per, "top_k": G_K, "router": "sigmoid top-8, correction bias",
+           "layers_rotated": G_LAYERS, "ms_per_step": ms, "tok_s": world * G_T / (ms * 1e-3),
+           "cuda_graph": captured, "parity_rel_l2": parity, "index_match": index_match,
+           "touched_experts_per_gpu": statistics.mean(touched),
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                        "peak_kind": peak_kind, "algo_bytes_per_gpu_step": algo,
+                        "kernel": "whole layer step per rank (route, pack, all-to-all, experts, all-to-all, combine)"
+                        if world > 1 else "whole layer step (route, experts, combine)"},
+           "e2e": {"value": world * G_T / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": G_T * G_H * 2,
+                   "d2h_bytes_per_step": G_T * G_H * 2, "ms_per_step": e2e_ms},
+           "clocks": clk.summary()}
+    if note and rank == 0:
+        res["graph_note"] = note
+    del layers, routers, xs
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -386,29 +621,6 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     _lib.load()
 
-    ep = world > 1
-    local_e = E // world if ep else E
-    shape = synth.MoEShape(H, F, local_e, TOPK)
-    sweep = tuple(int(t) for t in args.sweep.split(","))
-    if ep:
-        sweep = (args.tokens,)  # expert-parallel runs time the headline batch only
-    n_layers = max(1, args.layers)
-    layers = []
-    for li in range(n_layers):
-        table = ExpertTable(synth.device_experts(1000 * rank + li, shape, dev))
-        r = TopKRouter(hidden_dim=H, num_experts=E, experts_per_token=TOPK).to(dev, torch.bfloat16)
-        with torch.no_grad():
-            r.gate.weight.copy_(torch.randn(E, H, generator=torch.Generator(dev).manual_seed(77 + li),
-                                            device=dev) * 0.02)
-        if ep:
-            # experts sharded over the ranks: E/N per GPU, NCCL all-to-all dispatch and combine
-            from hydranet_b200.ep import ExpertParallelMoE
-            layers.append(ExpertParallelMoE(r, table, E).eval())
-        else:
-            layers.append(MoELayerInt4(r, table).eval())
-    torch.cuda.synchronize()
-    hbm_peak, _, peak_kind = peaks()
-
     def barrier():
         if world > 1:
             dist.barrier()
@@ -420,6 +632,43 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if world > 1:
+        # expert-parallel runs measure config 4 (GLM-4.5-Air layer, 32 sequences per GPU)
+        g = glm_c4(args, dev, world, rank, barrier, max_over_ranks)
+        if rank == 0:
+            line = {
+                "metric": METRIC, "value": g["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": g["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded, weights ~N(0,0.02) INT4 g128, activations ~N(0,1))",
+                "config": {"workload": G_WORKLOAD, "tokens_per_gpu": G_T, "hidden": G_H, "moe_ffn": G_F,
+                           "experts": G_E, "top_k": G_K, "group_size": 128, "layers_rotated": G_LAYERS,
+                           "l2": f"{G_LAYERS} distinct layers rotated (>= 2 x 130 MB of touched weights per rank)",
+                           "cuda_graph": g["cuda_graph"],
+                           "parallelism": f"ep{world} (experts sharded, NCCL all-to-all, one row per token and rank)"},
+                "roofline": {**g["roofline"], "traffic": None},
+                "e2e": g["e2e"], "gpu_launches": 8 * args.steps, "clocks": g["clocks"],
+                "parity_rel_l2": g["parity_rel_l2"], "index_match": g["index_match"], "glm_c4": g,
+                "cpu_baseline": None,
+            }
+            print(json.dumps(line), flush=True)
+        dist.destroy_process_group()
+        return
+
+    shape = synth.MoEShape(H, F, E, TOPK)
+    sweep = tuple(int(t) for t in args.sweep.split(","))
+    n_layers = max(1, args.layers)
+    layers = []
+    for li in range(n_layers):
+        table = ExpertTable(synth.device_experts(1000 * rank + li, shape, dev))
+        r = TopKRouter(hidden_dim=H, num_experts=E, experts_per_token=TOPK).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            r.gate.weight.copy_(torch.randn(E, H, generator=torch.Generator(dev).manual_seed(77 + li),
+                                            device=dev) * 0.02)
+        layers.append(MoELayerInt4(r, table).eval())
+    torch.cuda.synchronize()
+    hbm_peak, _, peak_kind = peaks()
+
     results = {}
     for T in sweep:
         xs = [torch.randn(T, H, generator=torch.Generator(dev).manual_seed(T * 10 + i), device=dev)
@@ -429,79 +678,8 @@ def main():
         with torch.no_grad():
             for li, layer in enumerate(layers):
                 idx = layer.router(xs[li].view(1, T, H)).expert_indices.reshape(-1)
-                if ep:
-                    # experts of THIS rank touched by any rank's tokens
-                    allidx = [torch.empty_like(idx) for _ in range(world)]
-                    dist.all_gather(allidx, idx)
-                    idx = torch.cat(allidx)
-                    idx = idx[(idx >= rank * local_e) & (idx < (rank + 1) * local_e)]
                 touched.append(int(torch.unique(idx).numel()))
         algo_bytes = statistics.mean(touched) * blob_bytes(H, F) + 2 * T * H * 2 + E * H * 2
-        if ep:
-            # The exchange never reads back to the host, so each layer's step
-            # (route, all-to-all, local experts, all-to-all, combine) is
-            # captured in a CUDA graph; every rank must capture for any to
-            # replay (a MIN over ranks), otherwise all ranks time eager steps.
-            graphs, note = None, None
-            with torch.no_grad():
-                try:
-                    s = torch.cuda.Stream(dev)
-                    s.wait_stream(torch.cuda.current_stream(dev))
-                    with torch.cuda.stream(s):
-                        for li, layer in enumerate(layers):
-                            layer(xs[li])  # warm-up on the capture stream (workspaces, communicators)
-                        torch.cuda.synchronize(dev)
-                        graphs = []
-                        for li, layer in enumerate(layers):
-                            g = torch.cuda.CUDAGraph()
-                            with torch.cuda.graph(g, stream=s):
-                                layer(xs[li])
-                            graphs.append(g)
-                    torch.cuda.current_stream(dev).wait_stream(s)
-                    torch.cuda.synchronize(dev)
-                except Exception as exc:  # noqa: BLE001 - any capture failure falls back to eager steps
-                    graphs, note = None, repr(exc)[:200]
-                    torch.cuda.synchronize(dev)
-                ok = torch.tensor([1 if graphs else 0], device=dev, dtype=torch.int32)
-                dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-                if int(ok.item()) == 0:
-                    graphs = None
-
-                def step(i):
-                    if graphs:
-                        graphs[i % n_layers].replay()
-                    else:
-                        layers[i % n_layers](xs[i % n_layers])
-
-                for i in range(args.warmup):
-                    step(i)
-                torch.cuda.synchronize(dev)
-                barrier()
-                torch.cuda.synchronize(dev)
-                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                with ClockSampler(local) as clk:
-                    ev0.record()
-                    for i in range(args.steps):
-                        step(i)
-                    ev1.record()
-                    torch.cuda.synchronize(dev)
-            ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
-            barrier()
-            results[T] = {"ms_per_step": ms, "tok_s": world * T / (ms * 1e-3),
-                          "touched_experts": statistics.mean(touched), "algo_bytes": algo_bytes,
-                          "gbs": algo_bytes / (ms * 1e-3) / 1e9, "clocks": clk.summary(),
-                          "cuda_graph": bool(graphs)}
-            if note and rank == 0:
-                results[T]["graph_note"] = note
-            results[T]["frac"] = results[T]["gbs"] / hbm_peak
-            # graphs holding NCCL work are released before the process group
-            # goes (every reference: the list and the capture loop's variable),
-            # or its teardown waits for good
-            for gr in graphs or []:
-                gr.reset()
-            graphs, g, gr = None, None, None
-            torch.cuda.synchronize(dev)
-            continue
         # capture one graph per layer (warm up on a side stream first)
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
@@ -519,8 +697,6 @@ def main():
         for i in range(args.warmup):
             graphs[i % n_layers].replay()
         torch.cuda.synchronize(dev)
-        barrier()
-        torch.cuda.synchronize(dev)
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clk:
             ev0.record()
@@ -529,25 +705,21 @@ def main():
             ev1.record()
             torch.cuda.synchronize(dev)
         ms = ev0.elapsed_time(ev1) / args.steps
-        barrier()
-        ms = max_over_ranks(ms)
-        results[T] = {"ms_per_step": ms, "tok_s": world * T / (ms * 1e-3), "touched_experts": statistics.mean(touched),
+        results[T] = {"ms_per_step": ms, "tok_s": T / (ms * 1e-3), "touched_experts": statistics.mean(touched),
                       "algo_bytes": algo_bytes, "gbs": algo_bytes / (ms * 1e-3) / 1e9,
                       "clocks": clk.summary()}
         results[T]["frac"] = results[T]["gbs"] / hbm_peak
         del graphs, outs
         torch.cuda.synchronize(dev)
 
-    # dominant kernel: the gate/up engine, timed live with CUDA events around
-    # its own launch (the layer issued as its three phases, eager, same stream)
+    # per-phase device times of the headline batch, with CUDA events between
+    # the layer's three launches (eager, same stream); the dominant kernel is
+    # the gate/up launch
     T = args.tokens if args.tokens in results else max(results)
-    kernel_times, gu_ms, gu_bytes = {}, None, None
     xk = [torch.randn(T, H, generator=torch.Generator(dev).manual_seed(T * 10 + i), device=dev).to(torch.bfloat16)
           for i in range(n_layers)]
     stream = torch.cuda.current_stream(dev)
     evs = []
-    if ep:
-        xk = []
 
     def mark(phase):
         ev = torch.cuda.Event(enable_timing=True)
@@ -555,15 +727,14 @@ def main():
         evs[-1].append(ev)
 
     with torch.no_grad():
-        for i in range(args.warmup if not ep else 0):
+        for i in range(args.warmup):
             layers[i % n_layers].forward_phases(xk[i % n_layers])
         torch.cuda.synchronize(dev)
         # hold the stream with a device-side sleep while the host queues every
         # timed launch, so the kernels run back to back and the events bracket
         # device time only (not host launch gaps)
-        if not ep:
-            torch.cuda._sleep(int(2e8))
-        for i in range(args.steps if not ep else 0):
+        torch.cuda._sleep(int(2e8))
+        for i in range(args.steps):
             e0 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             evs.append([e0])
@@ -572,13 +743,14 @@ def main():
             e3.record(stream)
             evs[-1].append(e3)
         torch.cuda.synchronize(dev)
-    if not ep:
-        prep_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-        gu_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-        down_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
-        touched_t = results[T]["touched_experts"]
-        gu_bytes = touched_t * 2 * F * (H // 2 + 2 * (H // 128)) + T * H * 2
-        kernel_times = {"prep_ms": prep_ms, "gateup_ms": gu_ms, "down_ms": down_ms}
+    prep_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    gu_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    down_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    touched_t = results[T]["touched_experts"]
+    gu_bytes = touched_t * 2 * F * (H // 2 + 2 * (H // 128)) + T * H * 2
+    kernel_times = {"prep_ms": prep_ms, "gateup_ms": gu_ms, "down_ms": down_ms}
+    gu_kernel = "gv_kernel gate/up (dominant)" if decode_engine(T) == "mma.sync" else \
+        "tc_engine_kernel gate/up (dominant)"
 
     # end-to-end through the public API: pinned host input -> device -> layer -> host
     x_host = [torch.randn(T, H, generator=torch.Generator().manual_seed(5 + i)).to(torch.bfloat16).pin_memory()
@@ -590,7 +762,6 @@ def main():
             x_dev.copy_(x_host[i % n_layers], non_blocking=True)
             out_host.copy_(layers[i % n_layers](x_dev), non_blocking=True)
         torch.cuda.synchronize(dev)
-        barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()
         for i in range(args.steps):
@@ -598,50 +769,48 @@ def main():
             out_host.copy_(layers[i % n_layers](x_dev), non_blocking=True)
         ev1.record()
         torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
-    barrier()
+    e2e_ms = ev0.elapsed_time(ev1) / args.steps
+    del layers
+    torch.cuda.empty_cache()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if not args.no_cpu_baseline:
         v, n, el = cpu_oracle_time(T, budget_s=args.ref_budget)
         cpu = {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
                "sample": f"{n} oracle layer steps at T={T} in {el:.1f}s (numpy float32 dequant-then-matmul, "
                          f"dequantisation done before timing)"}
 
-    prefill = None
-    if rank == 0 and world == 1 and not args.no_prefill:
-        prefill = prefill_measure(args, dev)
+    prefill = None if args.no_prefill else prefill_measure(args, dev)
+    glm = glm_c4(args, dev, 1, 0, barrier, max_over_ranks)
+    if not args.no_cpu_baseline:
+        gv, gms, gsample = glm_cpu_time()
+        glm["cpu_baseline"] = {"value": gv, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+                               "sample": gsample, "ms_per_step": gms}
 
-    if rank == 0:
-        hr = results[T]
-        line = {
-            "metric": METRIC, "value": hr["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": hr["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, weights ~N(0,0.02) INT4 g128)",
-            "config": {"workload": WORKLOAD, "tokens": T, "hidden": H, "ffn": F, "experts": E, "top_k": TOPK,
-                       "group_size": 128, "layers_rotated": n_layers, "l2": "weights per step > L2 (126 MB), "
-                       f"{n_layers} distinct layers rotated", "cuda_graph": bool(hr.get("cuda_graph", True)),
-                       "parallelism": f"ep{world} (experts sharded, NCCL all-to-all)" if ep else "single"},
-            "roofline": ({"bound": "hbm", "achieved": gu_bytes / (gu_ms * 1e-3) / 1e9, "peak": hbm_peak,
-                          "unit": "GB/s", "frac": gu_bytes / (gu_ms * 1e-3) / 1e9 / hbm_peak,
-                          "traffic": GATEUP_TRAFFIC.get(T), "kernel": "tc_engine_kernel gate/up (dominant)",
-                          "algo_bytes_per_launch": gu_bytes, "launch_ms": gu_ms, "peak_kind": peak_kind,
-                          "layer": {"achieved": hr["gbs"], "frac": hr["frac"], **kernel_times}} if not ep else
-                         {"bound": "hbm", "achieved": hr["gbs"], "peak": hbm_peak, "unit": "GB/s",
-                          "frac": hr["frac"], "traffic": None, "peak_kind": peak_kind,
-                          "kernel": "expert-parallel layer step per rank (route, all-to-all, experts, all-to-all)"}),
-            "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
-                    "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e_ms},
-            "gpu_launches": (decode_launches(T) if not ep else 5) * args.steps,
-            "clocks": hr["clocks"],
-            "cpu_baseline": cpu,
-            "prefill": prefill,
-            "sweep": {str(t): {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items() if k != "clocks"}
-                      for t, r in results.items()},
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    hr = results[T]
+    line = {
+        "metric": METRIC, "value": hr["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": hr["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, weights ~N(0,0.02) INT4 g128)",
+        "config": {"workload": WORKLOAD, "tokens": T, "hidden": H, "ffn": F, "experts": E, "top_k": TOPK,
+                   "group_size": 128, "layers_rotated": n_layers, "l2": "weights per step > L2 (126 MB), "
+                   f"{n_layers} distinct layers rotated", "cuda_graph": True, "parallelism": "single"},
+        "roofline": {"bound": "hbm", "achieved": gu_bytes / (gu_ms * 1e-3) / 1e9, "peak": hbm_peak,
+                     "unit": "GB/s", "frac": gu_bytes / (gu_ms * 1e-3) / 1e9 / hbm_peak,
+                     "traffic": GATEUP_TRAFFIC.get(T), "kernel": gu_kernel,
+                     "algo_bytes_per_launch": gu_bytes, "launch_ms": gu_ms, "peak_kind": peak_kind,
+                     "layer": {"achieved": hr["gbs"], "frac": hr["frac"], **kernel_times}},
+        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2, "ms_per_step": e2e_ms},
+        "gpu_launches": decode_launches(T) * args.steps,
+        "clocks": hr["clocks"],
+        "cpu_baseline": cpu,
+        "prefill": prefill,
+        "glm_c4": glm,
+        "sweep": {str(t): {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items() if k != "clocks"}
+                  for t, r in results.items()},
+    }
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -70,6 +70,12 @@ SIGNATURES = {
                                       c_int, c_void_p, c_int64, c_void_p]),
     "hn_selftest_wait_timeout": (c_int, [c_void_p, c_size_t, c_int, c_void_p]),
     "hn_set_decode_engine": (c_int, [c_int]),
+    "hn_ep_row_bytes": (c_size_t, [c_int64, c_int]),
+    "hn_ep_pack": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p, c_void_p, c_int64, c_int, c_void_p,
+                           c_void_p]),
+    "hn_ep_unpack": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "hn_ep_combine": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p, c_int64, c_int, c_void_p,
+                              c_void_p]),
     "hn_int4_linear_static_scratch_size": (c_size_t, [c_int64, c_int64, c_int64]),
     "hn_int4_linear_static_error": (c_int, [ctypes.POINTER(c_int), c_void_p]),
 }

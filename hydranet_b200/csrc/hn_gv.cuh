@@ -107,6 +107,8 @@ struct GvArgs {
   float* part;
   int* tile_ctr;
   int* rt_ctr;
+  const int* nval;  // [T] slots per token that hold an expert
+  const int* tidx;  // [T*K] expert of each slot, -1 = unused
   int defer_combine;
   int early;  // KIND_DOWN right after a gate/up launch: the plan is visible at entry, the staged rows later
   int P;
@@ -410,7 +412,8 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
         __syncthreads();
         if (tid < seg_m) {
           const int t = __ldcg(a.a_tok + seg_first + tid);
-          if (atomicAdd(a.rt_ctr + (int64_t)rt * a.T + t, 1) == a.topk - 1) s_misc[2 + atomicAdd(&s_misc[1], 1)] = t;
+          if (atomicAdd(a.rt_ctr + (int64_t)rt * a.T + t, 1) == __ldcg(a.nval + t) - 1)
+            s_misc[2 + atomicAdd(&s_misc[1], 1)] = t;
         }
         __syncthreads();
         __threadfence();
@@ -420,7 +423,9 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
           const int t = s_misc[2 + li];
           if (r < a.rows) {
             float sum = 0.f;
-            for (int k = 0; k < a.topk; ++k) sum += __ldcg(a.R + ((int64_t)t * a.topk + k) * a.rows + r);
+            for (int k = 0; k < a.topk; ++k)
+              if (__ldcg(a.tidx + (int64_t)t * a.topk + k) >= 0)  // unused slots wrote no row
+                sum += __ldcg(a.R + ((int64_t)t * a.topk + k) * a.rows + r);
             reinterpret_cast<typename Tr::T*>(a.out)[(int64_t)t * a.ldo + r] = Tr::from_f(sum);
           }
         }

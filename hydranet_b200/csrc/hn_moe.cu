@@ -56,6 +56,7 @@ struct Plan {
   int* pos;      // [T*K] assignment index of (t, k)
   int* idx;      // [T*K] top-k expert ids
   float* wts;    // [T*K] top-k weights (rounded to the activation dtype)
+  int* nval;     // [T] slots of each token that hold an expert (caller routing may leave slots -1)
   uint8_t* xp;   // [T][K_in/128][kChunk]    staged activations (token-major)
   uint8_t* hp;   // [T*K][F/128][kChunk]     staged SiLU(gate)*up (assignment-major)
   uint8_t* xs;   // [T*K][K_in/128][kChunk]  staged activations in assignment order (large routings), or NULL
@@ -355,17 +356,12 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   } else if (tid == 0) {
     for (int k = 0; k < a.K; ++k) {
       if (a.mode == ROUTE_GIVEN) {
-        // -1 marks an unused slot: a token with only unused slots is left out
-        // of the plan; unused slots next to real picks are weight-0 picks
-        int n_unused = 0;
-        for (int kk = 0; kk < a.K; ++kk) n_unused += a.given_idx[(int64_t)t * a.K + kk] == -1;
+        // -1 marks an unused slot: it takes no expert work and adds nothing
+        // to the combine; a token with only unused slots is left out entirely
         int e = a.given_idx[(int64_t)t * a.K + k];
         float w = a.given_w[(int64_t)t * a.K + k];
         if (e == -1) {
-          if (n_unused < a.K) {
-            e = 0;
-            w = 0.f;
-          }
+          w = 0.f;
         } else if (e < 0 || e >= a.E) {
           record_error(a.plan.err, DEV_ERR_BAD_INDEX);
           e = 0;
@@ -379,6 +375,11 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
     }
   }
   __syncthreads();
+  if (tid == 0) {
+    int nv = 0;
+    for (int k = 0; k < a.K; ++k) nv += s_idx[k] >= 0;
+    a.plan.nval[t] = nv;
+  }
   if (tid < a.K) {
     a.plan.idx[(int64_t)t * a.K + tid] = s_idx[tid];
     a.plan.wts[(int64_t)t * a.K + tid] = s_w[tid];
@@ -825,6 +826,8 @@ struct EngineArgs {
   float* part;
   int* tile_ctr;
   int* rt_ctr;
+  const int* nval;  // [T] slots per token that hold an expert (the combine's completion count)
+  const int* tidx;  // [T*K] expert of each slot, -1 = unused (skipped by the combine)
   int* err;
   int P;
   int early;  // KIND_DOWN after a gate/up launch: only the token producer waits for it
@@ -1410,7 +1413,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
       if (et < ti.m) {
         const int t = a.a_tok[ti.p0 + et];
         int* ctr = a.rt_ctr + (int64_t)ti.rt * a.T + t;
-        const bool last = atomicAdd(ctr, 1) == a.topk - 1;
+        const bool last = atomicAdd(ctr, 1) == __ldcg(a.nval + t) - 1;
         if (last) *ctr = 0;
         bcast[2 + et] = last ? t : -1;
       }
@@ -1426,6 +1429,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
           if (t >= 0) {
             float x = 0.f, y = 0.f;
             for (int kk = 0; kk < a.topk; ++kk) {
+              if (__ldcg(a.tidx + (int64_t)t * a.topk + kk) < 0) continue;  // an unused slot: no row was written
               const float2 v = __ldcg(reinterpret_cast<const float2*>(Rb + (int64_t)(t * a.topk + kk) * a.N));
               x += v.x;
               y += v.y;
@@ -1541,12 +1545,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_engine_kernel(const __grid_c
 // Decode-size routings combine inside the down-phase epilogue instead.
 // ---------------------------------------------------------------------------
 template <typename Tr>
-__global__ void __launch_bounds__(256) combine_kernel(const float* R, int T, int K, int H, void* out, int64_t ldo) {
+__global__ void __launch_bounds__(256) combine_kernel(const float* R, const int* tidx, int T, int K, int H, void* out,
+                                                      int64_t ldo) {
   const int64_t n4 = (int64_t)T * (H / 4);
   for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n4; i += (int64_t)gridDim.x * 256) {
     const int t = (int)(i / (H / 4)), h = (int)(i - (int64_t)t * (H / 4)) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < K; ++k) {
+      if (__ldg(tidx + (int64_t)t * K + k) < 0) continue;  // an unused slot: no row was written
       const float4 v = __ldcs(reinterpret_cast<const float4*>(R + ((int64_t)t * K + k) * H + h));
       acc.x += v.x;
       acc.y += v.y;
@@ -1681,6 +1687,8 @@ static GvArgs gv_args(const EngineArgs& e, int KIND) {
   g.part = e.part;
   g.tile_ctr = e.tile_ctr;
   g.rt_ctr = e.rt_ctr;
+  g.nval = e.nval;
+  g.tidx = e.tidx;
   g.defer_combine = e.defer_combine;
   g.early = e.early;
   g.P = e.P;
@@ -1743,8 +1751,8 @@ static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
 // call, because another shape's data section may have covered them.
 struct Layout {
   size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
-  size_t counts, n_segs, segs, n_segs2, segs2, a_tok, a_tk, a_w, pos, idx, wts, xp, hp, xs, part1, part2, R, rlog,
-      data;  // back (relative)
+  size_t counts, n_segs, segs, n_segs2, segs2, a_tok, a_tk, a_w, pos, idx, wts, nval, xp, hp, xs, part1, part2, R,
+      rlog, data;  // back (relative)
   bool has_rlog, has_xs;
   int seg2;          // second segment cut for the down phase (0: none)
   int64_t max_segs;  // segments the plan can hold
@@ -1791,6 +1799,7 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.pos = take(4 * TK);
   l.idx = take(4 * TK);
   l.wts = take(4 * TK);
+  l.nval = take(4 * T);
   l.xp = take((size_t)(Kin / 128) * T * kChunk);
   l.hp = take(F ? (size_t)(F / 128) * TK * kChunk : 0);
   // routed gate/up tokens staged in assignment order, read by TMA instead of
@@ -1836,6 +1845,7 @@ static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
   p.pos = reinterpret_cast<int*>(d + l.pos);
   p.idx = reinterpret_cast<int*>(d + l.idx);
   p.wts = reinterpret_cast<float*>(d + l.wts);
+  p.nval = reinterpret_cast<int*>(d + l.nval);
   p.xp = d + l.xp;
   p.hp = d + l.hp;
   p.xs = l.has_xs ? d + l.xs : nullptr;
@@ -2102,6 +2112,8 @@ static int run_moe(const MoECall& m) {
   e1.allow_rr = nt >= 8;
   e1.max_segs = l.max_segs;
   e1.max_nt = nt;
+  e1.nval = plan.nval;
+  e1.tidx = plan.idx;
   if (m.phase == 0 || m.phase == 2) rc = launch_engine<Tr, KIND_GATEUP, EPI_COMBINE>(nt, e1, m.stream);
   if (rc || m.phase == 2) return rc;
 
@@ -2137,7 +2149,7 @@ static int run_moe(const MoECall& m) {
   if (rc || !e2.defer_combine) return rc;
   const int64_t n4 = m.T * (m.H / 4);
   const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)grid_p(nt) * 8);
-  combine_kernel<Tr><<<blocks, 256, 0, m.stream>>>(plan.R, (int)m.T, m.topk, (int)m.H, m.out, m.ldo);
+  combine_kernel<Tr><<<blocks, 256, 0, m.stream>>>(plan.R, plan.idx, (int)m.T, m.topk, (int)m.H, m.out, m.ldo);
   HN_CUDA(cudaGetLastError());
   return HN_OK;
 }
@@ -2426,6 +2438,8 @@ int int4_linear_nt(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   e.allow_rr = nt >= 8;
   e.max_segs = l.max_segs;
   e.max_nt = nt;
+  e.nval = plan.nval;
+  e.tidx = plan.idx;
   int rc;
   if (dtype == HN_DTYPE_BF16) {
     rc = launch_route<BF16>(ra, s);

@@ -2,33 +2,32 @@
 
 Experts are partitioned in contiguous blocks: rank ``r`` of ``W`` owns experts
 ``[r*E/W, (r+1)*E/W)`` (GLM-4.5-Air: 64/32/16 experts per GPU at 2/4/8).
-Each rank routes its own tokens, then per layer, all on the device (no
-host synchronisation, so the host keeps queueing work):
+Each rank routes its own T tokens, then per layer, all on the device (no
+host synchronisation, so a step can be captured in a CUDA graph):
 
-1. the T*k assignments are grouped by owner rank and placed into a send
-   buffer of W blocks of C = T*k fixed slots (any split of the assignments
-   fits), one byte row per slot: the token's activations, its global expert
-   id (int32, -1 in an unused slot) and its routing weight (float32);
-2. one ``all_to_all_single`` with equal splits delivers block r to rank r;
-3. the rank's grouped kernel runs over the W*C received rows with
-   caller-supplied routing (``hn_moe_experts_int4``: top-1 per row with its
-   routing weight, so it returns weight * MLP_e(x); rows whose id is -1 are
-   skipped and cost no expert work);
-4. the mirror ``all_to_all_single`` returns the rows to their source ranks,
-   which sum the k rows of each token in slot order in float32 and cast to
-   the activation dtype.
+1. ``hn_ep_pack`` writes a send buffer of W blocks of T fixed rows: row t of
+   block d carries token t -- its activations only when one of its top-k picks
+   lives on rank d, so a token crosses to each rank at most once whatever its
+   k -- and its top-k list as rank d's local expert ids (-1 for picks owned
+   elsewhere) with the routing weights;
+2. one ``all_to_all_single`` with equal splits delivers block d to rank d;
+3. ``hn_ep_unpack`` lays the W*T received rows out for the grouped kernel,
+   which runs them with caller-supplied top-k routing (``hn_moe_experts_int4``:
+   each row's output is the weighted sum of its local picks; rows whose picks
+   are all -1 are skipped and cost no expert work);
+4. the mirror ``all_to_all_single`` returns each row to its source rank;
+5. ``hn_ep_combine`` sums, per token and in rank order in fp32, the partial
+   outputs of the ranks that held one of its picks.
 
 The reference runs experts one at a time in Python on one GPU
-(``model/mixtral.py:282-370``, ``model/glm4.py:375-473``); the exchange is the
-standard expert-parallel dispatch/combine.  One row is sent per (token, slot)
-assignment and the combine order is the slot order, so results do not depend
-on the number of ranks beyond fp32 summation of the k partial outputs.  The
-fixed slots trade a few MB of padding per step (W*T*k rows, mostly empty) for
-split sizes that never have to be read back to the host.
+(``model/mixtral.py:282-370``, ``model/glm4.py:375-473``) and lists expert
+parallelism on its roadmap (``README.md:179``).  Per step each rank sends and
+receives W*T rows of H*2 + 8k bytes: at GLM-4.5 decode (T = 32, k = 8, W = 8)
+that is 2 MB each way, against 16 MB with one row per (token, slot).
 
-``local_fn`` computes step 3 and defaults to the CUDA grouped kernel; tests
-on CPU ranks (gloo) pass a reference implementation to check the exchange
-bookkeeping without a GPU.
+``local_fn`` computes step 3 and ``exchange`` steps 1, 3 and 5; both default
+to the CUDA kernels.  Tests on CPU ranks (gloo) pass reference
+implementations to check the exchange bookkeeping without a GPU.
 """
 
 from __future__ import annotations
@@ -47,69 +46,77 @@ def expert_range(num_experts: int, rank: int, world: int) -> Tuple[int, int]:
     return rank * per, (rank + 1) * per
 
 
-def owner_of(expert: torch.Tensor, num_experts: int, world: int) -> torch.Tensor:
-    return torch.div(expert, num_experts // world, rounding_mode="floor")
+class CudaExchange:
+    """Steps 1, 3 and 5 on the device (``hn_ep_pack`` / ``hn_ep_unpack`` / ``hn_ep_combine``)."""
+
+    @staticmethod
+    def row_bytes(H: int, k: int) -> int:
+        from . import _lib
+        return int(_lib.load().hn_ep_row_bytes(H, k))
+
+    def pack(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_experts: int, world: int) -> torch.Tensor:
+        from . import _lib
+        T, H = x.shape
+        k = idx.shape[1]
+        send = torch.empty(world * T, self.row_bytes(H, k), dtype=torch.uint8, device=x.device)
+        _lib.check(_lib.load().hn_ep_pack(x.data_ptr(), _lib.dtype_code(x.dtype), T, H, k, idx.data_ptr(),
+                                          w.data_ptr(), num_experts, world, send.data_ptr(),
+                                          _lib.stream_ptr(x.device)))
+        return send
+
+    def unpack(self, recv: torch.Tensor, H: int, k: int, dtype: torch.dtype):
+        from . import _lib
+        rows = recv.shape[0]
+        xr = torch.empty(rows, H, dtype=dtype, device=recv.device)
+        ir = torch.empty(rows, k, dtype=torch.int32, device=recv.device)
+        wr = torch.empty(rows, k, dtype=torch.float32, device=recv.device)
+        _lib.check(_lib.load().hn_ep_unpack(recv.data_ptr(), _lib.dtype_code(dtype), rows, H, k, xr.data_ptr(),
+                                            ir.data_ptr(), wr.data_ptr(), _lib.stream_ptr(recv.device)))
+        return xr, ir, wr
+
+    def combine(self, back: torch.Tensor, idx: torch.Tensor, num_experts: int, world: int) -> torch.Tensor:
+        from . import _lib
+        T, k = idx.shape
+        H = back.shape[-1]
+        out = torch.empty(T, H, dtype=back.dtype, device=back.device)
+        _lib.check(_lib.load().hn_ep_combine(back.data_ptr(), _lib.dtype_code(back.dtype), T, H, k, idx.data_ptr(),
+                                             num_experts, world, out.data_ptr(), _lib.stream_ptr(back.device)))
+        return out
 
 
 def ep_moe_forward(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_experts: int,
                    local_fn: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor],
-                   group=None) -> torch.Tensor:
+                   group=None, exchange=None) -> torch.Tensor:
     """Expert-parallel dispatch -> local experts -> combine for this rank's tokens.
 
-    x [T, H] (this rank's tokens), idx [T, k] global expert ids, w [T, k]
-    routing weights.  ``local_fn(rows [n, H], local_expert [n], weight [n])``
-    returns weight * MLP_e(row) for each received row whose local expert is
-    >= 0 (activation dtype); rows with local expert -1 are unused slots and
-    their outputs are ignored.
+    x [T, H] (this rank's tokens), idx int32 [T, k] global expert ids, w
+    float32 [T, k] routing weights.  ``local_fn(rows [n, H], ids int32 [n, k],
+    weights float32 [n, k])`` returns, per row, the weighted sum of the
+    row's picks with id >= 0 (this rank's experts, local numbering); rows whose
+    ids are all -1 are unused and their outputs are ignored.
     """
+    ex = exchange if exchange is not None else CudaExchange()
     world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
     T, H = x.shape
     k = idx.shape[1]
-    dev = x.device
-    first, _ = expert_range(num_experts, rank, world)
-    n = T * k
-    C = n  # slots per destination block
-    flat = idx.reshape(-1)
-    dest = owner_of(flat, num_experts, world)
-    order = torch.sort(dest, stable=True).indices  # assignments grouped by destination, slot order kept
-    d_sorted = dest.index_select(0, order)
-    # per-destination counts without torch.bincount (which reads its maximum back to the host)
-    counts = torch.zeros(world, dtype=dest.dtype, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
-    starts = torch.cumsum(counts, 0) - counts
-    row = d_sorted * C + (torch.arange(n, device=dev) - starts.index_select(0, d_sorted))
-    tok = torch.div(order, k, rounding_mode="floor")
-    rb = H * x.element_size()
-    # send buffer: W blocks of C rows; unused rows carry expert id -1 (0xFF bytes)
-    send = torch.zeros(world * C, rb + 8, dtype=torch.uint8, device=dev)
-    send[:, rb:rb + 4] = 255
-    packed = torch.empty(n, rb + 8, dtype=torch.uint8, device=dev)
-    packed[:, :rb] = x.index_select(0, tok).view(torch.uint8).view(-1, rb)
-    packed[:, rb:rb + 4] = flat.index_select(0, order).to(torch.int32).view(-1, 1).view(torch.uint8)
-    packed[:, rb + 4:] = w.reshape(-1).index_select(0, order).to(torch.float32).view(-1, 1).view(torch.uint8)
-    send.index_copy_(0, row, packed)
+    send = ex.pack(x, idx, w, num_experts, world)
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send, group=group)
-    r_rows = recv[:, :rb].contiguous().view(x.dtype).view(-1, H)
-    g = recv[:, rb:rb + 4].contiguous().view(torch.int32).view(-1)
-    local = torch.where(g >= 0, g - first, g)  # global id -> this rank's; -1 stays
-    r_w = recv[:, rb + 4:].contiguous().view(torch.float32).view(-1)
-    y = local_fn(r_rows, local, r_w)
+    rows, ids, wts = ex.unpack(recv, H, k, x.dtype)
+    y = local_fn(rows, ids, wts)
     back = torch.empty_like(y)
     dist.all_to_all_single(back, y.contiguous(), group=group)
-    out = torch.zeros(T, H, dtype=torch.float32, device=dev)
-    out.index_add_(0, tok, back.index_select(0, row).to(torch.float32))
-    return out.to(x.dtype)
+    return ex.combine(back.view(world, T, H), idx, num_experts, world)
 
 
 def cuda_local_fn(table):
-    """Step 3 on the GPU: the grouped kernel over the received rows, each row one
-    assignment (top-1 with its routing weight) into this rank's expert table."""
+    """Step 3 on the GPU: the grouped kernel over the received rows with their
+    top-k local ids and weights (-1 slots take no work; all -1 rows are
+    skipped)."""
     from .moe import moe_experts
 
-    def fn(rows: torch.Tensor, local_expert: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-        # local expert -1 (an unused slot) is skipped by the kernel
-        return moe_experts(rows, local_expert.view(-1, 1).to(torch.int32), weight.view(-1, 1), table)
+    def fn(rows: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+        return moe_experts(rows, ids, weights, table)
 
     return fn
 
@@ -117,27 +124,47 @@ def cuda_local_fn(table):
 class ExpertParallelMoE(torch.nn.Module):
     """MoE layer with experts sharded over the ranks of ``group``.
 
-    ``router`` is the full router (replicated on every rank); ``local_table``
-    is the ``ExpertTable`` of this rank's experts, in global order."""
+    ``router`` is the full router (replicated on every rank: a ``TopKRouter``
+    or ``GLM4SigmoidRouter``); ``local_table`` is the ``ExpertTable`` of this
+    rank's experts, in global order; an optional ``shared_expert`` (GLM-4.5)
+    is replicated and runs on the rank's own tokens."""
 
     def __init__(self, router: torch.nn.Module, local_table, num_experts: int, group=None,
-                 local_fn: Optional[Callable] = None):
+                 local_fn: Optional[Callable] = None, top_k: Optional[int] = None,
+                 shared_expert: Optional[torch.nn.Module] = None):
         super().__init__()
         self.router = router
+        self.shared_expert = shared_expert
         self.table = local_table
         self.num_experts = num_experts
         self.group = group
+        self.top_k = top_k
         world = dist.get_world_size(group)
         if local_table is not None and len(local_table) * world != num_experts:
             raise ValueError("local expert table size times world size must equal the number of experts")
         self.local_fn = local_fn if local_fn is not None else cuda_local_fn(local_table)
 
+    def route(self, x: torch.Tensor):
+        """int32 top-k ids and float32 weights of x [T, H] (one device routing launch)."""
+        from . import ops
+        from .router import GLM4SigmoidRouter, TopKRouter
+        if isinstance(self.router, TopKRouter):
+            k = self.top_k if self.top_k is not None else self.router.experts_per_token
+            bonus = self.router.bonus_vector(x.device)
+            params = self.router.params(k, bonus)
+            keep = (bonus,)
+        elif isinstance(self.router, GLM4SigmoidRouter):
+            params, keep = self.router.params(), ()
+        else:
+            raise TypeError("unsupported router type")
+        idx, w, _ = ops.moe_route(x, params, self.num_experts, keep_refs=keep, want_logits=False)
+        return idx, w
+
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1]).contiguous()
-        out = self.router(x.view(1, *x.shape))  # routers take [batch, seq, hidden]
-        idx, w = (out.expert_indices, out.expert_weights) if hasattr(out, "expert_indices") else out
-        idx = idx.reshape(x.shape[0], -1)
-        w = w.reshape(x.shape[0], -1)
+        idx, w = self.route(x)
         y = ep_moe_forward(x, idx, w, self.num_experts, self.local_fn, self.group)
+        if self.shared_expert is not None:
+            y = self.shared_expert(x) + y
         return y.view(shape)

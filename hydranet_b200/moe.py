@@ -20,18 +20,40 @@ from .packing import ExpertTable
 from .router import GLM4SigmoidRouter, RouterOutput, TopKRouter
 
 
+class SharedExpertMLP(nn.Module):
+    """GLM-4.5's shared expert: a dense MLP every token runs
+    (``GLM4DenseMLP``, ``model/glm4.py:220-235``; built with
+    ``moe_intermediate_dim * num_shared_experts`` rows, ``:341-344``):
+    ``down(silu(gate(x)) * up(x))`` with unquantised weights in the model
+    dtype, so it runs as library GEMMs, as in the reference."""
+
+    def __init__(self, hidden_dim: int, intermediate_dim: int):
+        super().__init__()
+        self.hidden_dim, self.intermediate_dim = hidden_dim, intermediate_dim
+        self.gate_proj = nn.Linear(hidden_dim, intermediate_dim, bias=False)
+        self.up_proj = nn.Linear(hidden_dim, intermediate_dim, bias=False)
+        self.down_proj = nn.Linear(intermediate_dim, hidden_dim, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down_proj(torch.nn.functional.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
 class MoELayerInt4(nn.Module):
-    """Router + INT4 experts + combine.
+    """Router + INT4 experts + combine (+ an optional shared expert).
 
     ``router`` is a ``TopKRouter`` (softmax, Mixtral) or ``GLM4SigmoidRouter``.
     ``forward(hidden [B, S, H] or [T, H]) -> same shape``; with
     ``return_routing=True`` it also returns (idx int64, weights, logits).
+    With ``shared_expert`` (GLM-4.5) the output is
+    ``shared_expert(x) + routed(x)`` as in ``GLM4MoELayer.forward``
+    (``model/glm4.py:378,473``).
     """
 
-    def __init__(self, router: nn.Module, experts: ExpertTable):
+    def __init__(self, router: nn.Module, experts: ExpertTable, shared_expert: Optional[nn.Module] = None):
         super().__init__()
         self.router = router
         self.experts = experts
+        self.shared_expert = shared_expert
         self.num_experts = len(experts)
         if router.num_experts != self.num_experts:
             raise ValueError("router and expert table disagree on the number of experts")
@@ -53,6 +75,8 @@ class MoELayerInt4(nn.Module):
                                             self.num_experts,
                                             self.experts.intermediate_dim, want_routing=return_routing,
                                             keep_refs=(bonus,))
+        if self.shared_expert is not None:
+            out = self.shared_expert(x) + out
         out = out.view(shape)
         if return_routing:
             return out, RouterOutput(idx.long(), w.to(x.dtype), logits)
@@ -69,6 +93,8 @@ class MoELayerInt4(nn.Module):
         out = ops.moe_layer_phases(x, params, self.experts.device_table, self.experts.device_maps,
                                    self.num_experts, self.experts.intermediate_dim, between=between)
         del bonus
+        if self.shared_expert is not None:
+            out = self.shared_expert(x) + out
         return out.view(shape)
 
 

@@ -200,11 +200,10 @@ HN_API int hn_moe_layer_int4_phase(int phase, const void* x, int dtype, int64_t 
 /* Same as hn_moe_layer_int4 but with routing supplied by the caller
  * (topk_idx int32 [T, k], topk_w float32 [T, k]); used for expert-parallel
  * shards and for callers that route on their own.  An index of -1 marks an
- * unused slot: a token whose k slots are all -1 is skipped (no expert work;
- * its output row is left unspecified), and -1 slots of a token with other
- * picks count as weight-0 picks.  Other indices outside [0, E) are read as
- * expert 0 and set error code 2 in the workspace's error word
- * (hn_workspace_error). */
+ * unused slot: it takes no expert work and adds nothing to its token's sum; a
+ * token whose k slots are all -1 is skipped (its output row is left
+ * unspecified).  Other indices outside [0, E) are read as expert 0 and set
+ * error code 2 in the workspace's error word (hn_workspace_error). */
 HN_API int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
                         int top_k, const int32_t* topk_idx, const float* topk_w,
                         const hn_expert_ptrs* experts, const void* expert_maps, void* out,
@@ -214,6 +213,39 @@ HN_API int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, i
 HN_API int hn_moe_route(const void* x, int dtype, int64_t T, int64_t H, int64_t E,
                  const hn_router_params* router, int32_t* topk_idx, float* topk_w, float* logits,
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Expert-parallel exchange (no counterpart in the reference, which runs every
+ * expert on one GPU; its roadmap lists expert parallelism, README.md:179).
+ * Rank r of W owns experts [r*E/W, (r+1)*E/W).  A step is: hn_ep_pack ->
+ * all-to-all of W equal blocks -> hn_ep_unpack -> hn_moe_experts_int4 over the
+ * W*T received rows (top_k slots of local ids, -1 = not here) -> all-to-all of
+ * the W*T output rows back -> hn_ep_combine.  Every block holds T fixed rows,
+ * one per source token (sent at most once per destination rank), so nothing
+ * depends on counts the host would have to read.
+ * ------------------------------------------------------------------------- */
+
+/* Bytes of one exchange row: H activations (2 bytes each), top_k int32 local
+ * expert ids and top_k float32 weights, rounded up to 16 bytes. */
+HN_API size_t hn_ep_row_bytes(int64_t H, int top_k);
+
+/* send [W][T][row]: block d, row t = token t's activations (only when one of
+ * its picks lives on rank d) and its top-k list as rank d's local ids (-1
+ * where the pick lives elsewhere) with the routing weights (0 there).
+ * topk_idx int32 [T, top_k] global expert ids (-1 = unused slot), topk_w
+ * float32 [T, top_k].  x and send 16-byte aligned. */
+HN_API int hn_ep_pack(const void* x, int dtype, int64_t T, int64_t H, int top_k, const int32_t* topk_idx,
+                      const float* topk_w, int64_t E, int world, void* send, void* stream);
+
+/* recv [rows][row] -> x_out [rows, H] (rows without a local pick are left
+ * unwritten), idx_out int32 [rows, top_k], w_out float32 [rows, top_k]. */
+HN_API int hn_ep_unpack(const void* recv, int dtype, int64_t rows, int64_t H, int top_k, void* x_out,
+                        int32_t* idx_out, float* w_out, void* stream);
+
+/* out [T, H] = sum over the ranks d holding a pick of token t (in rank order,
+ * fp32) of back [d][t][H]; back rows of other ranks are never read. */
+HN_API int hn_ep_combine(const void* back, int dtype, int64_t T, int64_t H, int top_k, const int32_t* topk_idx,
+                         int64_t E, int world, void* out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Allocation-free int4_linear.  No counterpart in the reference: its Python

@@ -36,3 +36,17 @@ def test_reference_arm_other_ranks_exit_quietly():
     res = _run({"RANK": "1", "WORLD_SIZE": "2"})
     assert res.returncode == 0, res.stderr[-2000:]
     assert res.stdout.strip() == ""
+
+
+def test_reference_arm_expert_parallel_config():
+    """Under --gpus N > 1 the GPU arm measures config 4 (GLM-4.5-Air layer,
+    32 sequences per GPU), and so does the reference arm."""
+    env = dict(os.environ, RANK="0", WORLD_SIZE="2")
+    res = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--gpus", "2", "--steps", "1",
+                          "--warmup", "3", "--ref-budget", "1"], cwd=REPO, env=env, capture_output=True, text=True,
+                         timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    line = json.loads(res.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
+    assert line["config"]["workload"] == "glm45air_moe_layer_decode_ep" and line["config"]["experts"] == 128
+    assert line["cpu_baseline"]["value"] == line["value"] and "touched experts" in line["cpu_baseline"]["sample"]

@@ -1,10 +1,13 @@
 """Expert-parallel dispatch/combine bookkeeping on CPU ranks (gloo, world sizes 2 and 4; Mixtral and GLM-4.5 routing).
 
 Each rank routes its own tokens with the oracle router, exchanges rows with
-``hydranet_b200.ep.ep_moe_forward`` and runs its share of the experts with a
-test-only local function built from the oracle; the result must equal the
-single-process oracle layer (``model/mixtral.py:282-370`` semantics) on that
-rank's tokens.  No GPU is involved.
+``hydranet_b200.ep.ep_moe_forward`` (one row per token and destination rank,
+the token's picks rewritten as that rank's local ids) and runs its share of
+the experts with a test-only local function built from the oracle; the pack,
+unpack and combine steps use the torch reference of the CUDA kernels
+(``tests/ep_ref.py``).  The result must equal the single-process oracle layer
+(``model/mixtral.py:282-370`` semantics) on that rank's tokens.  No GPU is
+involved.
 """
 
 import os
@@ -18,6 +21,7 @@ import torch.multiprocessing as mp
 
 from hydranet_b200 import synth
 from oracle import int4_ref as R
+from tests.ep_ref import TorchExchange
 
 H, F, E, K = 256, 256, 8, 3
 GLM = dict(E=16, K=8, router="sigmoid")  # GLM-4.5 layout at a small size
@@ -56,18 +60,19 @@ def worker(rank, world, port, T, force_idx, results, n_exp=E, k=K, router="softm
             idx, w, _ = R.softmax_topk_router_ref(x, rw, k, "f32")
         if force_idx is not None:
             idx = force_idx[rank].copy()
-        def local_fn(rows, local_e, weight):
+        def local_fn(rows, ids, weight):
             rr = rows.numpy().astype(np.float32)
             out = np.zeros_like(rr)
             for i in range(rr.shape[0]):
-                if int(local_e[i]) < 0:
-                    continue  # an unused slot of the fixed-size exchange
-                e = first + int(local_e[i])
-                assert first <= e < last
-                out[i] = float(weight[i]) * experts[e](rr[i:i + 1])[0]
+                for j in range(ids.shape[1]):
+                    if int(ids[i, j]) < 0:
+                        continue  # a pick owned by another rank (or an unused row)
+                    e = first + int(ids[i, j])
+                    assert first <= e < last
+                    out[i] += float(weight[i, j]) * experts[e](rr[i:i + 1])[0]
             return torch.from_numpy(out)
-        y = ep_moe_forward(torch.from_numpy(x), torch.from_numpy(idx.astype(np.int64)), torch.from_numpy(w),
-                           n_exp, local_fn)
+        y = ep_moe_forward(torch.from_numpy(x), torch.from_numpy(idx.astype(np.int32)), torch.from_numpy(w),
+                           n_exp, local_fn, exchange=TorchExchange())
         ref = R.moe_combine_ref(x, idx, w, experts)
         err = float(np.abs(y.numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
         results[rank] = err

@@ -236,13 +236,15 @@ def test_driver_smoke_entry(lib):
     __graft_entry__.smoke()
 
 
-@pytest.mark.parametrize("T,k,E", [(37, 2, 6), (100, 1, 4), (5000, 1, 4)])
-def test_given_routing_unused_slots(lib, T, k, E):
-    """Index -1 marks an unused slot (the expert-parallel exchange pads with
-    them): tokens whose slots are all -1 are skipped, -1 next to real picks
-    counts as a weight-0 pick; the other tokens match the oracle.  Sizes cover
-    the gathered and the assignment-ordered token paths and the multi-CTA
-    planner (T*k > 4096)."""
+@pytest.mark.parametrize("T,k,E,sparse", [(37, 2, 6, 0.0), (100, 1, 4, 0.0), (5000, 1, 4, 0.0), (12, 8, 16, 0.8),
+                                          (256, 8, 16, 0.8)])
+def test_given_routing_unused_slots(lib, T, k, E, sparse):
+    """Index -1 marks an unused slot (the expert-parallel exchange rewrites
+    the picks owned by other ranks as -1): tokens whose slots are all -1 are
+    skipped, -1 next to real picks takes no work and adds nothing; the other
+    tokens match the oracle.  Sizes cover both engines, the gathered and the
+    assignment-ordered token paths and the multi-CTA planner (T*k > 4096);
+    ``sparse`` blanks that share of the slots, as at eight ranks with top-8."""
     shape = synth.MoEShape(256, 256, E, k)
     table, packed = host_moe(shape, 70 + T)
     rng = np.random.default_rng(T)
@@ -253,6 +255,10 @@ def test_given_routing_unused_slots(lib, T, k, E):
     if k > 1:
         part = (~skip) & (rng.random(T) < 0.3)
         idx[part, 0] = -1
+    if sparse:
+        blank = rng.random((T, k)) < sparse
+        blank[:, 1] = False  # every token not skipped keeps at least one pick
+        idx[blank] = -1
     x = act(rng.standard_normal((T, 256), dtype=np.float32), "bf16")
     out = moe_experts(x, torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), table)
     keep = ~skip
@@ -262,3 +268,34 @@ def test_given_routing_unused_slots(lib, T, k, E):
     assert rel_l2(to_np32(out)[keep], ref) <= TIGHT
     for ws in _lib.workspaces.all():
         assert _lib.workspace_error(ws) == 0
+
+
+def test_glm_layer_with_shared_expert(lib):
+    """``GLM4MoELayer.forward`` (``model/glm4.py:365-473``): shared_expert(x) +
+    routed(x), the shared expert a dense bf16 MLP of moe_ffn rows
+    (``:341-344``).  Oracle: the routed oracle plus the dense MLP in float32 on
+    the same bf16 weights."""
+    from hydranet_b200.moe import SharedExpertMLP
+    shape = synth.MoEShape(4096, 1408, 128, 8)
+    if "g" not in _FULL:
+        _FULL["g"] = device_moe(shape, 4321)
+    table, packed = _FULL["g"]
+    torch.manual_seed(9)
+    shared = SharedExpertMLP(4096, 1408)
+    for lin in (shared.gate_proj, shared.up_proj, shared.down_proj):
+        torch.nn.init.normal_(lin.weight, std=0.02)
+    shared = shared.cuda().to(torch.bfloat16)
+    r = GLM4SigmoidRouter(hidden_dim=4096, num_experts=128, experts_per_token=8).cuda()
+    layer = MoELayerInt4(r, table, shared_expert=shared)
+    x = torch.randn(2, 16, 4096, generator=torch.Generator("cuda").manual_seed(6), device="cuda").to(torch.bfloat16)
+    with torch.no_grad():
+        out, ro = layer(x, return_routing=True)
+    assert out.shape == x.shape
+    xi = to_np32(x.view(32, 4096))
+    idx = ro.expert_indices.view(32, 8).cpu().numpy()
+    w = to_np32(ro.expert_weights.view(32, 8))
+    routed = R.moe_combine_ref(xi, idx, w, oracle_experts(packed, idx.ravel()))
+    g, u, d = (to_np32(l.weight) for l in (shared.gate_proj, shared.up_proj, shared.down_proj))
+    sh = (R.silu(xi @ g.T) * (xi @ u.T)) @ d.T
+    err = rel_l2(to_np32(out.view(32, 4096)), routed + sh)
+    assert err <= TOL and err <= TIGHT, err
