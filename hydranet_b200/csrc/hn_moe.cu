@@ -36,6 +36,7 @@ constexpr int kChunk = 256;  // bytes per (token, k-group): 16 units of 16 B (12
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 32;
 constexpr int kPlanSmemEntries = 4096;  // routing entries the plan builder copies into shared memory
+constexpr int kPlanRankEntries = 1024;  // up to this many, assignment positions are counted directly
 
 enum { KIND_GATEUP = 0, KIND_DOWN = 1 };
 enum { EPI_COMBINE = 0, EPI_STORE = 1 };
@@ -153,6 +154,7 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   // plan copies of the routing follow scs (see the plan section); the router
   // weight chunk sits at the end of the dynamic shared memory
   __shared__ int s_last;
+  __shared__ int s_wsum[3][8];  // per-warp totals of the plan's scans
   __shared__ int s_idx[kMaxTopK];
   __shared__ float s_w[kMaxTopK];
   __shared__ __align__(8) uint64_t s_wbar;
@@ -422,27 +424,72 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
     if (e >= 0) atomicAdd(&cnt[e], 1);  // -1: a skipped token's slot
   }
   __syncthreads();
-  if (tid == 0) {
-    int o = 0, ns = 0, ns2 = 0;
-    for (int e = 0; e < a.E; ++e) {
-      off[e] = o;
+  // Offsets and segments of every expert by a block-wide exclusive scan over
+  // the experts (thread i owns experts [i*c, (i+1)*c)): each thread cuts its
+  // own experts' segments, in expert order, at the positions the scan gives.
+  {
+    const int c = (a.E + 255) / 256, e0 = tid * c, e1 = min(a.E, e0 + c);
+    int n = 0, ns = 0, ns2 = 0;
+    for (int e = e0; e < e1; ++e) {
       const int m = cnt[e];
-      for (int j = 0; j < m; j += a.seg) a.plan.segs[ns++] = make_int4(e, o + j, min(a.seg, m - j), 0);
+      n += m;
+      ns += (m + a.seg - 1) / a.seg;
+      if (a.plan.seg2) ns2 += (m + a.plan.seg2 - 1) / a.plan.seg2;
+    }
+    int incl[3] = {n, ns, ns2};
+#pragma unroll
+    for (int v = 0; v < 3; ++v)
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl[v], o);
+        if (lane >= o) incl[v] += y;
+      }
+    if (lane == 31)
+      for (int v = 0; v < 3; ++v) s_wsum[v][warp] = incl[v];
+    __syncthreads();
+    int base[3];
+    for (int v = 0; v < 3; ++v) {
+      base[v] = 0;
+      for (int w = 0; w < warp; ++w) base[v] += s_wsum[v][w];
+    }
+    int o = base[0] + incl[0] - n, sg = base[1] + incl[1] - ns, sg2 = base[2] + incl[2] - ns2;
+    for (int e = e0; e < e1; ++e) {
+      const int m = cnt[e];
+      off[e] = o;
+      for (int j = 0; j < m; j += a.seg) a.plan.segs[sg++] = make_int4(e, o + j, min(a.seg, m - j), 0);
       if (a.plan.seg2)
         for (int j = 0; j < m; j += a.plan.seg2)
-          a.plan.segs2[ns2++] = make_int4(e, o + j, min(a.plan.seg2, m - j), 0);
+          a.plan.segs2[sg2++] = make_int4(e, o + j, min(a.plan.seg2, m - j), 0);
       o += m;
       a.plan.counts[e] = m;
     }
-    *a.plan.n_segs = ns;
-    if (a.plan.seg2) *a.plan.n_segs2 = ns2;
-    *a.plan.route_ctr = 0;
-    s_idx[0] = o;  // assignments planned (skipped tokens' slots excluded)
+    if (tid == 255) {
+      *a.plan.n_segs = sg;
+      if (a.plan.seg2) *a.plan.n_segs2 = sg2;
+      *a.plan.route_ctr = 0;
+      s_idx[0] = o;  // assignments planned (skipped tokens' slots excluded)
+    }
   }
   __syncthreads();
   // positions past the planned assignments (left by skipped tokens) name
   // token 0, so a copy over all T*K positions stays in bounds
   for (int p = s_idx[0] + tid; p < TK; p += 256) a.plan.a_tok[p] = 0;
+  if (in_smem && TK <= kPlanRankEntries) {
+    // per-expert assignment order: by token, then by top-k slot -- the rank of
+    // assignment i among its expert's is the count of earlier ones with the
+    // same expert (a token listing an expert twice gets two slots)
+    for (int i = tid; i < TK; i += 256) {
+      const int e = pidx[i];
+      if (e < 0) continue;
+      int r = 0;
+      for (int j = 0; j < i; ++j) r += pidx[j] == e;
+      const int p = off[e] + r;
+      a.plan.pos[i] = p;
+      a.plan.a_tok[p] = i / a.K;
+      a.plan.a_tk[p] = i;
+      a.plan.a_w[p] = pwts[i];
+    }
+    return;
+  }
   // per-expert assignment order: by token, then by top-k slot (ballot over 32
   // tokens at a time); a token listing the same expert twice gets two slots
   for (int e = warp; e < a.E; e += 8) {
@@ -588,8 +635,8 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* x, int64
 // Router logits of a small batch whose router matrix spans several of the
 // prep kernel's 64 KB chunks (GLM-4.5: 128 experts x 4096 fp32 = 2 MB): the
 // per-token prep CTA would stream the whole matrix chunk by chunk, one round
-// trip each.  Here CTA b stages kRgvE expert rows in shared memory (as fp32)
-// and each warp dots them with one token's activations at a time; a lane
+// trip each.  Here CTA (b, c) stages kRgvE expert rows in shared memory (as
+// fp32) and each of its warps dots them with one of tokens 8c..8c+7; a lane
 // sums h = 8*lane + 256*i in order and the warp reduces by xor-shuffle, so
 // the result does not depend on the launch shape.  logits[t, e] is fp32 (the
 // prep kernel applies the Mixtral gate's model-dtype rounding).
@@ -652,44 +699,57 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const void* x, int64_t
   __syncthreads();
   const typename Tr::T* xp = reinterpret_cast<const typename Tr::T*>(x);
   const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 8 == 0);
-  for (int t = warp; t < T; t += 8) {
-    float acc[kRgvE];
+  // CTA row blockIdx.y takes 8 tokens, one per warp; a lane's 16-byte loads
+  // of its token are issued kRgvBatch at a time before any is used
+  const int t = blockIdx.y * 8 + warp;
+  if (t >= T) return;
+  float acc[kRgvE];
 #pragma unroll
-    for (int e = 0; e < kRgvE; ++e) acc[e] = 0.f;
-    const typename Tr::T* xr = xp + (int64_t)t * ldx;
-    for (int h = lane * 8; h < H; h += 256) {
-      float xv[8];
+  for (int e = 0; e < kRgvE; ++e) acc[e] = 0.f;
+  const typename Tr::T* xr = xp + (int64_t)t * ldx;
+  constexpr int kRgvBatch = 8;
+  for (int h0 = lane * 8; h0 < H; h0 += 256 * kRgvBatch) {
+    float xv[kRgvBatch][8];
+#pragma unroll
+    for (int b = 0; b < kRgvBatch; ++b) {
+      const int h = h0 + b * 256;
+      if (h >= H) continue;
       if (vec) {
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(xr + h));
         const typename Tr::T2* h2 = reinterpret_cast<const typename Tr::T2*>(&v);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          xv[2 * u] = Tr::to_f(h2[u].x);
-          xv[2 * u + 1] = Tr::to_f(h2[u].y);
+          xv[b][2 * u] = Tr::to_f(h2[u].x);
+          xv[b][2 * u + 1] = Tr::to_f(h2[u].y);
         }
       } else {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) xv[u] = Tr::to_f(xr[h + u]);
+        for (int u = 0; u < 8; ++u) xv[b][u] = Tr::to_f(xr[h + u]);
       }
+    }
+#pragma unroll
+    for (int b = 0; b < kRgvBatch; ++b) {
+      const int h = h0 + b * 256;
+      if (h >= H) continue;
 #pragma unroll
       for (int e = 0; e < kRgvE; ++e) {
         const float4 w0 = *reinterpret_cast<const float4*>(wsm + e * H + h);
         const float4 w1 = *reinterpret_cast<const float4*>(wsm + e * H + h + 4);
-        acc[e] = fmaf(xv[0], w0.x, acc[e]);
-        acc[e] = fmaf(xv[1], w0.y, acc[e]);
-        acc[e] = fmaf(xv[2], w0.z, acc[e]);
-        acc[e] = fmaf(xv[3], w0.w, acc[e]);
-        acc[e] = fmaf(xv[4], w1.x, acc[e]);
-        acc[e] = fmaf(xv[5], w1.y, acc[e]);
-        acc[e] = fmaf(xv[6], w1.z, acc[e]);
-        acc[e] = fmaf(xv[7], w1.w, acc[e]);
+        acc[e] = fmaf(xv[b][0], w0.x, acc[e]);
+        acc[e] = fmaf(xv[b][1], w0.y, acc[e]);
+        acc[e] = fmaf(xv[b][2], w0.z, acc[e]);
+        acc[e] = fmaf(xv[b][3], w0.w, acc[e]);
+        acc[e] = fmaf(xv[b][4], w1.x, acc[e]);
+        acc[e] = fmaf(xv[b][5], w1.y, acc[e]);
+        acc[e] = fmaf(xv[b][6], w1.z, acc[e]);
+        acc[e] = fmaf(xv[b][7], w1.w, acc[e]);
       }
     }
-#pragma unroll
-    for (int e = 0; e < kRgvE; ++e)
-      for (int o = 16; o; o >>= 1) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
-    if (lane < ne) out[(int64_t)t * E + e0 + lane] = lane == 0 ? acc[0] : acc[kRgvE > 1 ? 1 : 0];
   }
+#pragma unroll
+  for (int e = 0; e < kRgvE; ++e)
+    for (int o = 16; o; o >>= 1) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+  if (lane < ne) out[(int64_t)t * E + e0 + lane] = lane == 0 ? acc[0] : acc[kRgvE > 1 ? 1 : 0];
 }
 
 // ---------------------------------------------------------------------------
@@ -1899,8 +1959,8 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
     HN_REQUIRE(gsm <= 227 * 1024, "router: hidden size too large for the router GEMV");
     if (gsm > 48 * 1024)
       HN_CUDA(cudaFuncSetAttribute(router_gemv_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
-    router_gemv_kernel<Tr><<<(unsigned)((ra.E + kRgvE - 1) / kRgvE), 256, gsm, s>>>(ra.x, ra.ldx, ra.T, ra.H, ra.E,
-                                                                                  ra.rw, ra.rw_dtype, ra.plan.rlog);
+    const dim3 grid((unsigned)((ra.E + kRgvE - 1) / kRgvE), (unsigned)((ra.T + 7) / 8));
+    router_gemv_kernel<Tr><<<grid, 256, gsm, s>>>(ra.x, ra.ldx, ra.T, ra.H, ra.E, ra.rw, ra.rw_dtype, ra.plan.rlog);
     HN_CUDA(cudaGetLastError());
     r.pre_logits = ra.plan.rlog;
   }
