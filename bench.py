@@ -261,6 +261,121 @@ class OracleLayer:
         return self.R.moe_combine_ref(self.x, idx, w, self.experts)
 
 
+REF_INSTALL = REPO / "baseline" / "_ref"
+
+
+def import_reference():
+    """The reference installed unmodified in baseline/_ref, importable as the
+    package ``hydranet`` (its modules use package-relative imports); None when
+    it is not installed."""
+    if not (REF_INSTALL / "model" / "mixtral.py").exists():
+        return None
+    import tempfile
+    root = tempfile.mkdtemp(prefix="hn_ref_")
+    os.symlink(REF_INSTALL, os.path.join(root, "hydranet"))
+    sys.path.insert(0, root)
+    import importlib
+    return importlib.import_module("hydranet")
+
+
+class ReferenceCpuLayer:
+    """The reference's own ``MixtralMoELayer`` (``model/mixtral.py:259-370``) on
+    the host cores in its dequant mode: float32 weights registered with its
+    ``ExpertCacheManager`` on the CPU, the forward it runs without a GPU
+    (router, per-expert ``F.linear`` SwiGLU, ``index_add_``).  Weights are the
+    dequantised random nibbles of ``OracleLayer`` (the timing depends on the
+    shapes only); built outside any timing."""
+
+    def __init__(self, T: int):
+        import torch
+        import importlib
+        import_reference()
+        cfg = importlib.import_module("hydranet.config")
+        from hydranet.cache.expert_cache import ExpertCacheManager
+        from hydranet.model.mixtral import MixtralMoELayer
+        torch.set_num_threads(cpu_threads())
+        mc = cfg.MixtralConfig()
+        mc.num_layers, mc.num_experts, mc.hidden_dim, mc.intermediate_dim = 1, E, H, F
+        cc = cfg.ExpertCacheConfig(pinned_slots=0, hot_slots=E // 2, probation_slots=E - E // 2,
+                                   enable_affinity_bonus=False, enable_dynamic_slots=False,
+                                   max_slots_per_layer=E + 1, enable_prefetch=False)
+        self.cm = ExpertCacheManager(model_config=mc, cache_config=cc, device=torch.device("cpu"),
+                                     dtype=torch.float32)
+        base = OracleLayer(T)
+        for e, ex in base.experts.items():
+            self.cm.register_expert(0, e, {"gate_proj": torch.from_numpy(ex.gate), "up_proj": torch.from_numpy(ex.up),
+                                           "down_proj": torch.from_numpy(ex.down)})
+        base.experts = None
+        self.layer = MixtralMoELayer(mc, cc, 0, self.cm)
+        with torch.no_grad():
+            self.layer.router.gate.weight.copy_(torch.from_numpy(base.rw))
+        self.x = torch.from_numpy(base.x).view(1, T, H)
+        self.T = T
+
+    def step(self):
+        import torch
+        with torch.no_grad():
+            return self.layer(self.x, top_k=2)
+
+    def close(self):
+        self.cm.shutdown()
+
+
+def cpu_reference_time(T: int, budget_s: float = 15.0, max_steps: int = 400):
+    """tok/s of the reference's own CPU layer (``ReferenceCpuLayer``) when the
+    reference is installed, else of the oracle port; returns (tok/s, steps,
+    seconds, kind)."""
+    try:
+        layer, kind = ReferenceCpuLayer(T), "reference"
+    except Exception:  # noqa: BLE001 - not installed or not importable here: the restatement
+        layer, kind = OracleLayer(T), "port"
+    layer.step()  # warm-up (the cache manager fills its slots)
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        layer.step()
+        steps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or steps >= max_steps:
+            break
+    if hasattr(layer, "close"):
+        layer.close()
+    return T * steps / el, steps, el, kind
+
+
+def reference_triton_bar(dev) -> dict:
+    """The reference's own Triton INT4 expert MLP (``expert_mlp_int4_fused``,
+    ``kernels/int4_gemm.py:211-254``) on this B200 with float16 activations,
+    its native dtype: device time per call on one Mixtral expert (its models
+    call it once per touched expert) at 1 and 16 tokens, and the config-2
+    layer times that implies (T = 1: two calls of 1 token; T = 64: eight calls
+    of 16 tokens, the mean tokens per expert)."""
+    try:
+        import torch
+        if import_reference() is None:
+            return {"unavailable": "the reference is not installed in baseline/_ref"}
+        from hydranet.kernels.int4_gemm import expert_mlp_int4_fused
+        from hydranet_b200 import synth
+        slot = synth.device_experts(11, synth.MoEShape(H, F, 1, 1), dev)[0]
+        t = slot.tensors()
+        res = {"kernel": "reference expert_mlp_int4_fused (Triton 3.6), float16", "us_per_call": {}}
+        for m in (1, 16):
+            x = torch.randn(m, H, device=dev, dtype=torch.float16)
+            for _ in range(3):
+                expert_mlp_int4_fused(x, *t, group_size=128)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                expert_mlp_int4_fused(x, *t, group_size=128)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            res["us_per_call"][str(m)] = e0.elapsed_time(e1) / 20 * 1e3
+        res["layer_ms_est"] = {"1": 2 * res["us_per_call"]["1"] / 1e3, "64": 8 * res["us_per_call"]["16"] / 1e3}
+        return res
+    except Exception as exc:  # noqa: BLE001 - the bar is context; report why it is missing
+        return {"unavailable": repr(exc)[:300]}
+
+
 def cpu_oracle_time(T: int, budget_s: float = 15.0, max_steps: int = 400):
     """tok/s of the oracle MoE layer on the host cores over a bounded sample."""
     layer = OracleLayer(T)
@@ -358,7 +473,12 @@ def run_reference(args):
         print(json.dumps(line), flush=True)
         return
     T = args.tokens
-    layer = OracleLayer(T)
+    try:
+        layer, kind = ReferenceCpuLayer(T), "reference"
+        what = "the reference's own MixtralMoELayer.forward (dequant mode, float32 weights, torch CPU)"
+    except Exception:  # noqa: BLE001 - the reference is not installed: its restatement
+        layer, kind = OracleLayer(T), "port"
+        what = "oracle layer steps (numpy float32 dequant-then-matmul, weights dequantised before timing)"
     for _ in range(args.warmup):
         layer.step()
     t0 = time.perf_counter()
@@ -366,14 +486,15 @@ def run_reference(args):
         layer.step()
     el = time.perf_counter() - t0
     v = T * args.steps / el
+    if hasattr(layer, "close"):
+        layer.close()
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "tokens": T, "hidden": H, "ffn": F, "experts": E, "top_k": TOPK,
                        "group_size": 128},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
-                             "sample": f"{args.steps} oracle layer steps at T={T} (numpy float32 "
-                                       f"dequant-then-matmul, weights dequantised before timing)"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": kind,
+                             "sample": f"{args.steps} steps at T={T}: {what}"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -775,10 +896,12 @@ def main():
 
     cpu = None
     if not args.no_cpu_baseline:
-        v, n, el = cpu_oracle_time(T, budget_s=args.ref_budget)
-        cpu = {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
-               "sample": f"{n} oracle layer steps at T={T} in {el:.1f}s (numpy float32 dequant-then-matmul, "
-                         f"dequantisation done before timing)"}
+        v, n, el, kind = cpu_reference_time(T, budget_s=args.ref_budget)
+        what = ("the reference's own MixtralMoELayer.forward in dequant mode (float32 weights, torch CPU)"
+                if kind == "reference" else "oracle layer steps (numpy float32 dequant-then-matmul)")
+        cpu = {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": kind,
+               "sample": f"{n} steps at T={T} in {el:.1f}s: {what}, weights dequantised before timing"}
+    triton_bar = reference_triton_bar(dev)
 
     prefill = None if args.no_prefill else prefill_measure(args, dev)
     glm = glm_c4(args, dev, 1, 0, barrier, max_over_ranks)
@@ -807,6 +930,7 @@ def main():
         "cpu_baseline": cpu,
         "prefill": prefill,
         "glm_c4": glm,
+        "reference_gpu_bar": triton_bar,
         "sweep": {str(t): {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items() if k != "clocks"}
                   for t, r in results.items()},
     }
