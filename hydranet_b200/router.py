@@ -52,16 +52,32 @@ class TopKRouter(nn.Module):
         self.enable_affinity_bonus = _cfg(cache_config, "enable_affinity_bonus", False)
         self.register_buffer("usage_counts", torch.zeros(self.num_experts, dtype=torch.long), persistent=False)
         self._is_cached_fn: Optional[Callable[[int], bool]] = None
+        self._bonus_buf: Optional[torch.Tensor] = None
 
     def set_cache_checker(self, fn: Callable[[int], bool]):
         self._is_cached_fn = fn
 
     def bonus_vector(self, device) -> Optional[torch.Tensor]:
-        """Per-expert affinity bonus (``model/router.py:160-168``), or None when disabled."""
+        """Per-expert affinity bonus (``model/router.py:160-168``), or None when disabled.
+
+        The bonus lives in one persistent device buffer, refreshed in place
+        from the cache checker on every call outside CUDA-graph capture, so a
+        captured layer reads the current cache state when it replays (refresh
+        it with ``refresh_bonus`` before a replay)."""
         if not self.enable_affinity_bonus or self._is_cached_fn is None:
             return None
+        if self._bonus_buf is None or self._bonus_buf.device != torch.device(device):
+            self._bonus_buf = torch.zeros(self.num_experts, dtype=torch.float32, device=device)
+        if not torch.cuda.is_current_stream_capturing():
+            self.refresh_bonus()
+        return self._bonus_buf
+
+    def refresh_bonus(self):
+        """Write the current per-expert bonus into the persistent buffer (host values, one small copy)."""
+        if self._bonus_buf is None or self._is_cached_fn is None:
+            return
         vals = [self.affinity_bonus if self._is_cached_fn(e) else 0.0 for e in range(self.num_experts)]
-        return torch.tensor(vals, dtype=torch.float32, device=device)
+        self._bonus_buf.copy_(torch.tensor(vals, dtype=torch.float32))
 
     def params(self, top_k: int, bonus: Optional[torch.Tensor]) -> _lib.RouterParams:
         return ops.router_params(_lib.HN_ROUTER_SOFTMAX_TOPK, top_k, self.gate.weight, logits_in_act_dtype=True,
