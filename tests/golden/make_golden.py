@@ -160,6 +160,15 @@ def gatherer_cases(torch, GroupByExpertGatherer):
     return cases
 
 
+def scheduler_trace(torch):
+    """The scripted scheduler session of ``scheduler_script.py`` run on the
+    reference's ``scheduler/continuous_batch.py``."""
+    sys.path.insert(0, str(HERE))
+    import scheduler_script
+    from hydranet.scheduler import continuous_batch
+    return {"lines": np.array(scheduler_script.run(continuous_batch, torch))}
+
+
 def store_case(ref: Path):
     """A packed store written by the reference's own test helper
     (``tests/test_int4_loader.py:28-119``: 2 layers x 2 experts, H 256, F 512,
@@ -335,7 +344,8 @@ def main():
     from hydranet.scheduler.continuous_batch import GroupByExpertGatherer
     light = {"int4linear_quant": lambda: int4linear_cases(torch, Int4Linear),
              "gatherer": lambda: gatherer_cases(torch, GroupByExpertGatherer),
-             "reference_store": lambda: store_case(args.reference.resolve())}
+             "reference_store": lambda: store_case(args.reference.resolve()),
+             "scheduler_trace": lambda: scheduler_trace(torch)}
     for stem, make in light.items():
         if args.only in (None, stem):
             np.savez_compressed(HERE / f"{stem}.npz", **make())
