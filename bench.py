@@ -142,6 +142,69 @@ def prefill_measure(args, dev):
             "phases": phase, "clocks": clk.summary(), "cpu_baseline": cpu}
 
 
+def prefill_ep(args, dev, world, rank, barrier, max_over_ranks):
+    """Config 5 expert-parallel: 8192 tokens per GPU (weak scaling), the 128
+    experts split over the ranks, micro-batches of 8192 / world tokens per
+    rank (``ExpertParallelMoE(chunk_tokens=...)``: every grouped call sees
+    8192 rows, the exchanges of one micro-batch queued beside the experts of
+    the next).  Eager launches; device time per layer step with CUDA events,
+    max over ranks; FLOPs per rank 2 * T * k * 3 * H * F (on average a rank
+    runs T * k assignments) against the bf16 dense peak.  Parity: rank 0's
+    output against one GPU holding all experts."""
+    import torch
+    from hydranet_b200 import synth
+    from hydranet_b200.ep import ExpertParallelMoE
+    from hydranet_b200.moe import MoELayerInt4
+    from hydranet_b200.packing import ExpertTable
+    from hydranet_b200.router import GLM4SigmoidRouter
+
+    per = P_E // world
+    chunk = P_T // world
+    slots = synth.device_experts(4321, synth.MoEShape(P_H, P_F, P_E, P_K), dev)
+    r = GLM4SigmoidRouter(hidden_dim=P_H, num_experts=P_E, experts_per_token=P_K).to(dev)
+    r.set_correction_bias(torch.from_numpy(synth.host_correction_bias(3, P_E)).to(dev))
+    layer = ExpertParallelMoE(r, ExpertTable(slots[rank * per:(rank + 1) * per]), P_E, chunk_tokens=chunk).eval()
+    full = ExpertTable(slots) if rank == 0 else None
+    del slots
+    x = torch.randn(P_T, P_H, generator=torch.Generator(dev).manual_seed(5 + rank), device=dev).to(torch.bfloat16)
+    steps = max(3, min(args.steps, 10))
+    with torch.no_grad():
+        y = layer(x)
+        parity = None
+        if rank == 0:
+            ref = MoELayerInt4(r, full).eval()(x)
+            parity = float((y.float() - ref.float()).norm() / ref.float().norm())
+            del ref
+        full = None
+        del y
+        for _ in range(args.warmup):
+            layer(x)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index or 0) as clk:
+            ev0.record()
+            for _ in range(steps):
+                layer(x)
+            ev1.record()
+            torch.cuda.synchronize(dev)
+        ms = max_over_ranks(ev0.elapsed_time(ev1) / steps)
+        barrier()
+    flops = 2.0 * P_T * P_K * 3 * P_H * P_F
+    _, tc_peak, peak_kind = peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    del layer, x
+    torch.cuda.empty_cache()
+    return {"workload": "glm45air_moe_layer_prefill_ep", "n_gpus": world, "tokens_per_gpu": P_T,
+            "experts_per_gpu": per, "micro_batch_tokens": chunk, "hidden": P_H, "ffn": P_F, "experts": P_E,
+            "top_k": P_K, "steps": steps, "ms_per_step": ms, "tok_s": world * P_T / (ms * 1e-3),
+            "parity_rel_l2": parity,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": tf / tc_peak, "peak_kind": peak_kind, "flops_per_gpu_step": flops,
+                         "kernel": "whole layer step per rank (route, micro-batched exchange, experts, combine)"},
+            "clocks": clk.summary()}
+
+
 # DRAM bytes (read + write) of one gate/up engine launch, from the ncu capture
 # summarised in profiles/ (per launch, same workload); None where not captured.
 GATEUP_TRAFFIC = {64: 493860096}
@@ -499,6 +562,77 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+C3_LAYERS, C3_SLOTS, C3_BLOBS = 32, 126, 16
+
+
+def c3_measure(args, dev) -> dict:
+    """Config 3's MoE path: 32 Mixtral-shape MoE layers decoding one token at a
+    time through a 126-slot cache (``SlotCache``), router logits skewed per layer by a
+    Zipf(s = 1.1) expert bias (log-weights -1.1 ln(rank) over a seeded
+    permutation; a harness addition, as in the config).  Experts come from 16
+    distinct pinned host blobs shared round-robin by the 256 (layer, expert)
+    pairs: only the bytes moved matter to the cache.  Attention and the dense
+    parts of the model are out of scope, so tok/s is the MoE path alone
+    (routing, one host read per layer, H2D of misses, experts)."""
+    import torch
+    from hydranet_b200 import ops, synth, _lib
+    from hydranet_b200.router import TopKRouter
+    from hydranet_b200.slot_cache import ExpertSource, SlotCache, SlotCachedMoELayer
+
+    blobs = [s.blob.cpu().pin_memory() for s in synth.device_experts(900, synth.MoEShape(H, F, C3_BLOBS, TOPK), dev)]
+    source = ExpertSource(lambda layer, expert: blobs[(layer * E + expert) % C3_BLOBS])
+    cache = SlotCache(H, F, C3_LAYERS, E, C3_SLOTS, source, device=dev)
+    rng = np.random.default_rng(11)
+
+    class ZipfLayer(SlotCachedMoELayer):
+        def route(self, x):
+            p = ops.router_params(_lib.HN_ROUTER_SOFTMAX_TOPK, TOPK, self.router.gate.weight, logits_in_act_dtype=True,
+                                  affinity_bonus=self.zipf, entropy_threshold=-1.0)  # always added to the logits
+            idx, w, _ = ops.moe_route(x, p, E, keep_refs=(self.zipf,), want_logits=False)
+            return idx, w
+
+    layers = []
+    for li in range(C3_LAYERS):
+        r = TopKRouter(hidden_dim=H, num_experts=E, experts_per_token=TOPK).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            r.gate.weight.copy_(torch.randn(E, H, generator=torch.Generator(dev).manual_seed(300 + li), device=dev)
+                                * 0.02)
+        layer = ZipfLayer(r, cache, li)
+        ranks = rng.permutation(E) + 1
+        layer.zipf = torch.tensor(-1.1 * np.log(ranks), dtype=torch.float32, device=dev)
+        layers.append(layer)
+    gen = torch.Generator(dev).manual_seed(1)
+
+    def through(x):
+        for layer in layers:
+            x = layer(x)
+            # keep the synthetic stream at the N(0,1) scale (attention and norms are out of scope)
+            x = x / x.float().norm(dim=-1, keepdim=True).clamp_min(1e-3).to(x.dtype) * (H ** 0.5)
+        return x
+
+    n_prompt, n_tok = 512, 128
+    with torch.no_grad():
+        through(torch.randn(n_prompt, H, generator=gen, device=dev).to(torch.bfloat16))  # the prompt fills the cache
+        x = torch.randn(1, H, generator=gen, device=dev).to(torch.bfloat16)
+        torch.cuda.synchronize(dev)
+        s0 = (cache.stats.hits, cache.stats.misses, cache.stats.h2d_bytes)
+        t0 = time.perf_counter()
+        for _ in range(n_tok):
+            x = through(x)
+        torch.cuda.synchronize(dev)
+        el = time.perf_counter() - t0
+    hits, misses, h2d = (cache.stats.hits - s0[0], cache.stats.misses - s0[1], cache.stats.h2d_bytes - s0[2])
+    res = {"workload": "mixtral8x7b_moe_path_decode_126_slots", "layers": C3_LAYERS, "slots": C3_SLOTS,
+           "experts_total": C3_LAYERS * E, "prompt_tokens": n_prompt, "tokens": n_tok, "batch": 1,
+           "router_skew": "Zipf(s=1.1) per-expert logit bias per layer", "tok_s": n_tok / el,
+           "ms_per_token": 1e3 * el / n_tok, "hit_rate": hits / max(hits + misses, 1),
+           "misses_per_token": misses / n_tok, "h2d_gbs": h2d / el / 1e9,
+           "timing": "host wall clock around the 128 decode tokens (each layer reads its routing back to the host)"}
+    del layers, cache, blobs
+    torch.cuda.empty_cache()
+    return res
+
+
 def glm_cpu_time(budget_s: float = 10.0, n_exp: int = 16, tok_per_exp: int = 2):
     """Host-core time of one config-4 layer step (32 tokens, sigmoid top-8 over
     128 experts) by the oracle's dequant-then-matmul path, from a bounded
@@ -719,7 +853,13 @@ def main():
                     help="comma-separated token batches to time (default 1,8,32,64)")
     ap.add_argument("--layers", type=int, default=N_LAYERS, help="distinct layers rotated per step")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-5 prefill measurement")
+    ap.add_argument("--no-c3", action="store_true", help="skip the config-3 MoE-path (slot cache) measurement")
+    ap.add_argument("--quick", action="store_true",
+                    help="headline sweep only: no CPU baseline, reference GPU bar, prefill, GLM or config-3 "
+                         "(for profiler captures of the decode kernels)")
     args = ap.parse_args()
+    if args.quick:
+        args.no_cpu_baseline = args.no_prefill = args.no_c3 = True
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
@@ -756,6 +896,7 @@ def main():
     if world > 1:
         # expert-parallel runs measure config 4 (GLM-4.5-Air layer, 32 sequences per GPU)
         g = glm_c4(args, dev, world, rank, barrier, max_over_ranks)
+        pf = None if args.no_prefill else prefill_ep(args, dev, world, rank, barrier, max_over_ranks)
         if rank == 0:
             line = {
                 "metric": METRIC, "value": g["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -770,7 +911,7 @@ def main():
                 "roofline": {**g["roofline"], "traffic": None},
                 "e2e": g["e2e"], "gpu_launches": 8 * args.steps, "clocks": g["clocks"],
                 "parity_rel_l2": g["parity_rel_l2"], "index_match": g["index_match"], "glm_c4": g,
-                "cpu_baseline": None,
+                "prefill_ep": pf, "cpu_baseline": None,
             }
             print(json.dumps(line), flush=True)
         dist.destroy_process_group()
@@ -901,11 +1042,12 @@ def main():
                 if kind == "reference" else "oracle layer steps (numpy float32 dequant-then-matmul)")
         cpu = {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": kind,
                "sample": f"{n} steps at T={T} in {el:.1f}s: {what}, weights dequantised before timing"}
-    triton_bar = reference_triton_bar(dev)
+    triton_bar = None if args.quick else reference_triton_bar(dev)
 
     prefill = None if args.no_prefill else prefill_measure(args, dev)
-    glm = glm_c4(args, dev, 1, 0, barrier, max_over_ranks)
-    if not args.no_cpu_baseline:
+    glm = None if args.quick else glm_c4(args, dev, 1, 0, barrier, max_over_ranks)
+    c3 = None if args.no_c3 else c3_measure(args, dev)
+    if glm is not None and not args.no_cpu_baseline:
         gv, gms, gsample = glm_cpu_time()
         glm["cpu_baseline"] = {"value": gv, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
                                "sample": gsample, "ms_per_step": gms}
@@ -930,6 +1072,7 @@ def main():
         "cpu_baseline": cpu,
         "prefill": prefill,
         "glm_c4": glm,
+        "c3_moe_path": c3,
         "reference_gpu_bar": triton_bar,
         "sweep": {str(t): {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items() if k != "clocks"}
                   for t, r in results.items()},

@@ -58,6 +58,7 @@ struct Plan {
   int* idx;      // [T*K] top-k expert ids
   float* wts;    // [T*K] top-k weights (rounded to the activation dtype)
   int* nval;     // [T] slots of each token that hold an expert (caller routing may leave slots -1)
+  int* n_assign; // [1] assignments planned (T*K less the -1 slots)
   uint8_t* xp;   // [T][K_in/128][kChunk]    staged activations (token-major)
   uint8_t* hp;   // [T*K][F/128][kChunk]     staged SiLU(gate)*up (assignment-major)
   uint8_t* xs;   // [T*K][K_in/128][kChunk]  staged activations in assignment order (large routings), or NULL
@@ -466,6 +467,7 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
       *a.plan.n_segs = sg;
       if (a.plan.seg2) *a.plan.n_segs2 = sg2;
       *a.plan.route_ctr = 0;
+      *a.plan.n_assign = o;
       s_idx[0] = o;  // assignments planned (skipped tokens' slots excluded)
     }
   }
@@ -769,10 +771,12 @@ struct PlanArgs {
 // staged row of token a_tok[p], so the engine reads each segment as
 // consecutive rows (TMA boxes) instead of gathering token by token.  One
 // warp per row; 8 rows per block.
-__global__ void __launch_bounds__(256) stage_rows_kernel(const int* a_tok, int n_rows, const uint8_t* xp,
-                                                         uint8_t* xs, int64_t row_bytes) {
+// Rows past the planned assignments (the -1 slots of a caller routing) are
+// not copied: no segment covers them.
+__global__ void __launch_bounds__(256) stage_rows_kernel(const int* a_tok, const int* n_assign, int n_rows,
+                                                         const uint8_t* xp, uint8_t* xs, int64_t row_bytes) {
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (r >= n_rows) return;
+  if (r >= n_rows || r >= __ldcg(n_assign)) return;
   const int u = (int)(row_bytes / 16);
   const uint4* src = reinterpret_cast<const uint4*>(xp + (int64_t)a_tok[r] * row_bytes);
   uint4* dst = reinterpret_cast<uint4*>(xs + (int64_t)r * row_bytes);
@@ -811,15 +815,17 @@ __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
     if (e == a.E - 1) {
       *a.plan.n_segs = ns;
       if (s2) *a.plan.n_segs2 = ns2;
-      // positions past the planned assignments (skipped tokens' slots) name
-      // token 0, so a copy over all T*K positions stays in bounds
-      for (int64_t q = o + m; q < TK; ++q) a.plan.a_tok[q] = 0;
+      *a.plan.n_assign = o + m;
     }
   }
   // this expert's assignments in (token, slot) order: coalesced rounds of
   // 256 routing entries, a ballot per warp and a prefix over the 8 warps
   __shared__ int s_wcnt[8];
   __syncthreads();
+  if (e == a.E - 1)
+    // positions past the planned assignments (skipped tokens' slots) name
+    // token 0, so a copy over all T*K positions stays in bounds
+    for (int64_t q = s_base[0] + cnt[e] + tid; q < TK; q += 256) a.plan.a_tok[q] = 0;
   const int lane = tid & 31, wid = tid >> 5;
   int base = s_base[0];
   for (int64_t r0 = 0; r0 < TK; r0 += 256) {
@@ -1811,7 +1817,7 @@ static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
 // call, because another shape's data section may have covered them.
 struct Layout {
   size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
-  size_t counts, n_segs, segs, n_segs2, segs2, a_tok, a_tk, a_w, pos, idx, wts, nval, xp, hp, xs, part1, part2, R,
+  size_t counts, n_segs, segs, n_segs2, segs2, a_tok, a_tk, a_w, pos, idx, wts, nval, n_assign, xp, hp, xs, part1, part2, R,
       rlog, data;  // back (relative)
   bool has_rlog, has_xs;
   int seg2;          // second segment cut for the down phase (0: none)
@@ -1860,6 +1866,7 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.idx = take(4 * TK);
   l.wts = take(4 * TK);
   l.nval = take(4 * T);
+  l.n_assign = take(4);
   l.xp = take((size_t)(Kin / 128) * T * kChunk);
   l.hp = take(F ? (size_t)(F / 128) * TK * kChunk : 0);
   // routed gate/up tokens staged in assignment order, read by TMA instead of
@@ -1906,6 +1913,7 @@ static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
   p.idx = reinterpret_cast<int*>(d + l.idx);
   p.wts = reinterpret_cast<float*>(d + l.wts);
   p.nval = reinterpret_cast<int*>(d + l.nval);
+  p.n_assign = reinterpret_cast<int*>(d + l.n_assign);
   p.xp = d + l.xp;
   p.hp = d + l.hp;
   p.xs = l.has_xs ? d + l.xs : nullptr;
@@ -1973,7 +1981,8 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
     HN_CUDA(cudaGetLastError());
   }
   if (ra.plan.xs) {
-    stage_rows_kernel<<<(unsigned)((TK + 7) / 8), 256, 0, s>>>(ra.plan.a_tok, (int)TK, ra.plan.xp, ra.plan.xs,
+    stage_rows_kernel<<<(unsigned)((TK + 7) / 8), 256, 0, s>>>(ra.plan.a_tok, ra.plan.n_assign, (int)TK,
+                                                                ra.plan.xp, ra.plan.xs,
                                                                 (int64_t)(ra.H / 128) * kChunk);
     HN_CUDA(cudaGetLastError());
   }

@@ -25,6 +25,13 @@ parallelism on its roadmap (``README.md:179``).  Per step each rank sends and
 receives W*T rows of H*2 + 8k bytes: at GLM-4.5 decode (T = 32, k = 8, W = 8)
 that is 2 MB each way, against 16 MB with one row per (token, slot).
 
+For prefill-size batches ``ep_moe_forward_chunked`` runs the same steps on
+micro-batches of the rank's tokens, so each grouped call sees W*chunk rows
+(the size of a one-GPU call) and the exchanges of one micro-batch are queued
+beside the experts of the next: NCCL works on its own stream, the dispatch
+of micro-batch i+1 is issued before the experts of micro-batch i and the
+return of micro-batch i before the experts of micro-batch i+1.
+
 ``local_fn`` computes step 3 and ``exchange`` steps 1, 3 and 5; both default
 to the CUDA kernels.  Tests on CPU ranks (gloo) pass reference
 implementations to check the exchange bookkeeping without a GPU.
@@ -109,6 +116,42 @@ def ep_moe_forward(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_expe
     return ex.combine(back.view(world, T, H), idx, num_experts, world)
 
 
+def ep_moe_forward_chunked(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_experts: int,
+                           local_fn: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor],
+                           chunk: int, group=None, exchange=None) -> torch.Tensor:
+    """``ep_moe_forward`` over micro-batches of ``chunk`` tokens with the
+    all-to-alls issued asynchronously (every rank must pass the same T and
+    chunk: the ranks take the same collective steps in the same order)."""
+    if chunk <= 0:
+        raise ValueError("chunk must be positive")
+    ex = exchange if exchange is not None else CudaExchange()
+    world = dist.get_world_size(group)
+    T, H = x.shape
+    k = idx.shape[1]
+    out = torch.empty_like(x)
+
+    def dispatch(s):
+        e = min(s + chunk, T)
+        send = ex.pack(x[s:e], idx[s:e], w[s:e], num_experts, world)
+        recv = torch.empty_like(send)
+        return s, e, send, recv, dist.all_to_all_single(recv, send, group=group, async_op=True)
+
+    pending = dispatch(0) if T else None
+    returns = []
+    while pending is not None:
+        s, e, send, recv, work = pending
+        work.wait()  # the current stream waits for the delivered rows
+        pending = dispatch(e) if e < T else None
+        rows, ids, wts = ex.unpack(recv, H, k, x.dtype)
+        y = local_fn(rows, ids, wts).contiguous()
+        back = torch.empty_like(y)
+        returns.append((s, e, y, back, dist.all_to_all_single(back, y, group=group, async_op=True)))
+    for s, e, y, back, work in returns:
+        work.wait()
+        out[s:e] = ex.combine(back.view(world, e - s, H), idx[s:e], num_experts, world)
+    return out
+
+
 def cuda_local_fn(table):
     """Step 3 on the GPU: the grouped kernel over the received rows with their
     top-k local ids and weights (-1 slots take no work; all -1 rows are
@@ -127,12 +170,14 @@ class ExpertParallelMoE(torch.nn.Module):
     ``router`` is the full router (replicated on every rank: a ``TopKRouter``
     or ``GLM4SigmoidRouter``); ``local_table`` is the ``ExpertTable`` of this
     rank's experts, in global order; an optional ``shared_expert`` (GLM-4.5)
-    is replicated and runs on the rank's own tokens."""
+    is replicated and runs on the rank's own tokens.  With ``chunk_tokens``
+    set, batches larger than it go through ``ep_moe_forward_chunked``."""
 
     def __init__(self, router: torch.nn.Module, local_table, num_experts: int, group=None,
                  local_fn: Optional[Callable] = None, top_k: Optional[int] = None,
-                 shared_expert: Optional[torch.nn.Module] = None):
+                 shared_expert: Optional[torch.nn.Module] = None, chunk_tokens: Optional[int] = None):
         super().__init__()
+        self.chunk_tokens = chunk_tokens
         self.router = router
         self.shared_expert = shared_expert
         self.table = local_table
@@ -164,7 +209,10 @@ class ExpertParallelMoE(torch.nn.Module):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1]).contiguous()
         idx, w = self.route(x)
-        y = ep_moe_forward(x, idx, w, self.num_experts, self.local_fn, self.group)
+        if self.chunk_tokens and x.shape[0] > self.chunk_tokens:
+            y = ep_moe_forward_chunked(x, idx, w, self.num_experts, self.local_fn, self.chunk_tokens, self.group)
+        else:
+            y = ep_moe_forward(x, idx, w, self.num_experts, self.local_fn, self.group)
         if self.shared_expert is not None:
             y = self.shared_expert(x) + y
         return y.view(shape)

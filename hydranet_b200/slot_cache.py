@@ -227,11 +227,10 @@ class SlotCachedMoELayer(nn.Module):
         if hasattr(router, "set_cache_checker"):
             router.set_cache_checker(lambda e: cache.is_resident(layer_idx, e))
 
-    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+    def route(self, x: torch.Tensor):
+        """int32 top-k ids and float32 weights of x on the device."""
         from . import ops
         from .router import GLM4SigmoidRouter, TopKRouter
-        shape = hidden_states.shape
-        x = hidden_states.reshape(-1, shape[-1]).contiguous()
         if isinstance(self.router, TopKRouter):
             k = self.top_k if self.top_k is not None else self.router.experts_per_token
             bonus = self.router.bonus_vector(x.device)
@@ -241,6 +240,13 @@ class SlotCachedMoELayer(nn.Module):
             idx, w, _ = ops.moe_route(x, self.router.params(), self.cache.E, want_logits=False)
         else:
             raise TypeError("unsupported router type")
+        return idx, w
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        from . import ops
+        shape = hidden_states.shape
+        x = hidden_states.reshape(-1, shape[-1]).contiguous()
+        idx, w = self.route(x)
         needed = torch.unique(idx).tolist()  # the one host read of the step
         self.cache.ensure(self.layer_idx, [e for e in needed if e >= 0])
         table, maps = self.cache.table(self.layer_idx)

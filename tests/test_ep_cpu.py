@@ -44,12 +44,12 @@ def experts_oracle(n_exp=E, k=K):
     return out
 
 
-def worker(rank, world, port, T, force_idx, results, n_exp=E, k=K, router="softmax"):
+def worker(rank, world, port, T, force_idx, results, n_exp=E, k=K, router="softmax", chunk=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from hydranet_b200.ep import ep_moe_forward, expert_range
+        from hydranet_b200.ep import ep_moe_forward, ep_moe_forward_chunked, expert_range
         experts = experts_oracle(n_exp, k)
         first, last = expert_range(n_exp, rank, world)
         x = synth.host_activations(100 + rank, T, H)
@@ -71,8 +71,11 @@ def worker(rank, world, port, T, force_idx, results, n_exp=E, k=K, router="softm
                     assert first <= e < last
                     out[i] += float(weight[i, j]) * experts[e](rr[i:i + 1])[0]
             return torch.from_numpy(out)
-        y = ep_moe_forward(torch.from_numpy(x), torch.from_numpy(idx.astype(np.int32)), torch.from_numpy(w),
-                           n_exp, local_fn, exchange=TorchExchange())
+        args = (torch.from_numpy(x), torch.from_numpy(idx.astype(np.int32)), torch.from_numpy(w), n_exp, local_fn)
+        if chunk is None:
+            y = ep_moe_forward(*args, exchange=TorchExchange())
+        else:
+            y = ep_moe_forward_chunked(*args, chunk, exchange=TorchExchange())
         ref = R.moe_combine_ref(x, idx, w, experts)
         err = float(np.abs(y.numpy() - ref).max() / max(np.abs(ref).max(), 1e-30))
         results[rank] = err
@@ -86,7 +89,8 @@ def run(world, T, force_idx=None, **layout):
     port = free_port()
     procs = [ctx.Process(target=worker, args=(r, world, port, T, force_idx, results),
                          kwargs={"n_exp": layout.get("E", E), "k": layout.get("K", K),
-                                 "router": layout.get("router", "softmax")}) for r in range(world)]
+                                 "router": layout.get("router", "softmax"), "chunk": layout.get("chunk")})
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -120,6 +124,13 @@ def test_ep_glm_layout_four_ranks():
     """Sigmoid top-8 with a correction bias over 16 experts, 4 experts per
     rank: every token reaches several ranks, some more than once."""
     errs = run(4, 5, **GLM)
+    assert max(errs) < 1e-5, errs
+
+
+def test_ep_chunked_micro_batches():
+    """Prefill-size path: 11 tokens per rank in micro-batches of 4 (the last
+    one ragged), asynchronous all-to-alls, GLM routing over 2 ranks."""
+    errs = run(2, 11, chunk=4, **GLM)
     assert max(errs) < 1e-5, errs
 
 

@@ -41,13 +41,19 @@ with torch.no_grad():
 ep = ExpertParallelMoE(router, ExpertTable(slots[rank * per:(rank + 1) * per]), E)
 full = MoELayerInt4(router, ExpertTable(slots))
 x = torch.randn(T, H, generator=torch.Generator(dev).manual_seed(11 + rank), device=dev).to(torch.bfloat16)
+# micro-batched path (prefill): 40 tokens in chunks of 16, the last one ragged
+ep_mb = ExpertParallelMoE(router, ExpertTable(slots[rank * per:(rank + 1) * per]), E, chunk_tokens=16)
+x2 = torch.randn(40, H, generator=torch.Generator(dev).manual_seed(21 + rank), device=dev).to(torch.bfloat16)
 with torch.no_grad():
     y = ep(x)
     ref = full(x)
+    y2 = ep_mb(x2)
+    ref2 = full(x2)
 err = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
+err2 = ((y2.float() - ref2.float()).norm() / ref2.float().norm()).item()
 dist.destroy_process_group()
-print(f"rank {rank} rel_l2 {err:.3e}")
-sys.exit(0 if err < 1e-2 else 3)
+print(f"rank {rank} rel_l2 {err:.3e} chunked {err2:.3e}")
+sys.exit(0 if max(err, err2) < 1e-2 else 3)
 '''
 
 
