@@ -329,15 +329,24 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
     for (int gi = 0; gi < C::kSlice; ++gi) sd[gi * C::kRows] = (uint16_t)sreg[gi];
   };
 
+  // A down phase right after gate/up fills its weight ring before it waits:
+  // the weights do not depend on the gate/up results.  Its first step then
+  // waits for every group (the token slice is the newest).
+  const bool wfirst = KIND == KIND_DOWN && a.early;
+  pf_set();
+  if (wfirst)
+#pragma unroll
+    for (int i = 0; i < S - 1; ++i) pf_issue();
   if (KIND == KIND_DOWN) griddep_wait();  // the gate/up results are complete and visible from here on
   // current slice: relative steps [sl_begin, sl_end); the next one starts at (nx_i, nx_g)
   int sl_begin = 0, sl_end = slice_len(0, g_start), sl_n = 0, sl_prev_len = S - 1;
   load_tokens(0, 0, g_start, sl_end);
-  cp_async_commit();  // group 0: the first token slice
+  cp_async_commit();  // the first token slice
   load_scales(0, g_start, sl_end);
-  pf_set();
+  if (!wfirst)
 #pragma unroll
-  for (int i = 0; i < S - 1; ++i) pf_issue();
+    for (int i = 0; i < S - 1; ++i) pf_issue();
+
 
   // ---- consumer ----
   float acc[2][NT][4];
@@ -501,7 +510,10 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
       // a new slice: its tokens (and this step's weights) have landed; its
       // scales go to shared memory; after the barrier the buffers of the
       // slice before it are free and the next slice starts loading
-      cp_async_wait_n(min(S - 2, sl_prev_len - 1));
+      if (wfirst && r == 0)
+        cp_async_wait<0>();
+      else
+        cp_async_wait_n(min(S - 2, sl_prev_len - 1));
       store_scales(sl_n & 1);
       __syncthreads();
       if (sl_end < n_steps) {

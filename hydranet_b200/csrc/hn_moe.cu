@@ -634,6 +634,190 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* x, int64
 }
 
 // ---------------------------------------------------------------------------
+// Router logits of a large bf16 batch on the tensor cores (mma.sync
+// m16n8k16, bf16 operands, fp32 accumulation).  The tokens are exact in
+// bf16; the router weight is split into nsplit bf16 parts whose sum is the
+// weight exactly (three for fp32, whose 24-bit significand bf16 takes 8 bits
+// at a time; two for fp16; one for bf16), and the parts' products accumulate
+// into one fp32 sum, so the logits keep fp32-level accuracy (the reference
+// computes them as `F.linear(h.float(), W.float())`, model/glm4.py:279).
+// Each 64-wide chunk of h accumulates on the tensor core in a fresh fragment
+// that is then added to the running sum in fp32 (round to nearest): the
+// tensor core's own accumulation over all of h drifts several times further
+// from the exact sum than an fp32 matrix product does.
+// CTA tile 64 tokens x 128 experts over 64-wide chunks of h, double-buffered
+// in shared memory; warp tile 32 tokens x 32 experts (2 x 4 MMA tiles).
+// Every output sums its chunks in h order, whatever the launch shape.
+// ---------------------------------------------------------------------------
+constexpr int kRtM = 64, kRtN = 128, kRtK = 64, kRtLd = kRtK + 8;  // row pitch 144 B (16-byte aligned rows)
+constexpr size_t kRtSmem = (size_t)2 * (kRtM + 3 * kRtN) * kRtLd * 2;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// v = hi + mid + lo exactly (bf16 parts; each residual is exact in fp32)
+__device__ __forceinline__ void split3_bf16(float v, uint16_t& hi, uint16_t& mid, uint16_t& lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  const float r1 = v - __bfloat162float(h);
+  const __nv_bfloat16 m = __float2bfloat16_rn(r1);
+  const __nv_bfloat16 l = __float2bfloat16_rn(r1 - __bfloat162float(m));
+  hi = __bfloat16_as_ushort(h);
+  mid = __bfloat16_as_ushort(m);
+  lo = __bfloat16_as_ushort(l);
+}
+
+__global__ void __launch_bounds__(256) router_logits_tc_kernel(const __nv_bfloat16* x, int64_t ldx, int T, int H,
+                                                               int E, const void* rw, int rw_dtype, float* out) {
+  extern __shared__ __align__(16) uint16_t rts[];  // [2][kRtM][kRtLd] tokens, then [2][3][kRtN][kRtLd] weight parts
+  uint16_t* const xs = rts;
+  uint16_t* const ws = rts + 2 * kRtM * kRtLd;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = blockIdx.x * kRtM, e0 = blockIdx.y * kRtN;
+  const int nsplit = rw_dtype == HN_DTYPE_F32 ? 3 : (rw_dtype == HN_DTYPE_F16 ? 2 : 1);
+  // global -> registers: 2 token vectors (8 bf16) and 8 weight vectors (4 fp32 or, 16-bit, 4 of 8) per thread
+  uint4 xr[2], wr[8];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int v = tid + 256 * i, t = t0 + (v >> 3), k = k0 + (v & 7) * 8;
+      xr[i] = t < T ? __ldg(reinterpret_cast<const uint4*>(x + (int64_t)t * ldx + k)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (rw_dtype == HN_DTYPE_F32) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int v = tid + 256 * i, e = e0 + (v >> 4), k = k0 + (v & 15) * 4;
+        wr[i] = e < E ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(rw) + (int64_t)e * H + k))
+                      : make_uint4(0u, 0u, 0u, 0u);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int v = tid + 256 * i, e = e0 + (v >> 3), k = k0 + (v & 7) * 8;
+        wr[i] = e < E ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(rw) + (int64_t)e * H + k))
+                      : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  };
+  // registers -> shared buffer b (weight parts split here)
+  auto store = [&](int b) {
+    uint16_t* xb = xs + b * kRtM * kRtLd;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int v = tid + 256 * i;
+      *reinterpret_cast<uint4*>(xb + (v >> 3) * kRtLd + (v & 7) * 8) = xr[i];
+    }
+    uint16_t* wb = ws + b * 3 * kRtN * kRtLd;
+    if (rw_dtype == HN_DTYPE_F32) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int v = tid + 256 * i, row = v >> 4, col = (v & 15) * 4;
+        const float f[4] = {__uint_as_float(wr[i].x), __uint_as_float(wr[i].y), __uint_as_float(wr[i].z),
+                            __uint_as_float(wr[i].w)};
+        uint16_t p[3][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) split3_bf16(f[j], p[0][j], p[1][j], p[2][j]);
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+          *reinterpret_cast<uint2*>(wb + (q * kRtN + row) * kRtLd + col) =
+              make_uint2((uint32_t)p[q][0] | ((uint32_t)p[q][1] << 16), (uint32_t)p[q][2] | ((uint32_t)p[q][3] << 16));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int v = tid + 256 * i, row = v >> 3, col = (v & 7) * 8;
+        if (rw_dtype == HN_DTYPE_BF16) {
+          *reinterpret_cast<uint4*>(wb + row * kRtLd + col) = wr[i];
+        } else {
+          const uint16_t* h = reinterpret_cast<const uint16_t*>(&wr[i]);
+          uint16_t p[3][8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) split3_bf16(__half2float(__ushort_as_half(h[j])), p[0][j], p[1][j], p[2][j]);
+#pragma unroll
+          for (int q = 0; q < 2; ++q)
+            *reinterpret_cast<uint4*>(wb + (q * kRtN + row) * kRtLd + col) =
+                make_uint4((uint32_t)p[q][0] | ((uint32_t)p[q][1] << 16), (uint32_t)p[q][2] | ((uint32_t)p[q][3] << 16),
+                           (uint32_t)p[q][4] | ((uint32_t)p[q][5] << 16), (uint32_t)p[q][6] | ((uint32_t)p[q][7] << 16));
+        }
+      }
+    }
+  };
+  float acc[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[i][j][r] = 0.f;
+  const int wm = warp & 1, wn = warp >> 1;  // warp tile: tokens 32*wm.., experts 32*wn..
+  // ldmatrix row addresses of this lane: A (tokens) rows (l & 15), k half (l >> 4);
+  // B (weights) rows (l & 7) + 8 * (l >> 4), k half ((l >> 3) & 1)
+  const int a_row = lane & 15, a_k = (lane >> 4) * 8;
+  const int b_row = (lane & 7) + 8 * (lane >> 4), b_k = ((lane >> 3) & 1) * 8;
+  const int nk = H / kRtK;
+  load(0);
+  store(0);
+  __syncthreads();
+  for (int c = 0; c < nk; ++c) {
+    const int b = c & 1;
+    if (c + 1 < nk) load((c + 1) * kRtK);
+    const uint32_t xb = smem_u32(xs + b * kRtM * kRtLd);
+    const uint32_t wb = smem_u32(ws + b * 3 * kRtN * kRtLd);
+    float tg[2][4][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) tg[i][j][r] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kRtK; kk += 16) {
+      uint32_t af[2][4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi)
+        ldsm_x4(xb + ((wm * 32 + mi * 16 + a_row) * kRtLd + kk + a_k) * 2, af[mi][0], af[mi][1], af[mi][2], af[mi][3]);
+      for (int q = 0; q < nsplit; ++q) {
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          uint32_t b0, b1, b2, b3;  // n tiles 2np (b0, b1) and 2np+1 (b2, b3)
+          ldsm_x4(wb + ((q * kRtN + wn * 32 + np * 16 + b_row) * kRtLd + kk + b_k) * 2, b0, b1, b2, b3);
+#pragma unroll
+          for (int mi = 0; mi < 2; ++mi) {
+            mma_bf16(tg[mi][2 * np], af[mi], b0, b1);
+            mma_bf16(tg[mi][2 * np + 1], af[mi], b2, b3);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[i][j][r] += tg[i][j][r];
+    if (c + 1 < nk) store(b ^ 1);
+    __syncthreads();
+  }
+  const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int t = t0 + wm * 32 + mi * 16 + g + 8 * (r >> 1);
+        const int e = e0 + wn * 32 + ni * 8 + 2 * tq + (r & 1);
+        if (t < T && e < E) out[(int64_t)t * E + e] = acc[mi][ni][r];
+      }
+}
+
+// ---------------------------------------------------------------------------
 // Router logits of a small batch whose router matrix spans several of the
 // prep kernel's 64 KB chunks (GLM-4.5: 128 experts x 4096 fp32 = 2 MB): the
 // per-token prep CTA would stream the whole matrix chunk by chunk, one round
@@ -784,17 +968,32 @@ __global__ void __launch_bounds__(256) stage_rows_kernel(const int* a_tok, const
   for (int w = lane; w < u; w += 32) dst[w] = __ldcg(src + w);
 }
 
+// One CTA per expert.  Both passes over the routing read it with 16-byte
+// loads through L1; the second gives every thread a contiguous run of
+// (token, slot) entries, so one block-wide scan of the per-thread match
+// counts orders the expert's assignments by (token, slot) with no barrier
+// inside the loops.
 __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
   extern __shared__ int psm[];
   int* cnt = psm;  // [E]
   __shared__ int s_base[2];  // assignment offset, segment offset of this expert
-  const int e = blockIdx.x, tid = threadIdx.x;
+  __shared__ int s_wsum[8];
+  const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int64_t TK = (int64_t)a.T * a.K;
+  const int64_t n4 = TK >> 2;  // plan.idx is 256-byte aligned
+  const int4* idx4 = reinterpret_cast<const int4*>(a.plan.idx);
   for (int i = tid; i < a.E; i += 256) cnt[i] = 0;
   __syncthreads();
-  for (int64_t i = tid; i < TK; i += 256) {
-    const int x = __ldcg(a.plan.idx + i);
-    if (x >= 0) atomicAdd(&cnt[x], 1);  // -1: a skipped token's slot
+  for (int64_t i = tid; i < n4; i += 256) {
+    const int4 v = idx4[i];
+    if (v.x >= 0) atomicAdd(&cnt[v.x], 1);  // -1: a skipped token's slot
+    if (v.y >= 0) atomicAdd(&cnt[v.y], 1);
+    if (v.z >= 0) atomicAdd(&cnt[v.z], 1);
+    if (v.w >= 0) atomicAdd(&cnt[v.w], 1);
+  }
+  for (int64_t i = 4 * n4 + tid; i < TK; i += 256) {
+    const int x = a.plan.idx[i];
+    if (x >= 0) atomicAdd(&cnt[x], 1);
   }
   __syncthreads();
   if (tid == 0) {
@@ -818,38 +1017,42 @@ __global__ void __launch_bounds__(256) plan_kernel(const PlanArgs a) {
       *a.plan.n_assign = o + m;
     }
   }
-  // this expert's assignments in (token, slot) order: coalesced rounds of
-  // 256 routing entries, a ballot per warp and a prefix over the 8 warps
-  __shared__ int s_wcnt[8];
   __syncthreads();
   if (e == a.E - 1)
     // positions past the planned assignments (skipped tokens' slots) name
     // token 0, so a copy over all T*K positions stays in bounds
     for (int64_t q = s_base[0] + cnt[e] + tid; q < TK; q += 256) a.plan.a_tok[q] = 0;
-  const int lane = tid & 31, wid = tid >> 5;
-  int base = s_base[0];
-  for (int64_t r0 = 0; r0 < TK; r0 += 256) {
-    const int64_t i = r0 + tid;
-    const bool hit = i < TK && __ldcg(a.plan.idx + i) == e;
-    const unsigned bal = __ballot_sync(0xffffffffu, hit);
-    if (lane == 0) s_wcnt[wid] = __popc(bal);
-    __syncthreads();
-    int before = 0, total = 0;
+  // this thread's entries: [lo, hi), a multiple of 4 long except at the end
+  const int64_t run = ((TK + 255) / 256 + 3) & ~(int64_t)3;
+  const int64_t lo = min(TK, (int64_t)tid * run), hi = min(TK, lo + run);
+  auto match = [&](int64_t i, int x) { return x == e ? 1 : 0; };
+  int mine = 0;
+  for (int64_t i = lo; i < hi; i += 4) {
+    if (i + 4 <= hi) {
+      const int4 v = idx4[i >> 2];
+      mine += match(i, v.x) + match(i, v.y) + match(i, v.z) + match(i, v.w);
+    } else {
+      for (int64_t j = i; j < hi; ++j) mine += match(j, a.plan.idx[j]);
+    }
+  }
+  int incl = mine;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      const int cw = s_wcnt[w];
-      before += w < wid ? cw : 0;
-      total += cw;
-    }
-    if (hit) {
-      const int p = base + before + __popc(bal & ((1u << lane) - 1u));
-      a.plan.pos[i] = p;
-      a.plan.a_tok[p] = (int)(i / a.K);
-      a.plan.a_tk[p] = (int)i;
-      a.plan.a_w[p] = __ldcg(a.plan.wts + i);
-    }
-    base += total;
-    __syncthreads();  // s_wcnt is rewritten by the next round
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_wsum[wid] = incl;
+  __syncthreads();
+  int p = s_base[0] + incl - mine;
+  for (int w = 0; w < wid; ++w) p += s_wsum[w];
+  if (mine == 0) return;
+  for (int64_t i = lo; i < hi; ++i) {
+    if (a.plan.idx[i] != e) continue;
+    a.plan.pos[i] = p;
+    a.plan.a_tok[p] = (int)(i / a.K);
+    a.plan.a_tk[p] = (int)i;
+    a.plan.a_w[p] = a.plan.wts[i];
+    ++p;
   }
 }
 
@@ -1957,7 +2160,20 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   if (sm > 48 * 1024)
     HN_CUDA(cudaFuncSetAttribute(route_prep_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   r.plan_here = TK <= kPlanSmemEntries;
-  if (gemm) {
+  if (gemm && std::is_same<Tr, BF16>::value && ra.H % kRtK == 0) {
+    static std::atomic<bool> attr_tc[64] = {};  // per device; setting it twice is harmless
+    int dev = 0;
+    HN_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !attr_tc[dev].load(std::memory_order_acquire)) {
+      HN_CUDA(cudaFuncSetAttribute(router_logits_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRtSmem));
+      if (dev >= 0 && dev < 64) attr_tc[dev].store(true, std::memory_order_release);
+    }
+    router_logits_tc_kernel<<<dim3((unsigned)((ra.T + kRtM - 1) / kRtM), (unsigned)((ra.E + kRtN - 1) / kRtN)), 256,
+                              kRtSmem, s>>>(static_cast<const __nv_bfloat16*>(ra.x), ra.ldx, ra.T, ra.H, ra.E, ra.rw,
+                                            ra.rw_dtype, ra.plan.rlog);
+    HN_CUDA(cudaGetLastError());
+    r.pre_logits = ra.plan.rlog;
+  } else if (gemm) {
     router_logits_kernel<Tr><<<dim3((unsigned)((ra.T + kRgM - 1) / kRgM), (unsigned)((ra.E + kRgN - 1) / kRgN)), 256, 0, s>>>(
         ra.x, ra.ldx, ra.T, ra.H, ra.E, ra.rw, ra.rw_dtype, ra.plan.rlog);
     HN_CUDA(cudaGetLastError());

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from hydranet_b200 import synth
+from hydranet_b200 import _lib, synth
 from hydranet_b200.kernels import int4_gemm as k_gemm
 from hydranet_b200.moe import MoELayerInt4, moe_experts
 from hydranet_b200.router import GLM4SigmoidRouter, TopKRouter
@@ -111,3 +111,23 @@ def test_int4_linear_wide_segments(lib, M, N, K, dtype):
     ref = R.int4_linear_ref(to_np32(xt), p, s)
     err = rel_l2(to_np32(out), ref)
     assert err <= TOL and err <= {"bf16": 5e-3, "f16": 1e-3}[dtype], err
+
+
+@pytest.mark.parametrize("wdtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("T,E,H", [(512, 128, 1024), (300, 40, 512)])
+def test_large_batch_router_logits_precision(lib, wdtype, T, E, H):
+    """Router logits of a batch that takes the router GEMM (T >= 256): within
+    a few times the error of a float32 matrix product of the same operands,
+    measured against float64 (the split weight parts must add up exactly)."""
+    from hydranet_b200 import ops
+    g = torch.Generator("cuda").manual_seed(T + E)
+    x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+    wt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[wdtype]
+    rw = (torch.randn(E, H, generator=g, device="cuda") * 0.02).to(wt)
+    p = ops.router_params(_lib.HN_ROUTER_SIGMOID_TOPK, 4, rw, logits_in_act_dtype=False)
+    _, _, logits = ops.moe_route(x, p, E)
+    xi, wi = to_np32(x).astype(np.float64), to_np32(rw).astype(np.float64)
+    ref = xi @ wi.T
+    err = np.abs(logits.cpu().numpy().astype(np.float64) - ref).max()
+    err32 = np.abs((to_np32(x) @ to_np32(rw).T).astype(np.float64) - ref).max()
+    assert err <= 4 * err32 + 1e-6, (err, err32)
