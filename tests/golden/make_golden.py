@@ -169,6 +169,43 @@ def scheduler_trace(torch):
     return {"lines": np.array(scheduler_script.run(continuous_batch, torch))}
 
 
+def glm4_dense_cases(torch):
+    """The reference's ``GLM4Attention`` (prefill of 5 positions, then one
+    decode position through its ``SimpleKVCache``), ``GLM4DenseMLP`` and an
+    lm_head-shaped linear, float32 on CPU, at a small GLM-4.5 layout (8 query
+    / 2 KV heads, head_dim 32, partial rotary 0.5, attention bias)."""
+    from hydranet.config import GLM4AirConfig
+    from hydranet.model.glm4 import GLM4Attention, GLM4DenseMLP
+    from hydranet.cache.kv_cache import SimpleKVCache
+    cfg = GLM4AirConfig()
+    cfg.hidden_dim, cfg.num_attention_heads, cfg.num_kv_heads, cfg.head_dim = 256, 8, 2, 32
+    cfg.intermediate_dim, cfg.max_position_embeddings = 192, 64
+    torch.manual_seed(0)
+    attn = GLM4Attention(cfg, 0).float()
+    mlp = GLM4DenseMLP(cfg).float()
+    out = {}
+    with torch.no_grad():
+        for name, mod in (("attn", attn), ("mlp", mlp)):
+            for pn, p in mod.named_parameters():
+                v = torch.from_numpy(synth.host_normal(sum(pn.encode()) + 31, tuple(p.shape), 0.05))
+                p.copy_(v)
+                out[f"{name}/{pn}"] = v.numpy()
+        x = torch.from_numpy(synth.host_normal(5, (1, 6, 256), 1.0))
+        out["x"] = x.numpy()
+        cache = SimpleKVCache(num_layers=1, num_kv_heads=2, head_dim=32, max_seq_len=16, device=torch.device("cpu"),
+                              dtype=torch.float32)
+        out["attn_prefill"] = attn(x[:, :5], torch.arange(5).view(1, 5), kv_cache=cache).numpy()
+        cache.set_len(5)
+        out["attn_decode"] = attn(x[:, 5:6], torch.tensor([[5]]), kv_cache=cache).numpy()
+        out["attn_nocache"] = attn(x, torch.arange(6).view(1, 6)).numpy()
+        out["mlp"] = mlp(x).numpy()
+        lm = torch.nn.Linear(256, 96, bias=False).float()
+        lm.weight.copy_(torch.from_numpy(synth.host_normal(77, (96, 256), 0.05)))
+        out["lm_w"] = lm.weight.numpy()
+        out["lm"] = lm(x).numpy()
+    return out
+
+
 def store_case(ref: Path):
     """A packed store written by the reference's own test helper
     (``tests/test_int4_loader.py:28-119``: 2 layers x 2 experts, H 256, F 512,
@@ -345,7 +382,8 @@ def main():
     light = {"int4linear_quant": lambda: int4linear_cases(torch, Int4Linear),
              "gatherer": lambda: gatherer_cases(torch, GroupByExpertGatherer),
              "reference_store": lambda: store_case(args.reference.resolve()),
-             "scheduler_trace": lambda: scheduler_trace(torch)}
+             "scheduler_trace": lambda: scheduler_trace(torch),
+             "glm4_dense": lambda: glm4_dense_cases(torch)}
     for stem, make in light.items():
         if args.only in (None, stem):
             np.savez_compressed(HERE / f"{stem}.npz", **make())
