@@ -33,7 +33,8 @@ class RouterParams(ctypes.Structure):
     """``hn_router_params``."""
     _fields_ = [("kind", c_int), ("top_k", c_int), ("weight", c_void_p), ("weight_dtype", c_int),
                 ("logits_in_act_dtype", c_int), ("affinity_bonus", c_void_p), ("entropy_threshold", c_float),
-                ("correction_bias", c_void_p), ("norm_topk_prob", c_int), ("routed_scaling_factor", c_float)]
+                ("correction_bias", c_void_p), ("norm_topk_prob", c_int), ("routed_scaling_factor", c_float),
+                ("n_group", c_int), ("topk_group", c_int)]
 
 
 # name -> (restype, argtypes)
@@ -107,7 +108,7 @@ def load():
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
-            if lib.hn_abi_version() != 2:
+            if lib.hn_abi_version() != 3:
                 raise RuntimeError("libhydranet_b200.so ABI version mismatch")
             _lib = lib
     return _lib

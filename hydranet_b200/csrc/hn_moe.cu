@@ -115,6 +115,7 @@ struct RouteArgs {
   const float* bias;
   int norm;
   float scaling;
+  int n_group, topk_group;  // group-limited selection (sigmoid) when n_group > 1 && topk_group > 0
   const int32_t* given_idx;
   const float* given_w;
   int32_t* out_idx;
@@ -296,6 +297,34 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
         scs[e] = v;
       }
       __syncwarp();
+      // group-limited routing (model/glm4.py:285-297): lane g scores group g
+      // by its best selection score; the topk_group best groups stay, the
+      // other experts' scores become 0
+      unsigned keep = 0xffffffffu;
+      const bool grouped = a.kind == HN_ROUTER_SIGMOID_TOPK && a.n_group > 1 && a.topk_group > 0;
+      const int gsz = grouped ? a.E / a.n_group : a.E;
+      if (grouped) {
+        float gm = -INFINITY;
+        if (lane < a.n_group)
+          for (int i = 0; i < gsz; ++i) gm = fmaxf(gm, scs[lane * gsz + i]);
+        keep = 0u;
+        for (int j = 0; j < a.topk_group; ++j) {
+          float bv = lane < a.n_group && !((keep >> lane) & 1u) ? gm : -INFINITY;
+          int bi = lane < a.n_group && !((keep >> lane) & 1u) ? lane : 0x7fffffff;
+          for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+              bv = ov;
+              bi = oi;
+            }
+          }
+          if (bi < a.n_group) keep |= 1u << bi;
+        }
+        for (int e = lane; e < a.E; e += 32)
+          if (!((keep >> (e / gsz)) & 1u)) scs[e] = 0.f;
+        __syncwarp();
+      }
 #pragma unroll 1
       for (int k = 0; k < a.K; ++k) {
         float bv = -INFINITY;
@@ -340,10 +369,13 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
           }
           for (int k = 0; k < a.K; ++k) s_w[k] = s_w[k] / s2;
         } else {
-          // sigmoid scores of the selected experts, unbiased (model/glm4.py:300-307)
+          // sigmoid scores of the selected experts, unbiased (model/glm4.py:300-307);
+          // an expert of a dropped group (only when top_k exceeds the kept
+          // experts) carries its masked score, 0
           float sum = 0.f;
           for (int k = 0; k < a.K; ++k) {
-            s_w[k] = 1.0f / (1.0f + expf(-lg[s_idx[k]]));
+            const bool kept = (keep >> (s_idx[k] / gsz)) & 1u;
+            s_w[k] = kept ? 1.0f / (1.0f + expf(-lg[s_idx[k]])) : 0.f;
             sum += s_w[k];
           }
           for (int k = 0; k < a.K; ++k) {
@@ -1872,7 +1904,7 @@ static int encode_token_map(CUtensorMap* data, const void* base, int64_t rows, i
 // tensor pipe is four times wider (at 24-32 tokens per segment the mma.sync
 // pipe, not HBM, would bound the phase).
 static std::atomic<int> g_decode_engine{HN_ENGINE_AUTO};
-static int gv_nt(int nt) { return nt <= 1 ? 1 : 2; }
+static int gv_nt(int nt) { return nt <= 1 ? 1 : (nt == 2 ? 2 : 4); }
 // CTAs of an mma.sync engine launch (two per SM)
 static int gv_grid(int nt) {
   const int sms = sm_count_current();
@@ -1890,7 +1922,7 @@ static bool gv_fits(int nt, int64_t max_segs, int64_t rows, bool gateup) {
   const int64_t tiles = max_segs * ((rows + tile_rows - 1) / tile_rows);
   return tiles / gv_grid(nt) + 3 <= kGvMaxTiles;
 }
-static bool use_gv(int nt) { return nt <= 2 && g_decode_engine.load(std::memory_order_relaxed) != HN_ENGINE_TCGEN05; }
+static bool use_gv(int nt) { return nt <= 4 && g_decode_engine.load(std::memory_order_relaxed) != HN_ENGINE_TCGEN05; }
 // Bytes of stream-K partials an mma.sync engine launch may write.
 static size_t gv_part_bytes(int nt) {
   return (size_t)gv_grid(nt) * 2 * gv_warps(nt) * 2 * gv_nt(nt) * 32 * 16;
@@ -1924,7 +1956,8 @@ static int launch_gv_t(const GvArgs& a, cudaStream_t s) {
 template <typename Tr, int KIND, int EPI>
 static int launch_gv(int nt, const GvArgs& a, cudaStream_t s) {
   if (nt <= 1) return launch_gv_t<Tr, 1, KIND, EPI>(a, s);
-  return launch_gv_t<Tr, 2, KIND, EPI>(a, s);
+  if (nt == 2) return launch_gv_t<Tr, 2, KIND, EPI>(a, s);
+  return launch_gv_t<Tr, 4, KIND, EPI>(a, s);
 }
 
 // The mma.sync engine's arguments for the phase the tcgen05 engine's
@@ -2211,6 +2244,10 @@ static int check_router(const hn_router_params* r, int64_t E) {
   HN_REQUIRE(r->weight, "router weight is NULL");
   HN_REQUIRE(r->weight_dtype >= HN_DTYPE_F32 && r->weight_dtype <= HN_DTYPE_BF16, "bad router weight dtype");
   HN_REQUIRE(r->top_k >= 1 && r->top_k <= E && r->top_k <= kMaxTopK, "top_k out of range");
+  if (r->kind == HN_ROUTER_SIGMOID_TOPK && r->n_group > 1 && r->topk_group > 0) {
+    HN_REQUIRE(r->n_group <= 32 && E % r->n_group == 0, "n_group must divide the experts and be at most 32");
+    HN_REQUIRE(r->topk_group <= r->n_group, "topk_group exceeds n_group");
+  }
   return HN_OK;
 }
 
@@ -2337,6 +2374,8 @@ static int run_moe(const MoECall& m) {
     ra.bias = m.router->kind == HN_ROUTER_SIGMOID_TOPK ? m.router->correction_bias : nullptr;
     ra.norm = m.router->norm_topk_prob;
     ra.scaling = m.router->routed_scaling_factor;
+    ra.n_group = m.router->n_group;
+    ra.topk_group = m.router->topk_group;
   }
   ra.given_idx = m.given_idx;
   ra.given_w = m.given_w;

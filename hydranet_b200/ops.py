@@ -129,10 +129,10 @@ def expert_mlp_int4(x, gate_packed, gate_scales, up_packed, up_scales, down_pack
 def router_params(kind: int, top_k: int, weight: torch.Tensor, logits_in_act_dtype: bool,
                   affinity_bonus: torch.Tensor | None = None, entropy_threshold: float = 0.5,
                   correction_bias: torch.Tensor | None = None, norm_topk_prob: bool = True,
-                  routed_scaling_factor: float = 1.0) -> _lib.RouterParams:
+                  routed_scaling_factor: float = 1.0, n_group: int = 1, topk_group: int = 0) -> _lib.RouterParams:
     return _lib.RouterParams(kind, top_k, weight.data_ptr(), _lib.dtype_code(weight.dtype), int(logits_in_act_dtype),
                              ptr(affinity_bonus), entropy_threshold, ptr(correction_bias), int(norm_topk_prob),
-                             routed_scaling_factor)
+                             routed_scaling_factor, int(n_group), int(topk_group))
 
 
 def moe_route(x: torch.Tensor, params: _lib.RouterParams, num_experts: int, keep_refs=(), want_logits: bool = True):

@@ -110,22 +110,22 @@ class TopKRouter(nn.Module):
 
 
 class GLM4SigmoidRouter(nn.Module):
-    """GLM-4.5 router (``model/glm4.py:238-309``) with an optional correction bias."""
+    """GLM-4.5 router (``model/glm4.py:238-309``) with an optional correction bias;
+    group-limited selection when ``n_group > 1`` (``model/glm4.py:285-297``)."""
 
     def __init__(self, config=None, layer_idx: int = 0, *, hidden_dim: Optional[int] = None,
-                 num_experts: Optional[int] = None, experts_per_token: int = 8):
+                 num_experts: Optional[int] = None, experts_per_token: int = 8, n_group: int = 1,
+                 topk_group: int = 1):
         super().__init__()
         self.config = config
         self.layer_idx = layer_idx
         self.hidden_dim = hidden_dim or config.hidden_dim
         self.num_experts = num_experts or config.num_experts
         self.top_k = _cfg(config, "experts_per_token", experts_per_token)
-        self.n_group = _cfg(config, "n_group", 1)
-        self.topk_group = _cfg(config, "topk_group", 1)
+        self.n_group = _cfg(config, "n_group", n_group)
+        self.topk_group = _cfg(config, "topk_group", topk_group)
         self.norm_topk_prob = _cfg(config, "norm_topk_prob", True)
         self.routed_scaling_factor = _cfg(config, "routed_scaling_factor", 1.0)
-        if self.n_group > 1 and self.topk_group > 0:
-            raise NotImplementedError("group-limited routing (n_group > 1) is not implemented")
         self.weight = nn.Parameter(torch.empty(self.num_experts, self.hidden_dim))
         nn.init.normal_(self.weight, std=0.02)
         self.e_score_correction_bias: Optional[torch.Tensor] = None
@@ -136,7 +136,8 @@ class GLM4SigmoidRouter(nn.Module):
     def params(self) -> _lib.RouterParams:
         return ops.router_params(_lib.HN_ROUTER_SIGMOID_TOPK, self.top_k, self.weight, logits_in_act_dtype=False,
                                  correction_bias=self.e_score_correction_bias, norm_topk_prob=self.norm_topk_prob,
-                                 routed_scaling_factor=self.routed_scaling_factor)
+                                 routed_scaling_factor=self.routed_scaling_factor, n_group=self.n_group,
+                                 topk_group=self.topk_group)
 
     def forward(self, hidden_states: torch.Tensor):
         h = hidden_states.shape[-1]

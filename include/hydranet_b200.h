@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define HN_ABI_VERSION 2
+#define HN_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define HN_API __attribute__((visibility("default")))
@@ -149,6 +149,13 @@ typedef struct hn_router_params {
                                for selection only                                  */
   int norm_topk_prob;       /* sigmoid only (model/glm4.py:302-304)              */
   float routed_scaling_factor; /* sigmoid only (model/glm4.py:307)                */
+  int n_group;              /* sigmoid only: group-limited routing when n_group > 1
+                               and topk_group > 0 (model/glm4.py:285-297): the E
+                               experts form n_group equal groups (n_group <= 32),
+                               each scored by its best selection score; only the
+                               topk_group best groups' experts keep their scores,
+                               the others score 0 (ties: lower group index)       */
+  int topk_group;
 } hn_router_params;
 
 HN_API size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int top_k);

@@ -280,13 +280,15 @@ def softmax_topk_router_ref(h: np.ndarray, gate_w: np.ndarray, top_k: int, act_d
 
 def sigmoid_topk_router_ref(h: np.ndarray, router_w: np.ndarray, top_k: int, act_dtype: str = "f32",
                             correction_bias: np.ndarray | None = None, norm_topk_prob: bool = True,
-                            routed_scaling_factor: float = 1.0):
+                            routed_scaling_factor: float = 1.0, n_group: int = 1, topk_group: int = 0):
     """GLM-4.5 sigmoid top-k router.
 
     Follows ``GLM4SigmoidRouter.forward`` (``model/glm4.py:261-309``): float32
     logits (:279), sigmoid (:282), top-k (:300), normalise with ``+1e-9``
-    (:303-304), scale (:307), cast (:309).  The group mask (:285-297) is a
-    no-op for ``n_group == 1`` (``config.py:108-109``) and is not modelled.
+    (:303-304), scale (:307), cast (:309).  With ``n_group > 1`` and
+    ``topk_group > 0`` the group mask (:285-297): groups of E / n_group
+    experts scored by their best score, the ``topk_group`` best kept, the
+    other experts' scores multiplied by 0 before the top-k.
 
     ``correction_bias`` (an extension: the reference loads
     ``e_score_correction_bias`` but never applies it,
@@ -298,6 +300,14 @@ def sigmoid_topk_router_ref(h: np.ndarray, router_w: np.ndarray, top_k: int, act
     logits = h2 @ router_w.astype(np.float32).T
     scores = (np.float32(1.0) / (np.float32(1.0) + np.exp(-logits))).astype(np.float32)
     sel_scores = scores if correction_bias is None else scores + correction_bias.astype(np.float32)[None, :]
+    if n_group > 1 and topk_group > 0:
+        gs = sel_scores.shape[-1] // n_group
+        gmax = sel_scores.reshape(-1, n_group, gs).max(-1)
+        keep = np.zeros_like(gmax, dtype=bool)
+        np.put_along_axis(keep, topk_desc(gmax, topk_group), True, -1)
+        mask = np.repeat(keep, gs, axis=-1)
+        sel_scores = np.where(mask, sel_scores, np.float32(0.0))
+        scores = np.where(mask, scores, np.float32(0.0))
     idx = topk_desc(sel_scores, top_k)
     w = np.take_along_axis(scores, idx, -1)
     if norm_topk_prob:

@@ -206,6 +206,28 @@ def glm4_dense_cases(torch):
     return out
 
 
+def glm_group_router_cases(torch):
+    """The reference's ``GLM4SigmoidRouter`` with group-limited selection
+    (``model/glm4.py:285-297``): 32 experts in 4 groups, 2 groups kept, top-6,
+    and 64 experts in 8 groups, 3 kept, top-8; float32 on CPU."""
+    from hydranet.config import GLM4AirConfig
+    from hydranet.model.glm4 import GLM4SigmoidRouter
+    out = {}
+    for name, (E, ng, kg, k, H, T) in {"g4": (32, 4, 2, 6, 256, 40), "g8": (64, 8, 3, 8, 512, 33)}.items():
+        cfg = GLM4AirConfig()
+        cfg.num_experts, cfg.hidden_dim, cfg.experts_per_token = E, H, k
+        cfg.n_group, cfg.topk_group = ng, kg
+        r = GLM4SigmoidRouter(cfg, 0).float()
+        w = synth.host_normal(60 + E, (E, H), 0.05)
+        x = synth.host_normal(70 + E, (1, T, H), 1.0)
+        with torch.no_grad():
+            r.weight.copy_(torch.from_numpy(w))
+            idx, wt = r(torch.from_numpy(x))
+        out.update({f"{name}/w": w, f"{name}/x": x, f"{name}/idx": idx.numpy(), f"{name}/wt": wt.numpy(),
+                    f"{name}/cfg": np.array([E, ng, kg, k, H, T])})
+    return out
+
+
 def store_case(ref: Path):
     """A packed store written by the reference's own test helper
     (``tests/test_int4_loader.py:28-119``: 2 layers x 2 experts, H 256, F 512,
@@ -383,7 +405,8 @@ def main():
              "gatherer": lambda: gatherer_cases(torch, GroupByExpertGatherer),
              "reference_store": lambda: store_case(args.reference.resolve()),
              "scheduler_trace": lambda: scheduler_trace(torch),
-             "glm4_dense": lambda: glm4_dense_cases(torch)}
+             "glm4_dense": lambda: glm4_dense_cases(torch),
+             "glm_group_router": lambda: glm_group_router_cases(torch)}
     for stem, make in light.items():
         if args.only in (None, stem):
             np.savez_compressed(HERE / f"{stem}.npz", **make())

@@ -299,3 +299,35 @@ def test_glm_layer_with_shared_expert(lib):
     sh = (R.silu(xi @ g.T) * (xi @ u.T)) @ d.T
     err = rel_l2(to_np32(out.view(32, 4096)), routed + sh)
     assert err <= TOL and err <= TIGHT, err
+
+
+@pytest.mark.parametrize("case", ["g4", "g8"])
+def test_group_limited_router_matches_reference(lib, golden_dir, case):
+    """Group-limited sigmoid routing on the device, on the inputs the reference's
+    own ``GLM4SigmoidRouter`` routed (``model/glm4.py:285-297``)."""
+    d = dict(np.load(golden_dir / "glm_group_router.npz"))
+    E, ng, kg, k, H, T = (int(v) for v in d[case + "/cfg"])
+    r = GLM4SigmoidRouter(hidden_dim=H, num_experts=E, experts_per_token=k, n_group=ng, topk_group=kg).cuda()
+    with torch.no_grad():
+        r.weight.copy_(torch.from_numpy(d[case + "/w"]))
+    x = torch.from_numpy(d[case + "/x"]).cuda()
+    idx, w = r(x)
+    np.testing.assert_array_equal(np.sort(idx.cpu().numpy(), 1), np.sort(d[case + "/idx"], 1))
+    np.testing.assert_allclose(np.sort(to_np32(w), 1), np.sort(d[case + "/wt"], 1), rtol=1e-5, atol=1e-6)
+
+
+def test_group_limited_glm_layer(lib):
+    """A routed layer with group-limited routing (4 groups of 8 experts, 2 kept,
+    top-6), bf16, against the oracle."""
+    H, F, E, k = 512, 256, 32, 6
+    shape = synth.MoEShape(H, F, E, k)
+    table, packed = host_moe(shape, 808)
+    r = GLM4SigmoidRouter(hidden_dim=H, num_experts=E, experts_per_token=k, n_group=4, topk_group=2).cuda()
+    layer = MoELayerInt4(r, table)
+    x = torch.randn(24, H, generator=torch.Generator("cuda").manual_seed(6), device="cuda").to(torch.bfloat16)
+    out, ro = layer(x, return_routing=True)
+    xi = to_np32(x)
+    idx, w, logits = R.sigmoid_topk_router_ref(xi, to_np32(r.weight), k, "bf16", n_group=4, topk_group=2)
+    np.testing.assert_array_equal(np.sort(ro.expert_indices.cpu().numpy(), 1), np.sort(idx, 1))
+    ref = R.moe_combine_ref(xi, idx, w, oracle_experts(packed))
+    assert rel_l2(to_np32(out), ref) <= TIGHT

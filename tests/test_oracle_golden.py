@@ -144,3 +144,16 @@ def test_glm_router_full_width(golden_dir, name, dtype):
     idx, w, _ = R.sigmoid_topk_router_ref(x, synth.host_router_weight(seed, shape), K, dtype)
     np.testing.assert_array_equal(idx, g["idx"])
     np.testing.assert_allclose(w, g["weights"], rtol=1e-2 if dtype == "bf16" else 1e-5, atol=1e-6)
+
+
+def test_glm_group_limited_router_golden(golden_dir):
+    """Group-limited sigmoid routing (``model/glm4.py:285-297``) against the reference's own router."""
+    d = dict(np.load(golden_dir / "glm_group_router.npz"))
+    for n in ("g4", "g8"):
+        E, ng, kg, k, H, T = (int(v) for v in d[n + "/cfg"])
+        idx, w, _ = R.sigmoid_topk_router_ref(d[n + "/x"][0], d[n + "/w"], k, "f32", n_group=ng, topk_group=kg)
+        np.testing.assert_array_equal(np.sort(idx, 1), np.sort(d[n + "/idx"], 1))
+        np.testing.assert_allclose(np.sort(w, 1), np.sort(d[n + "/wt"], 1), rtol=1e-6, atol=1e-7)
+        # the mask matters here: the plain top-k would pick other experts
+        plain, _, _ = R.sigmoid_topk_router_ref(d[n + "/x"][0], d[n + "/w"], k, "f32")
+        assert (np.sort(plain, 1) != np.sort(idx, 1)).any()
