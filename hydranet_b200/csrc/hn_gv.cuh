@@ -478,31 +478,68 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) tot[mt][j][e] = 0.f;
-    for (int cc = c0; cc <= c1; ++cc) {
-      const int64_t b0 = gv_begin(NS, cc, P);
-      if (b0 >= gv_begin(NS, cc + 1, P)) continue;
-      if (cc == c) {
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int j = 0; j < NT; ++j)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) tot[mt][j][e] += acc[mt][j][e];
-      } else {
+    // the pieces in CTA order, kU at a time with all their loads in flight
+    // before the first add (a tile of a small step is split over up to ~10 CTAs)
+    constexpr int kU = NT == 1 ? 4 : 2;
+    if constexpr (NT == 4) {
+      // 32-token tiles: no registers to spare for loads in flight
+      for (int cc = c0; cc <= c1; ++cc) {
+        const int64_t b0 = gv_begin(NS, cc, P);
+        if (b0 >= gv_begin(NS, cc + 1, P)) continue;
         const int sl = b0 / G == tile ? 0 : 1;
-        const float4* other =
+        const float4* src =
             reinterpret_cast<const float4*>(a.part) + (((int64_t)cc * 2 + sl) * W + warp) * (2 * NT * 32);
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
           for (int j = 0; j < NT; ++j) {
-            const float4 q = __ldcg(other + (mt * NT + j) * 32 + lane);
+            const float4 q = cc == c ? make_float4(acc[mt][j][0], acc[mt][j][1], acc[mt][j][2], acc[mt][j][3])
+                                     : __ldcg(src + (mt * NT + j) * 32 + lane);
             tot[mt][j][0] += q.x;
             tot[mt][j][1] += q.y;
             tot[mt][j][2] += q.z;
             tot[mt][j][3] += q.w;
           }
       }
+    } else {
+    for (int cb = c0; cb <= c1; cb += kU) {
+      float4 q[kU][2][NT];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int cc = cb + u;
+        const int64_t b0 = gv_begin(NS, cc, P);
+        const bool other = cc <= c1 && cc != c && b0 < gv_begin(NS, cc + 1, P);
+        const int sl = b0 / G == tile ? 0 : 1;
+        const float4* src =
+            reinterpret_cast<const float4*>(a.part) + (((int64_t)cc * 2 + sl) * W + warp) * (2 * NT * 32);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int j = 0; j < NT; ++j)
+            q[u][mt][j] = other ? __ldcg(src + (mt * NT + j) * 32 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int cc = cb + u;
+        if (cc > c1 || gv_begin(NS, cc, P) >= gv_begin(NS, cc + 1, P)) continue;
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            if (cc == c) {
+              tot[mt][j][0] += acc[mt][j][0];
+              tot[mt][j][1] += acc[mt][j][1];
+              tot[mt][j][2] += acc[mt][j][2];
+              tot[mt][j][3] += acc[mt][j][3];
+            } else {
+              tot[mt][j][0] += q[u][mt][j].x;
+              tot[mt][j][1] += q[u][mt][j].y;
+              tot[mt][j][2] += q[u][mt][j].z;
+              tot[mt][j][3] += q[u][mt][j].w;
+            }
+          }
+      }
+    }
     }
     epilogue(tot, tile);
   };

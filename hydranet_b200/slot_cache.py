@@ -14,11 +14,14 @@ async H2D copies through pinned staging (``PinnedStagingRing`` and
   once; a layer's expert table (``hn_expert_ptrs`` rows + descriptors) is
   rebuilt on the host from the slot numbers of its resident experts and
   uploaded as one small copy when residency changes;
-* eviction is least-recently-used over the slots whose expert the current
-  call does not need (the reference's per-layer sticky-LFU tiers are a policy
-  choice the kernels do not depend on); the copy stream waits for the compute
-  stream before overwriting a slot, and the compute stream waits for the copy
-  before the experts run.
+* eviction picks, among the slots whose expert the current call does not
+  need, the least frequently used one (policy "lfu", the default: a use
+  count per (layer, expert) that halves every ``decay_every`` uses of the
+  cache, ties to the least recent -- the frequency idea of the reference's
+  sticky-LFU tiers, ``cache/expert_cache.py``) or the least recently used
+  one (policy "lru"); the copy stream waits for the compute stream before
+  overwriting a slot, and the compute stream waits for the copy before the
+  experts run.
 
 ``SlotCachedMoELayer`` is the routed MoE layer over such a cache: the
 router runs on the device, the selected experts reach the host (one read,
@@ -86,14 +89,80 @@ class CacheStats:
         return self.hits / n if n else 0.0
 
 
+class Residency:
+    """Which (layer, expert) lives in which of ``num_slots`` slots; host only.
+
+    ``admit(layer, experts)`` makes the given experts resident, evicting by
+    the policy among the slots the call does not need, and returns the
+    loads to make as (slot, key) pairs; it never evicts an expert of the same
+    call and refuses a call that needs more experts than there are slots."""
+
+    def __init__(self, num_slots: int, policy: str = "lfu", decay_every: int = 4096):
+        if num_slots < 1:
+            raise ValueError("need at least one slot")
+        if policy not in ("lfu", "lru"):
+            raise ValueError("policy must be 'lfu' or 'lru'")
+        self.S = num_slots
+        self.policy = policy
+        self.decay_every = decay_every
+        self.freq: Dict[Tuple[int, int], float] = {}
+        self.owner: List[Optional[Tuple[int, int]]] = [None] * num_slots
+        self.where: Dict[Tuple[int, int], int] = {}
+        self.last_use = [0] * num_slots
+        self.clock = 0
+        self.stats = CacheStats()
+
+    def _victim(self, keep: set) -> int:
+        free = [s for s in range(self.S) if self.owner[s] is None]
+        if free:
+            return free[0]
+        cands = [s for s in range(self.S) if self.owner[s] not in keep]
+        if not cands:
+            raise RuntimeError(f"slot budget {self.S} is smaller than the experts one call needs ({len(keep)})")
+        if self.policy == "lru":
+            return min(cands, key=lambda s: self.last_use[s])
+        return min(cands, key=lambda s: (self.freq.get(self.owner[s], 0.0), self.last_use[s]))
+
+    def admit(self, layer: int, experts: Sequence[int]):
+        """Returns (loads [(slot, key)], evicted keys)."""
+        keep = {(layer, int(e)) for e in experts}
+        if len(keep) > self.S:
+            raise RuntimeError(f"slot budget {self.S} is smaller than the experts one call needs ({len(keep)})")
+        loads, evicted = [], []
+        for e in sorted({int(e) for e in experts}):
+            self.clock += 1
+            key = (layer, e)
+            self.freq[key] = self.freq.get(key, 0.0) + 1.0
+            if self.clock % self.decay_every == 0:
+                self.freq = {k: v * 0.5 for k, v in self.freq.items() if v >= 1.0 / 64}
+            s = self.where.get(key)
+            if s is not None:
+                self.stats.hits += 1
+                self.last_use[s] = self.clock
+                continue
+            self.stats.misses += 1
+            self.stats.per_layer_misses[layer] = self.stats.per_layer_misses.get(layer, 0) + 1
+            s = self._victim(keep)
+            old = self.owner[s]
+            if old is not None:
+                self.stats.evictions += 1
+                del self.where[old]
+                evicted.append(old)
+            self.owner[s] = key
+            self.where[key] = s
+            self.last_use[s] = self.clock
+            loads.append((s, key))
+        return loads, evicted
+
+
 class SlotCache:
     """``num_slots`` device slots shared by every layer (the reference's per-layer
     caches sum to a slot budget too, e.g. 126 for Mixtral on 16 GB)."""
 
     def __init__(self, hidden_dim: int, intermediate_dim: int, num_layers: int, num_experts: int,
-                 num_slots: int, source: ExpertSource, device="cuda", group_size: int = 128):
-        if num_slots < 1:
-            raise ValueError("need at least one slot")
+                 num_slots: int, source: ExpertSource, device="cuda", group_size: int = 128,
+                 policy: str = "lfu", decay_every: int = 4096):
+        self.res = Residency(num_slots, policy, decay_every)
         self.H, self.F, self.L, self.E, self.S = hidden_dim, intermediate_dim, num_layers, num_experts, num_slots
         self.group_size = group_size
         self.device = torch.device(device)
@@ -107,10 +176,6 @@ class SlotCache:
         self.slot_ptrs = [[getattr(sl, n).data_ptr() for n in SLOT_TENSORS] for sl in self.slots]
         self.per_map = int(_lib.load().hn_expert_maps_bytes())
         self.slot_maps = self._encode(self.slot_ptrs)  # bytes: per slot, its three descriptors
-        self.owner: List[Optional[Tuple[int, int]]] = [None] * num_slots
-        self.where: Dict[Tuple[int, int], int] = {}
-        self.last_use = [0] * num_slots
-        self.clock = 0
         self.copy_stream = torch.cuda.Stream(self.device)
         self.loaded = [torch.cuda.Event() for _ in range(num_slots)]
         # per layer: device table [E, 6] int64 and descriptors [E * per_map], host row -> slot
@@ -118,7 +183,14 @@ class SlotCache:
         self.maps = [torch.zeros(num_experts * self.per_map + 64, dtype=torch.uint8, device=self.device)
                      for _ in range(num_layers)]
         self.row_slot = [[-1] * num_experts for _ in range(num_layers)]
-        self.stats = CacheStats()
+
+    @property
+    def stats(self) -> CacheStats:
+        return self.res.stats
+
+    @property
+    def where(self) -> Dict[Tuple[int, int], int]:
+        return self.res.where
 
     def _encode(self, rows: Sequence[Sequence[int]]) -> bytes:
         lib = _lib.load()
@@ -132,41 +204,14 @@ class SlotCache:
     def is_resident(self, layer: int, expert: int) -> bool:
         return (layer, expert) in self.where
 
-    def _victim(self, keep: set) -> int:
-        free = [s for s in range(self.S) if self.owner[s] is None]
-        if free:
-            return free[0]
-        cands = [s for s in range(self.S) if self.owner[s] not in keep]
-        if not cands:
-            raise RuntimeError(f"slot budget {self.S} is smaller than the experts one call needs ({len(keep)})")
-        return min(cands, key=lambda s: self.last_use[s])
-
     def ensure(self, layer: int, experts: Sequence[int]) -> None:
         """Make every expert in ``experts`` (of ``layer``) resident and point the
         layer's table at their slots; the current stream waits for the loads."""
         compute = torch.cuda.current_stream(self.device)
         keep = {(layer, int(e)) for e in experts}
-        loads = []
-        for e in sorted({int(e) for e in experts}):
-            self.clock += 1
-            key = (layer, e)
-            s = self.where.get(key)
-            if s is not None:
-                self.stats.hits += 1
-                self.last_use[s] = self.clock
-                continue
-            self.stats.misses += 1
-            self.stats.per_layer_misses[layer] = self.stats.per_layer_misses.get(layer, 0) + 1
-            s = self._victim(keep)
-            old = self.owner[s]
-            if old is not None:
-                self.stats.evictions += 1
-                del self.where[old]
-                self.row_slot[old[0]][old[1]] = -1
-            self.owner[s] = key
-            self.where[key] = s
-            self.last_use[s] = self.clock
-            loads.append((s, key))
+        loads, evicted = self.res.admit(layer, experts)
+        for lyr, e in evicted:
+            self.row_slot[lyr][e] = -1
         if loads:
             # nothing queued on the compute stream may still read a slot being overwritten
             self.copy_stream.wait_stream(compute)
