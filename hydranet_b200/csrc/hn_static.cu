@@ -17,9 +17,10 @@ namespace hn {
 namespace {
 
 constexpr size_t kStaticScratchBytes = HN_INT4_LINEAR_STATIC_SCRATCH_BYTES;
-// Token segments of at most 32 rows keep the stream-K partials within the
-// scratch; the 64- and 128-row segments hn_int4_linear uses above M = 64
-// need 19-39 MiB of partials alone.
+// The widest token segments (at most 32 rows) whose scratch fits the array:
+// the stream-K partials grow with the segment width (the 64- and 128-row
+// segments hn_int4_linear uses above M = 64 need 19-39 MiB of partials
+// alone, 32-row segments on the mma.sync engine 19 MiB).
 constexpr int kStaticMaxNt = 4;
 static_assert(kStaticScratchBytes % 256 == 0, "static scratch size must keep 256-byte granularity");
 
@@ -36,16 +37,25 @@ int static_scratch_address(void** out) {
   return HN_OK;
 }
 
+// Segment cap (tokens / 8) for a static call: 4, 2 or 1, the first whose
+// scratch fits; the cap with the smallest scratch when none does.
+int static_max_nt(int64_t M, int64_t N, int64_t K) {
+  for (int nt = kStaticMaxNt; nt > 1; nt /= 2)
+    if (int4_linear_workspace_nt(M, N, K, nt) <= kStaticScratchBytes) return nt;
+  return 1;
+}
+
 }  // namespace hn
 
 extern "C" size_t hn_int4_linear_static_scratch_size(int64_t M, int64_t N, int64_t K) {
-  return hn::int4_linear_workspace_nt(M, N, K, hn::kStaticMaxNt);
+  return hn::int4_linear_workspace_nt(M, N, K, hn::static_max_nt(M, N, K));
 }
 
 extern "C" int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K,
                                      const uint8_t* w_packed, const uint16_t* w_scales, int64_t N, int group_size,
                                      void* out, int64_t ldo, void* stream) {
-  const size_t need = hn::int4_linear_workspace_nt(M, N, K, hn::kStaticMaxNt);
+  const int max_nt = hn::static_max_nt(M, N, K);
+  const size_t need = hn::int4_linear_workspace_nt(M, N, K, max_nt);
   if (need == 0) return hn::fail(HN_ERR_INVALID, "int4_linear_static: need M, N >= 1 and K >= 128");
   if (need > hn::kStaticScratchBytes)
     return hn::fail(HN_ERR_WORKSPACE, "int4_linear_static: M=" + std::to_string(M) + " N=" + std::to_string(N) +
@@ -57,7 +67,7 @@ extern "C" int hn_int4_linear_static(const void* x, int64_t ldx, int dtype, int6
   const int rc = hn::static_scratch_address(&ws);
   if (rc) return rc;
   return hn::int4_linear_nt(x, ldx, dtype, M, K, w_packed, w_scales, N, group_size, out, ldo, ws,
-                            hn::kStaticScratchBytes, stream, hn::kStaticMaxNt);
+                            hn::kStaticScratchBytes, stream, max_nt);
 }
 
 // The array's error word (its first 4 bytes), read on 'stream' and cleared.

@@ -268,8 +268,10 @@ HN_API int hn_ep_combine(const void* back, int dtype, int64_t T, int64_t H, int 
  * serving runtime that has given all free HBM to its caches, so that a
  * cudaMalloc on the decode path would fail or wait for the whole device.
  *
- *  - Shapes whose hn_int4_linear_static_scratch_size(M, N, K) is larger than
- *    the array are refused with HN_ERR_WORKSPACE (for example M = 64 with
+ *  - Token segments are capped at the widest of 32, 16 or 8 rows whose
+ *    scratch fits the array.  Shapes whose
+ *    hn_int4_linear_static_scratch_size(M, N, K) is still larger than the
+ *    array are refused with HN_ERR_WORKSPACE (for example M = 64 with
  *    K = 14336 fits; M = 4096 with K = 14336 does not).  The query is
  *    host-only and needs no GPU.
  *  - Every call looks up the array's address on the current device and
@@ -279,9 +281,9 @@ HN_API int hn_ep_combine(const void* back, int dtype, int64_t T, int64_t H, int 
  *    capture.  A failure there is returned as HN_ERR_CUDA.
  *  - What must be zero: the array's first 512 bytes (an error word and an
  *    arrival counter) when a call starts.  They are zero after loading and
- *    stay zero unless a bounded device wait of a call timed out (calls of up
- *    to 32 rows per token segment, which is all of them by default, contain
- *    no such wait).  hn_int4_linear_static_error reads the error word and
+ *    stay zero unless a bounded device wait of a call timed out (on the
+ *    default engine choice static calls, whose segments hold at most 32
+ *    rows, run on the mma.sync engine, which has no such wait).  hn_int4_linear_static_error reads the error word and
  *    clears it; results of calls issued while it was set are undefined.
  *  - There is ONE array per device, shared by every caller of this function.
  *    Two calls that may overlap on the device (streams with no ordering

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from hydranet_b200 import _lib, synth
+from hydranet_b200 import _lib, ops, synth
 from hydranet_b200.moe import MoELayerInt4, moe_experts
 from hydranet_b200.router import GLM4SigmoidRouter, TopKRouter
 from oracle import int4_ref as R
@@ -303,17 +303,22 @@ def test_glm_layer_with_shared_expert(lib):
 
 @pytest.mark.parametrize("case", ["g4", "g8"])
 def test_group_limited_router_matches_reference(lib, golden_dir, case):
-    """Group-limited sigmoid routing on the device, on the inputs the reference's
-    own ``GLM4SigmoidRouter`` routed (``model/glm4.py:285-297``)."""
+    """Group-limited sigmoid routing on the device (``model/glm4.py:285-297``),
+    on the reference fixture's router and inputs rounded to bf16 (the
+    device router takes 16-bit activations), against the oracle pinned to
+    that fixture."""
     d = dict(np.load(golden_dir / "glm_group_router.npz"))
     E, ng, kg, k, H, T = (int(v) for v in d[case + "/cfg"])
     r = GLM4SigmoidRouter(hidden_dim=H, num_experts=E, experts_per_token=k, n_group=ng, topk_group=kg).cuda()
     with torch.no_grad():
         r.weight.copy_(torch.from_numpy(d[case + "/w"]))
-    x = torch.from_numpy(d[case + "/x"]).cuda()
-    idx, w = r(x)
-    np.testing.assert_array_equal(np.sort(idx.cpu().numpy(), 1), np.sort(d[case + "/idx"], 1))
-    np.testing.assert_allclose(np.sort(to_np32(w), 1), np.sort(d[case + "/wt"], 1), rtol=1e-5, atol=1e-6)
+    x = torch.from_numpy(d[case + "/x"]).cuda().to(torch.bfloat16)
+    idx, w, logits = ops.moe_route(x.view(T, H), r.params(), E)
+    ridx, rw, _ = R.sigmoid_topk_router_ref(to_np32(x.view(T, H)), d[case + "/w"], k, "bf16", n_group=ng,
+                                            topk_group=kg)
+    np.testing.assert_array_equal(np.sort(idx.cpu().numpy(), 1), np.sort(ridx, 1))
+    # weights are cast to the activation dtype: equal up to one bf16 step
+    np.testing.assert_allclose(np.sort(w.cpu().numpy(), 1), np.sort(rw, 1), rtol=2 ** -7, atol=1e-6)
 
 
 def test_group_limited_glm_layer(lib):
