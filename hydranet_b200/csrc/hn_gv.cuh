@@ -50,11 +50,8 @@ constexpr int kGvStages = 4;     // weight ring stages per warp (one k-group eac
 constexpr int kGvMaxTiles = 32;  // tiles of one CTA's step range whose metadata is cached in shared memory
 
 // Launch shape and shared-memory plan per token-tile count NT (8*NT tokens
-// per segment, NT = 1, 2 or 4): 8 warps and two CTAs per SM, four warps per
-// scheduler within 128 registers.  At NT = 4 there is no room for a second
-// fp32 fragment per group: the weights are scaled in float16 before the MMA
-// ((n - 8) * scale rounded once, the reference kernel's arithmetic) and the
-// MMAs accumulate straight into the running sums (kScaled).
+// per segment, NT = 1 or 2): 8 warps and two CTAs per SM, four warps per
+// scheduler within 128 registers.
 //   weight ring  [warp][stage][4 loads][32 lanes][16 B]  (each thread reads back only what it copied)
 //   token slices 2 x [group][4 q][8NT tokens][4 t][16 B]
 //   scale slices 2 x [group][warp][2 MMA tiles][8 g][2 h] fp16
@@ -68,12 +65,11 @@ struct GvTileMeta {
 };
 template <int NT>
 struct GvCfg {
-  static_assert(NT == 1 || NT == 2 || NT == 4, "the mma.sync engine runs segments of up to 32 tokens");
+  static_assert(NT == 1 || NT == 2, "the mma.sync engine runs segments of up to 16 tokens");
   static constexpr int W = 8;
   static constexpr int kCtasPerSm = 2;
   static constexpr int kThreads = W * 32;
-  static constexpr bool kScaled = NT == 4;
-  static constexpr int kSlice = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // k-groups per token slice (16 KB of tokens)
+  static constexpr int kSlice = NT == 1 ? 8 : 4;  // k-groups per token slice (16 KB of tokens)
   static constexpr int kStage = 2048;             // one warp's 32 rows x 64 B of a k-group
   static constexpr int kGroupBytes = 2048 * NT;
   static constexpr int kRows = W * 32;  // weight rows of a tile (both matrices): one per thread
@@ -481,27 +477,6 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
     // the pieces in CTA order, kU at a time with all their loads in flight
     // before the first add (a tile of a small step is split over up to ~10 CTAs)
     constexpr int kU = NT == 1 ? 4 : 2;
-    if constexpr (NT == 4) {
-      // 32-token tiles: no registers to spare for loads in flight
-      for (int cc = c0; cc <= c1; ++cc) {
-        const int64_t b0 = gv_begin(NS, cc, P);
-        if (b0 >= gv_begin(NS, cc + 1, P)) continue;
-        const int sl = b0 / G == tile ? 0 : 1;
-        const float4* src =
-            reinterpret_cast<const float4*>(a.part) + (((int64_t)cc * 2 + sl) * W + warp) * (2 * NT * 32);
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            const float4 q = cc == c ? make_float4(acc[mt][j][0], acc[mt][j][1], acc[mt][j][2], acc[mt][j][3])
-                                     : __ldcg(src + (mt * NT + j) * 32 + lane);
-            tot[mt][j][0] += q.x;
-            tot[mt][j][1] += q.y;
-            tot[mt][j][2] += q.z;
-            tot[mt][j][3] += q.w;
-          }
-      }
-    } else {
     for (int cb = c0; cb <= c1; cb += kU) {
       float4 q[kU][2][NT];
 #pragma unroll
@@ -539,7 +514,6 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
             }
           }
       }
-    }
     }
     epilogue(tot, tile);
   };
@@ -588,15 +562,11 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
       sc2[mt] = *reinterpret_cast<const uint32_t*>(sbuf + (sl_n & 1) * C::kSBuf + gi * (C::kRows * 2) +
                                                    ((warp * 2 + mt) * 8 + gl) * 4);
     const uint8_t* bg = bbuf + (sl_n & 1) * C::kBBuf + gi * C::kGroupBytes + lane * 16;
-    float tg[2][NT][4];  // a k-group's fresh sums (unscaled path); fix-up scratch in finish_piece
+    float tg[2][NT][4];  // a k-group's fresh sums; fix-up scratch in finish_piece
     // dequantise, multiply and fold one k-group for the segment's NTA token
     // tiles (a compile-time count, so the MMA chains of all tiles interleave)
     auto consume = [&](auto nta_c) {
       constexpr int NTA = decltype(nta_c)::value;
-      // kScaled: the two rows' scales of each MMA tile as float16 pairs
-      const uint32_t sh[2][2] = {{(sc2[0] & 0xFFFFu) | (sc2[0] << 16), (sc2[0] >> 16) | (sc2[0] & 0xFFFF0000u)},
-                                 {(sc2[1] & 0xFFFFu) | (sc2[1] << 16), (sc2[1] >> 16) | (sc2[1] & 0xFFFF0000u)}};
-      (void)sh;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint4 bv[NTA];
@@ -607,47 +577,32 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
           uint32_t lo[4], hi[4];
           dq_word(q == 0 ? wv[mt][0].x : q == 1 ? wv[mt][0].y : q == 2 ? wv[mt][0].z : wv[mt][0].w, lo);
           dq_word(q == 0 ? wv[mt][1].x : q == 1 ? wv[mt][1].y : q == 2 ? wv[mt][1].z : wv[mt][1].w, hi);
-          if constexpr (C::kScaled) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(lo[i]) : "r"(sh[mt][0]));
-              asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(hi[i]) : "r"(sh[mt][1]));
-            }
-#pragma unroll
-            for (int j = 0; j < NTA; ++j) {
-              mma_f16(acc[mt][j], lo[0], hi[0], lo[1], hi[1], bv[j].x, bv[j].y);
-              mma_f16(acc[mt][j], lo[2], hi[2], lo[3], hi[3], bv[j].z, bv[j].w);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < NTA; ++j) {
-              if (q == 0)
-                mma_f16_z(tg[mt][j], lo[0], hi[0], lo[1], hi[1], bv[j].x, bv[j].y);
-              else
-                mma_f16(tg[mt][j], lo[0], hi[0], lo[1], hi[1], bv[j].x, bv[j].y);
-              mma_f16(tg[mt][j], lo[2], hi[2], lo[3], hi[3], bv[j].z, bv[j].w);
-            }
+          for (int j = 0; j < NTA; ++j) {
+            if (q == 0)
+              mma_f16_z(tg[mt][j], lo[0], hi[0], lo[1], hi[1], bv[j].x, bv[j].y);
+            else
+              mma_f16(tg[mt][j], lo[0], hi[0], lo[1], hi[1], bv[j].x, bv[j].y);
+            mma_f16(tg[mt][j], lo[2], hi[2], lo[3], hi[3], bv[j].z, bv[j].w);
           }
         }
       }
       // fold the group into the running sums with its fp32 scales
-      if constexpr (!C::kScaled) {
-        for (int mt = 0; mt < 2; ++mt) {
-          const float s0 = __half2float(__ushort_as_half((unsigned short)(sc2[mt] & 0xFFFFu)));
-          const float s1 = __half2float(__ushort_as_half((unsigned short)(sc2[mt] >> 16)));
-          for (int j = 0; j < NTA; ++j) {
-            acc[mt][j][0] = fmaf(s0, tg[mt][j][0], acc[mt][j][0]);
-            acc[mt][j][1] = fmaf(s0, tg[mt][j][1], acc[mt][j][1]);
-            acc[mt][j][2] = fmaf(s1, tg[mt][j][2], acc[mt][j][2]);
-            acc[mt][j][3] = fmaf(s1, tg[mt][j][3], acc[mt][j][3]);
-          }
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const float s0 = __half2float(__ushort_as_half((unsigned short)(sc2[mt] & 0xFFFFu)));
+        const float s1 = __half2float(__ushort_as_half((unsigned short)(sc2[mt] >> 16)));
+#pragma unroll
+        for (int j = 0; j < NTA; ++j) {
+          acc[mt][j][0] = fmaf(s0, tg[mt][j][0], acc[mt][j][0]);
+          acc[mt][j][1] = fmaf(s0, tg[mt][j][1], acc[mt][j][1]);
+          acc[mt][j][2] = fmaf(s1, tg[mt][j][2], acc[mt][j][2]);
+          acc[mt][j][3] = fmaf(s1, tg[mt][j][3], acc[mt][j][3]);
         }
       }
     };
     if (NT == 1 || nta <= 1)
       consume(std::integral_constant<int, 1>{});
-    else if (NT == 4 && nta == 2)
-      consume(std::integral_constant<int, 2>{});
     else
       consume(std::integral_constant<int, NT>{});
     cur_slot = cur_slot + 1 == S ? 0 : cur_slot + 1;

@@ -1877,9 +1877,11 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* R, const int*
 static int pick_nt(int64_t T, int64_t K, int64_t E) {
   if (T <= 8) return 1;
   if (T <= 64) {
-    // decode: 16-token segments while experts get at most 4 assignments on
-    // average (few experts ever reach 16), else 16 (T <= 16) or 32 tokens
+    // decode: 8-token segments while experts get at most 2 assignments on
+    // average (GLM-4.5 at 32 tokens: hardly any expert reaches 9), 16-token
+    // ones up to 4 on average (or T <= 16), else 32 tokens
     const int64_t avg = T * K / std::max<int64_t>(E, 1);
+    if (avg <= 2) return 1;
     return (avg <= 4 || T <= 16) ? 2 : 4;
   }
   const int64_t avg = T * K / std::max<int64_t>(E, 1);
@@ -1904,7 +1906,7 @@ static int encode_token_map(CUtensorMap* data, const void* base, int64_t rows, i
 // tensor pipe is four times wider (at 24-32 tokens per segment the mma.sync
 // pipe, not HBM, would bound the phase).
 static std::atomic<int> g_decode_engine{HN_ENGINE_AUTO};
-static int gv_nt(int nt) { return nt <= 1 ? 1 : (nt == 2 ? 2 : 4); }
+static int gv_nt(int nt) { return nt <= 1 ? 1 : 2; }
 // CTAs of an mma.sync engine launch (two per SM)
 static int gv_grid(int nt) {
   const int sms = sm_count_current();
@@ -1922,7 +1924,7 @@ static bool gv_fits(int nt, int64_t max_segs, int64_t rows, bool gateup) {
   const int64_t tiles = max_segs * ((rows + tile_rows - 1) / tile_rows);
   return tiles / gv_grid(nt) + 3 <= kGvMaxTiles;
 }
-static bool use_gv(int nt) { return nt <= 4 && g_decode_engine.load(std::memory_order_relaxed) != HN_ENGINE_TCGEN05; }
+static bool use_gv(int nt) { return nt <= 2 && g_decode_engine.load(std::memory_order_relaxed) != HN_ENGINE_TCGEN05; }
 // Bytes of stream-K partials an mma.sync engine launch may write.
 static size_t gv_part_bytes(int nt) {
   return (size_t)gv_grid(nt) * 2 * gv_warps(nt) * 2 * gv_nt(nt) * 32 * 16;
@@ -1956,8 +1958,7 @@ static int launch_gv_t(const GvArgs& a, cudaStream_t s) {
 template <typename Tr, int KIND, int EPI>
 static int launch_gv(int nt, const GvArgs& a, cudaStream_t s) {
   if (nt <= 1) return launch_gv_t<Tr, 1, KIND, EPI>(a, s);
-  if (nt == 2) return launch_gv_t<Tr, 2, KIND, EPI>(a, s);
-  return launch_gv_t<Tr, 4, KIND, EPI>(a, s);
+  return launch_gv_t<Tr, 2, KIND, EPI>(a, s);
 }
 
 // The mma.sync engine's arguments for the phase the tcgen05 engine's

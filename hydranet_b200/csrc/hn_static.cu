@@ -20,7 +20,7 @@ constexpr size_t kStaticScratchBytes = HN_INT4_LINEAR_STATIC_SCRATCH_BYTES;
 // The widest token segments (at most 32 rows) whose scratch fits the array:
 // the stream-K partials grow with the segment width (the 64- and 128-row
 // segments hn_int4_linear uses above M = 64 need 19-39 MiB of partials
-// alone, 32-row segments on the mma.sync engine 19 MiB).
+// alone).
 constexpr int kStaticMaxNt = 4;
 static_assert(kStaticScratchBytes % 256 == 0, "static scratch size must keep 256-byte granularity");
 

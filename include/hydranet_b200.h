@@ -281,9 +281,9 @@ HN_API int hn_ep_combine(const void* back, int dtype, int64_t T, int64_t H, int 
  *    capture.  A failure there is returned as HN_ERR_CUDA.
  *  - What must be zero: the array's first 512 bytes (an error word and an
  *    arrival counter) when a call starts.  They are zero after loading and
- *    stay zero unless a bounded device wait of a call timed out (on the
- *    default engine choice static calls, whose segments hold at most 32
- *    rows, run on the mma.sync engine, which has no such wait).  hn_int4_linear_static_error reads the error word and
+ *    stay zero unless a bounded device wait of a call timed out (segments of
+ *    up to 16 rows run on the mma.sync engine, which has no such wait; the
+ *    tcgen05 engine's waits are bounded).  hn_int4_linear_static_error reads the error word and
  *    clears it; results of calls issued while it was set are undefined.
  *  - There is ONE array per device, shared by every caller of this function.
  *    Two calls that may overlap on the device (streams with no ordering
