@@ -53,6 +53,10 @@ SIGNATURES = {
     "hn_expert_mlp_int4": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "hn_moe_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int]),
+    "hn_moe_experts_workspace_size_expected": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int, c_int64]),
+    "hn_moe_experts_int4_expected": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p,
+                                             c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_size_t,
+                                             c_void_p]),
     "hn_moe_layer_launches": (c_int, [c_int64, c_int64, c_int64, c_int64, c_int]),
     "hn_expert_maps_bytes": (c_size_t, []),
     "hn_expert_maps_encode": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p]),

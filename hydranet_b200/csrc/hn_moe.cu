@@ -2342,12 +2342,20 @@ struct MoECall {
   cudaStream_t stream;
   bool run_experts;
   int phase;  // 0: all; 1: prep only; 2: gate/up engine only; 3: down engine only
+  int64_t expected;  // caller routing: slots expected to hold an expert (0: all T*topk)
 };
+
+// Segment width of a call: from the tokens whose slots are expected to hold an
+// expert (a caller-routed block of which only some slots are this call's).
+static int call_nt(int64_t T, int topk, int64_t E, int64_t expected) {
+  const int64_t t_eff = expected > 0 ? std::max<int64_t>(1, std::min<int64_t>(T, expected / topk)) : T;
+  return pick_nt(t_eff, topk, E);
+}
 
 template <typename Tr>
 static int run_moe(const MoECall& m) {
   const int64_t TK = m.T * m.topk;
-  const int nt = pick_nt(m.T, m.topk, m.E);
+  const int nt = call_nt(m.T, m.topk, m.E, m.expected);
   const int P = grid_p(nt);
   // routed calls always scale by the routing weight and combine; the identity
   // plan of a single expert MLP stores rows directly
@@ -2502,8 +2510,13 @@ using namespace hn;
 extern "C" {
 
 size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int top_k) {
-  if (T < 1 || H < 128 || F < 128 || E < 1 || top_k < 1) return 0;
-  const int nt = pick_nt(T, top_k, E);
+  return hn_moe_experts_workspace_size_expected(T, H, F, E, top_k, 0);
+}
+
+size_t hn_moe_experts_workspace_size_expected(int64_t T, int64_t H, int64_t F, int64_t E, int top_k,
+                                              int64_t expected_assignments) {
+  if (T < 1 || H < 128 || F < 128 || E < 1 || top_k < 1 || expected_assignments < 0) return 0;
+  const int nt = call_nt(T, top_k, E, expected_assignments);
   return make_layout(T, H, E, top_k, F, H, nt, grid_p(nt), true).total() + 256;
 }
 
@@ -2594,8 +2607,17 @@ int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t 
                         const int32_t* topk_idx, const float* topk_w, const hn_expert_ptrs* experts,
                         const void* expert_maps, void* out,
                         void* workspace, size_t workspace_bytes, void* stream) {
+  return hn_moe_experts_int4_expected(x, dtype, T, H, F, E, top_k, topk_idx, topk_w, experts, expert_maps, out, 0,
+                                      workspace, workspace_bytes, stream);
+}
+
+int hn_moe_experts_int4_expected(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int top_k,
+                                 const int32_t* topk_idx, const float* topk_w, const hn_expert_ptrs* experts,
+                                 const void* expert_maps, void* out, int64_t expected_assignments,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_dims(T, H, F, E);
   if (rc) return rc;
+  HN_REQUIRE(expected_assignments >= 0, "expected_assignments must be >= 0");
   HN_REQUIRE(top_k >= 1 && top_k <= E && top_k <= kMaxTopK, "top_k out of range");
   HN_REQUIRE(x && topk_idx && topk_w && experts && expert_maps && out && workspace,
              "hn_moe_experts_int4: null pointer");
@@ -2620,6 +2642,7 @@ int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, int64_t 
   m.ws_bytes = workspace_bytes;
   m.stream = (cudaStream_t)stream;
   m.run_experts = true;
+  m.expected = expected_assignments;
   return dispatch_moe(m);
 }
 

@@ -152,14 +152,16 @@ def ep_moe_forward_chunked(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, 
     return out
 
 
-def cuda_local_fn(table):
+def cuda_local_fn(table, world: int = 1):
     """Step 3 on the GPU: the grouped kernel over the received rows with their
     top-k local ids and weights (-1 slots take no work; all -1 rows are
-    skipped)."""
+    skipped).  About 1/world of the slots are this rank's, which sets the
+    kernel's token-segment width (``expected_assignments``)."""
     from .moe import moe_experts
 
     def fn(rows: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
-        return moe_experts(rows, ids, weights, table)
+        expected = (rows.shape[0] * ids.shape[1] + world - 1) // max(world, 1)
+        return moe_experts(rows, ids, weights, table, expected_assignments=expected)
 
     return fn
 
@@ -187,7 +189,7 @@ class ExpertParallelMoE(torch.nn.Module):
         world = dist.get_world_size(group)
         if local_table is not None and len(local_table) * world != num_experts:
             raise ValueError("local expert table size times world size must equal the number of experts")
-        self.local_fn = local_fn if local_fn is not None else cuda_local_fn(local_table)
+        self.local_fn = local_fn if local_fn is not None else cuda_local_fn(local_table, world)
 
     def route(self, x: torch.Tensor):
         """int32 top-k ids and float32 weights of x [T, H] (one device routing launch)."""

@@ -98,7 +98,9 @@ class MoELayerInt4(nn.Module):
         return out.view(shape)
 
 
-def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts: ExpertTable) -> torch.Tensor:
-    """Experts + weighted combine for externally routed tokens (x [T, H])."""
+def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts: ExpertTable,
+                expected_assignments: int = 0) -> torch.Tensor:
+    """Experts + weighted combine for externally routed tokens (x [T, H]);
+    ``expected_assignments`` as in ``ops.moe_experts``."""
     return ops.moe_experts(x, topk_idx, topk_w, experts.device_table, experts.device_maps, len(experts),
-                           experts.intermediate_dim)
+                           experts.intermediate_dim, expected_assignments)

@@ -201,8 +201,10 @@ def moe_layer_phases(x: torch.Tensor, params: _lib.RouterParams, expert_table: t
 
 
 def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, expert_table: torch.Tensor,
-                expert_maps: torch.Tensor, num_experts: int, ffn: int) -> torch.Tensor:
-    """Experts + combine with caller-supplied routing (int32 idx, float32 weights)."""
+                expert_maps: torch.Tensor, num_experts: int, ffn: int, expected_assignments: int = 0) -> torch.Tensor:
+    """Experts + combine with caller-supplied routing (int32 idx, float32 weights).
+    ``expected_assignments``: the caller's estimate of the slots that hold an
+    expert when most are -1 (expert-parallel rows); it picks the segment width."""
     T, H = x.shape
     k = topk_idx.shape[1]
     out = torch.empty_like(x)
@@ -211,10 +213,10 @@ def moe_experts(x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, e
     topk_idx = topk_idx.to(torch.int32).contiguous()
     topk_w = topk_w.to(torch.float32).contiguous()
     lib = load()
-    need = lib.hn_moe_workspace_size(T, H, ffn, num_experts, k)
+    need = lib.hn_moe_experts_workspace_size_expected(T, H, ffn, num_experts, k, expected_assignments)
     ws = _lib.workspaces.get(need, x.device)
     with torch.cuda.device(x.device):
-        check(lib.hn_moe_experts_int4(ptr(x), _act_dtype(x), T, H, ffn, num_experts, k, ptr(topk_idx), ptr(topk_w),
-                                      expert_table.data_ptr(), expert_maps.data_ptr(), ptr(out), ptr(ws), ws.numel(),
-                                      stream_ptr(x.device)))
+        check(lib.hn_moe_experts_int4_expected(ptr(x), _act_dtype(x), T, H, ffn, num_experts, k, ptr(topk_idx),
+                                               ptr(topk_w), expert_table.data_ptr(), expert_maps.data_ptr(), ptr(out),
+                                               int(expected_assignments), ptr(ws), ws.numel(), stream_ptr(x.device)))
     return out

@@ -216,6 +216,22 @@ HN_API int hn_moe_experts_int4(const void* x, int dtype, int64_t T, int64_t H, i
                         const hn_expert_ptrs* experts, const void* expert_maps, void* out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* hn_moe_experts_int4 for a block of rows of which only some slots hold an
+ * expert (no counterpart in the reference: the rows an expert-parallel
+ * exchange delivers, where about T * top_k / W of the slots are this rank's):
+ * expected_assignments (> 0) is the caller's estimate of the slots that hold
+ * an expert, from which the token-segment width is chosen instead of
+ * T * top_k (0: the same as hn_moe_experts_int4).  The result does not depend
+ * on the estimate, only the speed; the workspace is sized by
+ * hn_moe_experts_workspace_size_expected with the same estimate. */
+HN_API size_t hn_moe_experts_workspace_size_expected(int64_t T, int64_t H, int64_t F, int64_t E, int top_k,
+                                                     int64_t expected_assignments);
+HN_API int hn_moe_experts_int4_expected(const void* x, int dtype, int64_t T, int64_t H, int64_t F, int64_t E,
+                                        int top_k, const int32_t* topk_idx, const float* topk_w,
+                                        const hn_expert_ptrs* experts, const void* expert_maps, void* out,
+                                        int64_t expected_assignments, void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
 /* Router only: writes topk_idx/topk_w (and logits if non-NULL). */
 HN_API int hn_moe_route(const void* x, int dtype, int64_t T, int64_t H, int64_t E,
                  const hn_router_params* router, int32_t* topk_idx, float* topk_w, float* logits,

@@ -38,7 +38,7 @@ def _setup():
     return _STATE["s"]
 
 
-@pytest.mark.parametrize("world", [2, 8])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_emulated_ranks_match_single_gpu_layer(lib, world):
     from hydranet_b200 import ops
     slots, router, full = _setup()
@@ -54,7 +54,8 @@ def test_emulated_ranks_match_single_gpu_layer(lib, world):
     ys = []
     for d in range(world):
         rows, ids, wts = ex.unpack(recvs[d], H, K, torch.bfloat16)
-        ys.append(cuda_local_fn(ExpertTable(slots[d * per:(d + 1) * per]))(rows, ids, wts))
+        # the local call is told that about 1/world of the slots are this rank's
+        ys.append(cuda_local_fn(ExpertTable(slots[d * per:(d + 1) * per]), world)(rows, ids, wts))
     for r in range(world):
         back = torch.stack([ys[d][r * T:(r + 1) * T] for d in range(world)])
         out = ex.combine(back, idxs[r], E, world)
