@@ -27,9 +27,15 @@
 // Per thread (lane = 4*g + t) and k-group: row g and row g+8 of each of its
 // two 16-row MMA tiles; for each row the 16 bytes at 16*t of the group (k
 // 32t..32t+31).  Word q of those bytes (k 32t+8q..+7) becomes the A
-// registers of MMA k-steps 2q and 2q+1: the exponent-magic conversion gives
-// the float16 pairs (k0,k4), (k2,k6) [low nibbles] and (k1,k5), (k3,k7) [high
-// nibbles] of the word, exactly n - 8.  The token operand is stored so that
+// registers of MMA k-steps 2q and 2q+1: OR-ing the nibbles into the mantissa
+// of 1024.0 gives the float16 pairs (k0,k4), (k2,k6) = 1024 + n [low
+// nibbles, even k] and (k1,k5), (k3,k7) = 1024 + 16n [high nibbles, odd k],
+// exact integers, fed to the tensor core as they are (four instructions and
+// a shift per word).  The staged tokens hold x at even k and b = x / 16 at
+// odd k, so the products are (1024 + n) x = (n - 8) x + 1032 x and
+// (1024 + 16n) b = (n - 8) x + 1152 b: the group's MMA sum exceeds the wanted
+// sum by 1032 * sum_even x + 1152 * sum_odd b, the per-token correction
+// staged beside the tokens (gv_offset_correction), subtracted in the fold.  The token operand is stored so that
 // one 16-byte shared load per (q, 8 tokens) yields the matching B registers:
 // unit (q, t) of a token is the staged unit 4t+q of its k-group (the pair
 // order above), at [q][token][t] inside the group.  Each k-group's MMAs
@@ -78,7 +84,9 @@ struct GvCfg {
   static constexpr int kSBuf = kSlice * kRows * 2;
   static constexpr int kMeta = kGvMaxTiles * (int)sizeof(GvTileMeta<NT>);
   static constexpr int kMisc = 256;
-  static constexpr int kTotal = kWRing + 2 * kBBuf + 2 * kSBuf + kMeta + kMisc;
+  static constexpr int kCBuf = kSlice * 8 * NT * 4;  // offset corrections of a slice's tokens
+  static constexpr int kCRed = W * 8 * NT * 4;       // gate/up epilogue: per-warp correction partials
+  static constexpr int kTotal = kWRing + 2 * kBBuf + 2 * kSBuf + kMeta + kMisc + 2 * kCBuf + kCRed;
   static_assert(kTotal * kCtasPerSm <= 227 * 1024, "gv shared-memory plan exceeds the SM");
 };
 
@@ -111,6 +119,8 @@ struct GvArgs {
   const int* tidx;  // [T*K] expert of each slot, -1 = unused
   int defer_combine;
   int early;  // KIND_DOWN right after a gate/up launch: the plan is visible at entry, the staged rows later
+  const float* corr_b;  // [staged row][G] offset correction of each staged row's k-groups
+  float* corr_out;      // KIND_GATEUP: [assignment][rows / 128] corrections of the staged SiLU(gate)*up
   int P;
 };
 
@@ -142,6 +152,21 @@ __device__ __forceinline__ void dq_word(uint32_t w, uint32_t (&o)[4]) {
   asm("add.rn.f16x2 %0, %0, %1;" : "+r"(o[1]) : "r"(0xE408E408u));
   asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(o[2]) : "r"(0x2C002C00u), "r"(0xD480D480u));
   asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(o[3]) : "r"(0x2C002C00u), "r"(0xD480D480u));
+}
+
+// Eight packed nibbles -> the float16 pairs 1024 + n (even k) and 1024 + 16n
+// (odd k) in the staged pair order, exact; the offsets are removed by the
+// per-group correction.  Five instructions.
+__device__ __forceinline__ void dq_word_offset(uint32_t w, uint32_t (&o)[4]) {
+  const uint32_t w8 = w >> 8;
+  o[0] = lop3_and_or<0x000F000Fu>(w, 0x64006400u);
+  o[1] = lop3_and_or<0x000F000Fu>(w8, 0x64006400u);
+  o[2] = lop3_and_or<0x00F000F0u>(w, 0x64006400u);
+  o[3] = lop3_and_or<0x00F000F0u>(w8, 0x64006400u);
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
 
 // Weight stream: read once per layer, so it bypasses L1 and is evict-first in L2.
@@ -200,6 +225,8 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
   uint8_t* const sbuf = bbuf + 2 * C::kBBuf;
   Meta* const meta = reinterpret_cast<Meta*>(sbuf + 2 * C::kSBuf);
   int* const s_misc = reinterpret_cast<int*>(sbuf + 2 * C::kSBuf + C::kMeta);  // [0] flag, [1] count, [2..] tokens
+  float* const cbuf = reinterpret_cast<float*>(sbuf + 2 * C::kSBuf + C::kMeta + C::kMisc);  // [2][kSlice][8NT]
+  float* const cred = cbuf + 2 * (C::kCBuf / 4);                                             // [W][8NT]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gl = lane >> 2, tq = lane & 3;
   const int c = blockIdx.x, P = gridDim.x;
@@ -310,6 +337,13 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
           if (gi < gs) cp_async16(dst + gi * C::kGroupBytes, src + gi * kChunk);
       }
     }
+    // the tokens' offset corrections of the slice's groups: [gi][n]
+    if (tid < 8 * NT * C::kSlice) {
+      const int n = tid / C::kSlice, gi = tid - n * C::kSlice;
+      if (n < mi.m && gi < gs)
+        cp_async4(smem_u32(cbuf + bufi * (C::kCBuf / 4) + gi * 8 * NT + n),
+                  a.corr_b + (int64_t)mi.rows[n] * G + g0 + gi);
+    }
   };
   // scales of a slice: thread tid holds tile row tid's scales in registers
   uint32_t sreg[C::kSlice];
@@ -369,7 +403,16 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
   auto epilogue = [&](const float (&v)[2][NT][4], int tile) {
     const int rt = tile % a.tps;
     if (KIND == KIND_GATEUP) {
+      // SiLU(gate)*up staged for the down phase as the prep kernel stages
+      // tokens (odd k divided by 16), and per token the offset correction of
+      // this tile's 128 rows -- one k-group of the down phase: the thread's
+      // rows (all of k's parity, that of gl), the 8 lanes of its tq, then the
+      // warps in order, so the sum does not depend on timing
       const int f0 = rt * (16 * W) + warp * 16 + gl;
+      const bool odd = gl & 1;
+      float cpart[NT][2];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) cpart[j][0] = cpart[j][1] = 0.f;
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
         if (j >= nta) break;
@@ -379,10 +422,27 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
           const int f = f0 + 8 * (e >> 1);
           if (n < seg_m && f < a.rows) {
             const float hv = silu_f(v[0][j][e]) * v[1][j][e];
+            const __half h = __float2half_rn(odd ? hv * 0.0625f : hv);
             *reinterpret_cast<__half*>(a.hp + (int64_t)(seg_first + n) * a.hp_rstride + (f >> 7) * kChunk +
-                                       staged_offset(f & 127)) = __float2half_rn(hv);
+                                       staged_offset(f & 127)) = h;
+            cpart[j][e & 1] += __half2float(h);
           }
         }
+      }
+      __syncthreads();  // cred of the previous tile has been read
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float c = odd ? gv_offset_correction(0.f, cpart[j][u]) : gv_offset_correction(cpart[j][u], 0.f);
+          for (int o = 4; o < 32; o <<= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+          if (gl == 0) cred[warp * 8 * NT + 8 * j + 2 * tq + u] = c;
+        }
+      __syncthreads();
+      if (tid < seg_m) {
+        float c = 0.f;
+        for (int w = 0; w < W; ++w) c += cred[w * 8 * NT + tid];
+        a.corr_out[(int64_t)(seg_first + tid) * (a.rows / 128) + rt] = c;
       }
     } else {
       const int r0 = rt * (32 * W) + warp * 32 + gl;
@@ -575,8 +635,8 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
           uint32_t lo[4], hi[4];
-          dq_word(q == 0 ? wv[mt][0].x : q == 1 ? wv[mt][0].y : q == 2 ? wv[mt][0].z : wv[mt][0].w, lo);
-          dq_word(q == 0 ? wv[mt][1].x : q == 1 ? wv[mt][1].y : q == 2 ? wv[mt][1].z : wv[mt][1].w, hi);
+          dq_word_offset(q == 0 ? wv[mt][0].x : q == 1 ? wv[mt][0].y : q == 2 ? wv[mt][0].z : wv[mt][0].w, lo);
+          dq_word_offset(q == 0 ? wv[mt][1].x : q == 1 ? wv[mt][1].y : q == 2 ? wv[mt][1].z : wv[mt][1].w, hi);
 #pragma unroll
           for (int j = 0; j < NTA; ++j) {
             if (q == 0)
@@ -587,17 +647,20 @@ __global__ void __launch_bounds__(GvCfg<NT>::kThreads, GvCfg<NT>::kCtasPerSm)
           }
         }
       }
-      // fold the group into the running sums with its fp32 scales
+      // fold the group into the running sums: minus the tokens' offset
+      // corrections, times the rows' fp32 scales
+      const float* cg = cbuf + (sl_n & 1) * (C::kCBuf / 4) + gi * 8 * NT + 2 * tq;
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         const float s0 = __half2float(__ushort_as_half((unsigned short)(sc2[mt] & 0xFFFFu)));
         const float s1 = __half2float(__ushort_as_half((unsigned short)(sc2[mt] >> 16)));
 #pragma unroll
         for (int j = 0; j < NTA; ++j) {
-          acc[mt][j][0] = fmaf(s0, tg[mt][j][0], acc[mt][j][0]);
-          acc[mt][j][1] = fmaf(s0, tg[mt][j][1], acc[mt][j][1]);
-          acc[mt][j][2] = fmaf(s1, tg[mt][j][2], acc[mt][j][2]);
-          acc[mt][j][3] = fmaf(s1, tg[mt][j][3], acc[mt][j][3]);
+          const float2 cr = *reinterpret_cast<const float2*>(cg + 8 * j);
+          acc[mt][j][0] = fmaf(s0, tg[mt][j][0] - cr.x, acc[mt][j][0]);
+          acc[mt][j][1] = fmaf(s0, tg[mt][j][1] - cr.y, acc[mt][j][1]);
+          acc[mt][j][2] = fmaf(s1, tg[mt][j][2] - cr.x, acc[mt][j][2]);
+          acc[mt][j][3] = fmaf(s1, tg[mt][j][3] - cr.y, acc[mt][j][3]);
         }
       }
     };

@@ -61,6 +61,8 @@ struct Plan {
   int* n_assign; // [1] assignments planned (T*K less the -1 slots)
   uint8_t* xp;   // [T][K_in/128][kChunk]    staged activations (token-major)
   uint8_t* hp;   // [T*K][F/128][kChunk]     staged SiLU(gate)*up (assignment-major)
+  float* corr_x; // [T][K_in/128]  offset staging: per (token, k-group) correction of the mma.sync engine
+  float* corr_h; // [T*K][F/128]   the same for hp
   uint8_t* xs;   // [T*K][K_in/128][kChunk]  staged activations in assignment order (large routings), or NULL
   float* part1;  // stream-K partial tiles, phase 1
   float* part2;  // stream-K partial tiles, phase 2
@@ -90,6 +92,16 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 __device__ __forceinline__ uint4 pack_unit(const float (&v)[8]) {
   return make_uint4(pack_h2(v[0], v[4]), pack_h2(v[2], v[6]), pack_h2(v[1], v[5]), pack_h2(v[3], v[7]));
 }
+// Offset staging for the mma.sync engine: it feeds the tensor core the
+// exponent-magic values 1024 + n (even k) and 1024 + 16n (odd k) as they
+// are, so the odd k of the tokens are staged divided by 16 and each
+// (token, k-group) carries the sum the offsets add:
+//   sum_k (w_k - 8) b_k = MMA - (1032 * sum_even b + 1152 * sum_odd b)
+// with b the staged float16 values (odd ones already divided by 16).
+__device__ __forceinline__ float gv_offset_correction(float sum_even, float sum_odd) {
+  return 1032.f * sum_even + 1152.f * sum_odd;
+}
+
 // Byte offset of k (0..127) inside a staged chunk: unit k / 8, then the
 // position of i = k % 8 in the order above (i with its three bits reversed).
 __device__ __forceinline__ int staged_offset(int k) {
@@ -122,6 +134,7 @@ struct RouteArgs {
   float* out_w;
   float* out_logits;
   int seg;
+  int gv_stage;  // 1: stage for the mma.sync engine (odd k divided by 16, per-group corrections)
   const float* pre_logits;  // [T][E] router logits from router_logits_kernel, or NULL: computed here
   int wbuf_off;    // byte offset of the router-weight chunk in dynamic shared memory
   int plan_here;   // 1: the last CTA builds the plan; 0: plan_kernel runs after this kernel
@@ -191,13 +204,30 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   }
   __syncthreads();
 
-  // 1. staged activations
-  for (int u = tid; u < a.H / 8; u += 256) {
+  // 1. staged activations.  For the mma.sync engine (gv_stage) the odd k are
+  // stored divided by 16 and each k-group gets its offset correction
+  // (gv_offset_correction): the engine multiplies by 1024 + n and 1024 + 16n.
+  // Lanes 16h..16h+15 of a warp hold the 16 units of one k-group.
+  for (int u0 = 0; u0 < a.H / 8; u0 += 256) {
+    const int u = u0 + tid;
+    const bool ok = u < a.H / 8;
     const int g = u >> 4, ch = u & 15;
     float v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = xs[g * 128 + ch * 8 + i];
-    *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)t * (a.H / 128) + g) * kChunk + ch * 16) = pack_unit(v);
+    for (int i = 0; i < 8; ++i) v[i] = ok ? xs[g * 128 + ch * 8 + i] : 0.f;
+    if (a.gv_stage) {
+      float ce = 0.f, co = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        v[i + 1] *= 0.0625f;
+        ce += __half2float(__float2half_rn(v[i]));
+        co += __half2float(__float2half_rn(v[i + 1]));
+      }
+      float c = gv_offset_correction(ce, co);
+      for (int o = 8; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+      if (ok && ch == 0) a.plan.corr_x[(int64_t)t * (a.H / 128) + g] = c;
+    }
+    if (ok) *reinterpret_cast<uint4*>(a.plan.xp + ((int64_t)t * (a.H / 128) + g) * kChunk + ch * 16) = pack_unit(v);
   }
 
   // 2. routing for this token
@@ -1136,6 +1166,9 @@ struct EngineArgs {
   int allow_rr;       // whole tiles round-robin over the CTAs when there are >= 4 per CTA (prefill sizes)
   int64_t max_segs;   // segments the plan can hold (bounds the tiles of an mma.sync engine CTA)
   int max_nt;         // tokens per segment / 8
+  int gv;             // this call runs on the mma.sync engine (decided once for all its phases)
+  float* corr_x;      // offset corrections of the staged activations / SiLU(gate)*up (mma.sync engine)
+  float* corr_h;
 };
 
 template <int KIND>
@@ -1982,6 +2015,8 @@ static GvArgs gv_args(const EngineArgs& e, int KIND) {
   g.bsrc = e.bsrc;
   g.b_rstride = e.b_rstride;
   g.b_by_token = KIND == KIND_GATEUP ? 1 : e.b_use_tok;  // gate/up reads x by token (xp), down its own rows
+  g.corr_b = g.b_by_token ? e.corr_x : e.corr_h;          // offset corrections of those staged rows
+  g.corr_out = KIND == KIND_GATEUP ? e.corr_h : nullptr;  // gate/up stages hp and its corrections
   g.hp = e.hp;
   g.hp_rstride = e.hp_rstride;
   g.R = e.R;
@@ -2035,8 +2070,7 @@ static int launch_engine_t(const EngineArgs& a, cudaStream_t s) {
 
 template <typename Tr, int KIND, int EPI>
 static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
-  if (use_gv(nt) && gv_fits(nt, a.max_segs, a.N, KIND == KIND_GATEUP))
-    return launch_gv<Tr, KIND, EPI>(nt, gv_args(a, KIND), s);
+  if (a.gv) return launch_gv<Tr, KIND, EPI>(nt, gv_args(a, KIND), s);
   if (nt <= 2) return launch_engine_t<Tr, 16, KIND, EPI>(a, s);
   if (nt <= 4) return launch_engine_t<Tr, 32, KIND, EPI>(a, s);
   if (nt <= 8) return launch_engine_t<Tr, 64, KIND, EPI>(a, s);
@@ -2054,9 +2088,10 @@ static int launch_engine(int nt, const EngineArgs& a, cudaStream_t s) {
 // call, because another shape's data section may have covered them.
 struct Layout {
   size_t err, route_ctr, ctr1, ctr2, rtctr, counters;                                     // front
-  size_t counts, n_segs, segs, n_segs2, segs2, a_tok, a_tk, a_w, pos, idx, wts, nval, n_assign, xp, hp, xs, part1, part2, R,
+  size_t counts, n_segs, segs, n_segs2, segs2, a_tok, a_tk, a_w, pos, idx, wts, nval, n_assign, corr_x, corr_h, xp, hp, xs, part1, part2, R,
       rlog, data;  // back (relative)
   bool has_rlog, has_xs;
+  bool gv;           // the call runs on the mma.sync engine (every phase, offset staging)
   int seg2;          // second segment cut for the down phase (0: none)
   int64_t max_segs;  // segments the plan can hold
   size_t total() const { return counters + data; }
@@ -2104,13 +2139,17 @@ static Layout make_layout(int64_t T, int64_t Kin, int64_t E, int topk, int64_t F
   l.wts = take(4 * TK);
   l.nval = take(4 * T);
   l.n_assign = take(4);
+  l.corr_x = take((size_t)4 * (Kin / 128) * T);
+  l.corr_h = take(F ? (size_t)4 * (F / 128) * TK : 0);
   l.xp = take((size_t)(Kin / 128) * T * kChunk);
   l.hp = take(F ? (size_t)(F / 128) * TK * kChunk : 0);
   // routed gate/up tokens staged in assignment order, read by TMA instead of
   // gathered token by token: pays for its extra copy from a mean of 12
   // assignments per expert (e.g. Mixtral at 64 tokens) and 32-token segments
-  const bool gv_gateup = F && use_gv(nt) && gv_fits(nt, max_segs, F, true);
-  l.has_xs = F && combine && nt >= 4 && TK >= 12 * E && !gv_gateup;
+  // one engine for every phase of a call: the mma.sync engine when each
+  // phase's tile table fits it (its staging differs from the tcgen05 engine's)
+  l.gv = use_gv(nt) && gv_fits(nt, max_segs, N2, false) && (!F || gv_fits(nt, max_segs, F, true));
+  l.has_xs = F && combine && nt >= 4 && TK >= 12 * E && !l.gv;
   l.xs = take(l.has_xs ? (size_t)(Kin / 128) * TK * kChunk : 0);
   // tcgen05 engine: [CTA][2 slots][fold warp][N][32] fp32 with N >= 16; the
   // mma.sync engine: [CTA][2 slots][warp][2 MMA tiles][NT][32 lanes][4] fp32
@@ -2151,6 +2190,8 @@ static Plan plan_at(void* ws, size_t ws_bytes, const Layout& l) {
   p.wts = reinterpret_cast<float*>(d + l.wts);
   p.nval = reinterpret_cast<int*>(d + l.nval);
   p.n_assign = reinterpret_cast<int*>(d + l.n_assign);
+  p.corr_x = reinterpret_cast<float*>(d + l.corr_x);
+  p.corr_h = reinterpret_cast<float*>(d + l.corr_h);
   p.xp = d + l.xp;
   p.hp = d + l.hp;
   p.xs = l.has_xs ? d + l.xs : nullptr;
@@ -2393,6 +2434,7 @@ static int run_moe(const MoECall& m) {
   ra.out_logits = m.out_logits;
   ra.seg = seg_tokens(nt);
   ra.plan = plan;
+  ra.gv_stage = m.run_experts && l.gv;
   // a route-only call (hn_moe_route) runs no expert phase, so nothing would
   // read the assignment-ordered copy of the tokens: skip making it
   if (!m.run_experts) ra.plan.xs = nullptr;
@@ -2447,6 +2489,9 @@ static int run_moe(const MoECall& m) {
   e1.max_nt = nt;
   e1.nval = plan.nval;
   e1.tidx = plan.idx;
+  e1.gv = l.gv;
+  e1.corr_x = plan.corr_x;
+  e1.corr_h = plan.corr_h;
   if (m.phase == 0 || m.phase == 2) rc = launch_engine<Tr, KIND_GATEUP, EPI_COMBINE>(nt, e1, m.stream);
   if (rc || m.phase == 2) return rc;
 
@@ -2752,6 +2797,7 @@ int int4_linear_nt(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   ra.mode = ROUTE_IDENTITY;
   ra.seg = seg_tokens(nt);
   ra.plan = plan;
+  ra.gv_stage = l.gv;
   EngineArgs e{};
   e.K = (int)K;
   e.G = (int)(K / 128);
@@ -2788,6 +2834,9 @@ int int4_linear_nt(const void* x, int64_t ldx, int dtype, int64_t M, int64_t K, 
   e.max_nt = nt;
   e.nval = plan.nval;
   e.tidx = plan.idx;
+  e.gv = l.gv;
+  e.corr_x = plan.corr_x;
+  e.corr_h = plan.corr_h;
   int rc;
   if (dtype == HN_DTYPE_BF16) {
     rc = launch_route<BF16>(ra, s);
