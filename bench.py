@@ -789,8 +789,25 @@ def glm_c4(args, dev, world, rank, barrier, max_over_ranks):
                 step(i)
             ev1.record()
             torch.cuda.synchronize(dev)
-        ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+        ms_graph = max_over_ranks(ev0.elapsed_time(ev1) / args.steps) if graphs else None
         barrier()
+        # the same steps launched eagerly (with NCCL all-to-alls, replaying the
+        # captured graphs is not always the faster way): device time, max over ranks
+        for i in range(args.warmup):
+            layers[i % G_LAYERS](xs[i % G_LAYERS])
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev2.record()
+        for i in range(args.steps):
+            layers[i % G_LAYERS](xs[i % G_LAYERS])
+        ev3.record()
+        torch.cuda.synchronize(dev)
+        ms_eager = max_over_ranks(ev2.elapsed_time(ev3) / args.steps)
+        barrier()
+        ms = min(ms_eager, ms_graph) if ms_graph is not None else ms_eager
+        mode = "cuda_graph" if ms_graph is not None and ms_graph <= ms_eager else "eager"
         captured = bool(graphs)
         # graphs holding NCCL work are released before the process group goes
         for gr in graphs or []:
@@ -820,7 +837,8 @@ def glm_c4(args, dev, world, rank, barrier, max_over_ranks):
     res = {"workload": G_WORKLOAD, "n_gpus": world, "tokens_per_gpu": G_T, "hidden": G_H, "moe_ffn": G_F,
            "experts": G_E, "experts_per_gpu": per, "top_k": G_K, "router": "sigmoid top-8, correction bias",
            "layers_rotated": G_LAYERS, "ms_per_step": ms, "tok_s": world * G_T / (ms * 1e-3),
-           "cuda_graph": captured, "parity_rel_l2": parity, "index_match": index_match,
+           "cuda_graph": mode == "cuda_graph", "launch_mode": mode, "ms_graph": ms_graph, "ms_eager": ms_eager,
+           "captured": captured, "parity_rel_l2": parity, "index_match": index_match,
            "touched_experts_per_gpu": statistics.mean(touched),
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                         "peak_kind": peak_kind, "algo_bytes_per_gpu_step": algo,
