@@ -40,6 +40,7 @@ class RouterParams(ctypes.Structure):
 # name -> (restype, argtypes)
 SIGNATURES = {
     "hn_abi_version": (c_int, []),
+    "hn_set_sm_limit": (c_int, [c_int]),
     "hn_last_error": (ctypes.c_char_p, []),
     "hn_device_sm_count": (c_int, [c_int]),
     "hn_quantize_int4": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p]),

@@ -1,5 +1,6 @@
 // Error plumbing, device queries, the INT4 packer/unpacker/dequantiser and the
 // elementwise SiLU*mul kernel.
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <unordered_map>
@@ -24,7 +25,9 @@ int check_cuda(cudaError_t e, const char* what) {
   return fail(HN_ERR_CUDA, m);
 }
 
-int sm_count_current() {
+static std::atomic<int> g_sm_limit{0};  // hn_set_sm_limit (0: none)
+
+static int sm_count_device() {
   static std::mutex mu;
   static std::unordered_map<int, int> cache;
   int dev = 0;
@@ -36,6 +39,13 @@ int sm_count_current() {
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
   cache[dev] = n;
   return n;
+}
+
+// SMs the engines size their grids for: the device's, or fewer under hn_set_sm_limit.
+int sm_count_current() {
+  const int n = sm_count_device();
+  const int lim = g_sm_limit.load(std::memory_order_relaxed);
+  return (n > 0 && lim > 0 && lim < n) ? lim : n;
 }
 
 // ---------------------------------------------------------------------------
@@ -146,6 +156,11 @@ int hn_device_sm_count(int device) {
     return 0;
   }
   return n;
+}
+
+int hn_set_sm_limit(int max_sms) {
+  if (max_sms < 0) return -1;
+  return hn::g_sm_limit.exchange(max_sms);
 }
 
 int hn_quantize_int4(const void* w, int w_dtype, int64_t rows, int64_t cols, int group_size, uint8_t* packed,

@@ -118,12 +118,24 @@ def ep_moe_forward(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_expe
 
 def ep_moe_forward_chunked(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, num_experts: int,
                            local_fn: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor],
-                           chunk: int, group=None, exchange=None) -> torch.Tensor:
+                           chunk: int, group=None, exchange=None, reserve_sms: int = 16) -> torch.Tensor:
     """``ep_moe_forward`` over micro-batches of ``chunk`` tokens with the
     all-to-alls issued asynchronously (every rank must pass the same T and
-    chunk: the ranks take the same collective steps in the same order)."""
+    chunk: the ranks take the same collective steps in the same order).  On
+    the GPU the grouped kernels leave ``reserve_sms`` SMs free meanwhile
+    (``hn_set_sm_limit``) so that NCCL's all-to-all kernels can run beside
+    them."""
     if chunk <= 0:
         raise ValueError("chunk must be positive")
+    if x.is_cuda and reserve_sms > 0:
+        from . import _lib
+        lib = _lib.load()
+        sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+        prev = lib.hn_set_sm_limit(max(1, sms - reserve_sms))
+        try:
+            return ep_moe_forward_chunked(x, idx, w, num_experts, local_fn, chunk, group, exchange, 0)
+        finally:
+            lib.hn_set_sm_limit(prev)
     ex = exchange if exchange is not None else CudaExchange()
     world = dist.get_world_size(group)
     T, H = x.shape

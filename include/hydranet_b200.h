@@ -333,6 +333,16 @@ HN_API int hn_int4_linear_static_error(int* error_code, void* stream);
 enum hn_engine { HN_ENGINE_AUTO = 0, HN_ENGINE_TCGEN05 = 1 };
 HN_API int hn_set_decode_engine(int engine);
 
+/* Grids of the grouped kernels are sized for at most max_sms SMs from the
+ * next call on (0: all of the device's; process-wide; returns the previous
+ * limit, or -1 for a negative argument).  No counterpart in the reference.
+ * The persistent kernels otherwise hold every SM for their whole run, so a
+ * collective issued beside them (an expert-parallel exchange on NCCL's
+ * stream) cannot start until they end; leaving a few SMs free lets it run
+ * alongside.  Results do not depend on the limit; workspaces sized under one
+ * limit serve calls under any smaller one. */
+HN_API int hn_set_sm_limit(int max_sms);
+
 /* Device-side error word of a workspace (bounded waits that timed out set it).
  * Copies 4 bytes device->host on 'stream' and synchronises that stream. */
 HN_API int hn_workspace_error(const void* workspace, size_t workspace_bytes, int* error_code, void* stream);

@@ -155,3 +155,13 @@ def test_moe_layer_launch_count_query():
     assert lib.hn_moe_layer_launches(32, 4096, 1408, 128, 8) == 4  # + the router GEMV (128 x 4096 router)
     assert lib.hn_moe_layer_launches(0, 4096, 14336, 8, 2) == 0
     assert lib.hn_moe_layer_launches(4, 64, 14336, 8, 2) == 0
+
+
+def test_sm_limit_setter():
+    lib = _lib.load()
+    prev = lib.hn_set_sm_limit(100)
+    try:
+        assert lib.hn_set_sm_limit(90) == 100
+        assert lib.hn_set_sm_limit(-3) == -1
+    finally:
+        lib.hn_set_sm_limit(prev)

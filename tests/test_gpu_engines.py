@@ -147,3 +147,25 @@ def test_given_routing_duplicates_and_unused_engines(lib):
     ref = R.moe_combine_ref(to_np32(x)[keep], ii, ww, oracle_experts(packed))
     assert rel_l2(a, ref) <= TIGHT["bf16"]
     assert rel_l2(b, ref) <= TIGHT["bf16"]
+
+
+@pytest.mark.parametrize("T", [8, 64, 300])
+def test_sm_limit_same_results(lib, T):
+    """Grids sized for fewer SMs (hn_set_sm_limit, as the expert-parallel
+    prefill does to leave room for NCCL) compute the same layer."""
+    shape = synth.MoEShape(1024, 2048, 8, 2)
+    table, packed = _table("m", shape, 31)
+    r = TopKRouter(hidden_dim=1024, num_experts=8, experts_per_token=2).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        r.gate.weight.copy_(torch.randn(8, 1024, generator=torch.Generator("cuda").manual_seed(7), device="cuda") * 0.02)
+    layer = MoELayerInt4(r, table)
+    x = torch.randn(T, 1024, generator=torch.Generator("cuda").manual_seed(T), device="cuda").to(torch.bfloat16)
+    lib_ = _lib.load()
+    with torch.no_grad():
+        a = layer(x)
+        prev = lib_.hn_set_sm_limit(100)
+        try:
+            b = layer(x)
+        finally:
+            lib_.hn_set_sm_limit(prev)
+    assert rel_l2(to_np32(a), to_np32(b)) <= ENGINE_AGREE
