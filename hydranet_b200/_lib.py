@@ -41,6 +41,11 @@ class RouterParams(ctypes.Structure):
 SIGNATURES = {
     "hn_abi_version": (c_int, []),
     "hn_set_sm_limit": (c_int, [c_int]),
+    "hn_slots_create": (c_void_p, [c_int, c_int, c_int64]),
+    "hn_slots_destroy": (None, [c_void_p]),
+    "hn_slots_admit": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+    "hn_slots_lookup": (c_int, [c_void_p, c_int, c_int]),
+    "hn_slots_stats": (c_int, [c_void_p, c_void_p]),
     "hn_last_error": (ctypes.c_char_p, []),
     "hn_device_sm_count": (c_int, [c_int]),
     "hn_quantize_int4": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p]),

@@ -14,7 +14,8 @@ async H2D copies through pinned staging (``PinnedStagingRing`` and
   once; a layer's expert table (``hn_expert_ptrs`` rows + descriptors) is
   rebuilt on the host from the slot numbers of its resident experts and
   uploaded as one small copy when residency changes;
-* eviction picks, among the slots whose expert the current call does not
+* the residency decisions are the library's host-side table (``hn_slots_*``,
+  C++): eviction picks, among the slots whose expert the current call does not
   need, the least frequently used one (policy "lfu", the default: a use
   count per (layer, expert) that halves every ``decay_every`` uses of the
   cache, ties to the least recent -- the frequency idea of the reference's
@@ -90,12 +91,15 @@ class CacheStats:
 
 
 class Residency:
-    """Which (layer, expert) lives in which of ``num_slots`` slots; host only.
+    """Which (layer, expert) lives in which of ``num_slots`` slots: the
+    library's host-side residency table (``hn_slots_*``, C++), with a Python
+    mirror of the placement for lookups.
 
     ``admit(layer, experts)`` makes the given experts resident, evicting by
     the policy among the slots the call does not need, and returns the
-    loads to make as (slot, key) pairs; it never evicts an expert of the same
-    call and refuses a call that needs more experts than there are slots."""
+    loads to make as (slot, key) pairs and the evicted keys; it never evicts
+    an expert of the same call and refuses a call that needs more experts
+    than there are slots (nothing changes then)."""
 
     def __init__(self, num_slots: int, policy: str = "lfu", decay_every: int = 4096):
         if num_slots < 1:
@@ -104,54 +108,41 @@ class Residency:
             raise ValueError("policy must be 'lfu' or 'lru'")
         self.S = num_slots
         self.policy = policy
-        self.decay_every = decay_every
-        self.freq: Dict[Tuple[int, int], float] = {}
-        self.owner: List[Optional[Tuple[int, int]]] = [None] * num_slots
+        self._lib = _lib.load()
+        self._h = self._lib.hn_slots_create(num_slots, 0 if policy == "lfu" else 1, decay_every)
+        if not self._h:
+            raise ValueError("hn_slots_create refused the arguments")
+        self._loads = (ctypes.c_int32 * (2 * num_slots))()
+        self._evicted = (ctypes.c_int32 * (2 * num_slots))()
+        self._n_ev = ctypes.c_int(0)
+        self._st = (ctypes.c_int64 * 3)()
         self.where: Dict[Tuple[int, int], int] = {}
-        self.last_use = [0] * num_slots
-        self.clock = 0
         self.stats = CacheStats()
 
-    def _victim(self, keep: set) -> int:
-        free = [s for s in range(self.S) if self.owner[s] is None]
-        if free:
-            return free[0]
-        cands = [s for s in range(self.S) if self.owner[s] not in keep]
-        if not cands:
-            raise RuntimeError(f"slot budget {self.S} is smaller than the experts one call needs ({len(keep)})")
-        if self.policy == "lru":
-            return min(cands, key=lambda s: self.last_use[s])
-        return min(cands, key=lambda s: (self.freq.get(self.owner[s], 0.0), self.last_use[s]))
+    def __del__(self):
+        h, self._h = getattr(self, "_h", None), None
+        if h:
+            self._lib.hn_slots_destroy(h)
 
     def admit(self, layer: int, experts: Sequence[int]):
         """Returns (loads [(slot, key)], evicted keys)."""
-        keep = {(layer, int(e)) for e in experts}
-        if len(keep) > self.S:
-            raise RuntimeError(f"slot budget {self.S} is smaller than the experts one call needs ({len(keep)})")
-        loads, evicted = [], []
-        for e in sorted({int(e) for e in experts}):
-            self.clock += 1
-            key = (layer, e)
-            self.freq[key] = self.freq.get(key, 0.0) + 1.0
-            if self.clock % self.decay_every == 0:
-                self.freq = {k: v * 0.5 for k, v in self.freq.items() if v >= 1.0 / 64}
-            s = self.where.get(key)
-            if s is not None:
-                self.stats.hits += 1
-                self.last_use[s] = self.clock
-                continue
-            self.stats.misses += 1
-            self.stats.per_layer_misses[layer] = self.stats.per_layer_misses.get(layer, 0) + 1
-            s = self._victim(keep)
-            old = self.owner[s]
-            if old is not None:
-                self.stats.evictions += 1
-                del self.where[old]
-                evicted.append(old)
-            self.owner[s] = key
-            self.where[key] = s
-            self.last_use[s] = self.clock
-            loads.append((s, key))
+        es = [int(e) for e in experts]
+        arr = (ctypes.c_int32 * max(1, len(es)))(*es)
+        nl = self._lib.hn_slots_admit(self._h, layer, arr, len(es), self._loads, self._evicted,
+                                      ctypes.byref(self._n_ev))
+        if nl < 0:
+            raise RuntimeError(f"slot budget {self.S} is smaller than the experts one call needs "
+                               f"({len({e for e in es if e >= 0})})")
+        evicted = [(self._evicted[2 * i], self._evicted[2 * i + 1]) for i in range(self._n_ev.value)]
+        loads = [(self._loads[2 * i], (layer, self._loads[2 * i + 1])) for i in range(nl)]
+        for key in evicted:
+            self.where.pop(key, None)
+        for slot, key in loads:
+            self.where[key] = slot
+        self._lib.hn_slots_stats(self._h, self._st)
+        self.stats.hits, self.stats.misses, self.stats.evictions = self._st[0], self._st[1], self._st[2]
+        if nl:
+            self.stats.per_layer_misses[layer] = self.stats.per_layer_misses.get(layer, 0) + nl
         return loads, evicted
 
 

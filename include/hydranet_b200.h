@@ -343,6 +343,34 @@ HN_API int hn_set_decode_engine(int engine);
  * limit serve calls under any smaller one. */
 HN_API int hn_set_sm_limit(int max_sms);
 
+/* ---------------------------------------------------------------------------
+ * Expert slot residency (host only, launches nothing): which (layer, expert)
+ * occupies which of num_slots device slots of an over-budget expert cache.
+ * The reference keeps this bookkeeping in Python per layer
+ * (cache/expert_cache.py, ExpertCacheManager's tiers); here one table serves
+ * all layers.  hn_slots_admit makes the n given experts of `layer` resident
+ * (ids < 0 are ignored, duplicates count once, processed in ascending id
+ * order): it writes one (slot, expert) pair per expert to load into `loads`
+ * and one (layer, expert) pair per evicted expert into `evicted` (each at
+ * most 2 * num_slots ints), sets *n_evicted and returns the number of loads;
+ * a call needing more experts than there are slots changes nothing and
+ * returns -HN_ERR_WORKSPACE.  Eviction takes, among the slots the call does
+ * not need, a free one, else the least frequently used (HN_SLOTS_LFU: a use
+ * count per (layer, expert), halved every decay_every uses, ties to the least
+ * recent) or the least recently used (HN_SLOTS_LRU); ties to the lower slot.
+ * Thread-safe per handle.  No counterpart in the reference's C API.
+ * ------------------------------------------------------------------------- */
+enum hn_slots_policy { HN_SLOTS_LFU = 0, HN_SLOTS_LRU = 1 };
+typedef struct hn_slots hn_slots;
+HN_API hn_slots* hn_slots_create(int num_slots, int policy, int64_t decay_every);
+HN_API void hn_slots_destroy(hn_slots* slots);
+HN_API int hn_slots_admit(hn_slots* slots, int layer, const int32_t* experts, int n, int32_t* loads,
+                          int32_t* evicted, int* n_evicted);
+/* Slot of (layer, expert), or -1 when it is not resident. */
+HN_API int hn_slots_lookup(hn_slots* slots, int layer, int expert);
+/* hits, misses and evictions so far, into out3[0..2]. */
+HN_API int hn_slots_stats(hn_slots* slots, int64_t* out3);
+
 /* Device-side error word of a workspace (bounded waits that timed out set it).
  * Copies 4 bytes device->host on 'stream' and synchronises that stream. */
 HN_API int hn_workspace_error(const void* workspace, size_t workspace_bytes, int* error_code, void* stream);

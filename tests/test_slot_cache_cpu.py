@@ -56,3 +56,26 @@ def _stream_hit_rate(policy, seed=3):
 def test_lfu_beats_lru_on_a_zipf_stream():
     lfu, lru = _stream_hit_rate("lfu"), _stream_hit_rate("lru")
     assert lfu > lru + 0.05, (lfu, lru)
+
+
+def test_native_table_lookup_and_refusal_through_the_c_abi():
+    """The C ABI of the residency table directly: loads, lookups, duplicates
+    and -1 ids, and a too-large call that changes nothing."""
+    import ctypes
+    from hydranet_b200 import _lib
+    lib = _lib.load()
+    h = lib.hn_slots_create(2, 1, 4096)  # LRU
+    try:
+        loads, ev, nev = (ctypes.c_int32 * 4)(), (ctypes.c_int32 * 4)(), ctypes.c_int(0)
+        ids = (ctypes.c_int32 * 4)(5, -1, 5, 3)
+        assert lib.hn_slots_admit(h, 2, ids, 4, loads, ev, ctypes.byref(nev)) == 2 and nev.value == 0
+        assert list(loads) == [0, 3, 1, 5]          # ascending ids: 3 -> slot 0, 5 -> slot 1
+        assert lib.hn_slots_lookup(h, 2, 5) == 1 and lib.hn_slots_lookup(h, 1, 5) == -1
+        big = (ctypes.c_int32 * 3)(7, 8, 9)
+        assert lib.hn_slots_admit(h, 2, big, 3, loads, ev, ctypes.byref(nev)) == -_lib.HN_ERR_WORKSPACE
+        st = (ctypes.c_int64 * 3)()
+        lib.hn_slots_stats(h, st)
+        assert list(st) == [0, 2, 0]
+        assert lib.hn_slots_create(0, 0, 1) is None
+    finally:
+        lib.hn_slots_destroy(h)
