@@ -849,9 +849,53 @@ def glm_c4(args, dev, world, rank, barrier, max_over_ranks):
            "clocks": clk.summary()}
     if note and rank == 0:
         res["graph_note"] = note
+    if world > 1:
+        res["phases_ms"] = ep_phase_times(layers[0], xs[0], max(3, min(args.steps, 20)), max_over_ranks, barrier)
     del layers, routers, xs
     torch.cuda.empty_cache()
     return res
+
+
+def ep_phase_times(layer, x, steps, max_over_ranks, barrier) -> dict:
+    """Where an expert-parallel decode step spends its time: the steps of
+    ``ep_moe_forward`` launched eagerly with CUDA events between them
+    (device time per phase, mean over steps, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from hydranet_b200.ep import CudaExchange
+
+    ex = CudaExchange()
+    world = dist.get_world_size(layer.group)
+    T, H = x.shape
+    names = ("route", "pack", "dispatch_all_to_all", "unpack", "local_experts", "return_all_to_all", "combine")
+    sums = dict.fromkeys(names, 0.0)
+    torch.cuda.synchronize()
+    barrier()
+    with torch.no_grad():
+        for _ in range(steps):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+            ev[0].record()
+            idx, w = layer.route(x)
+            ev[1].record()
+            send = ex.pack(x, idx, w, layer.num_experts, world)
+            ev[2].record()
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=layer.group)
+            ev[3].record()
+            rows, ids, wts = ex.unpack(recv, H, idx.shape[1], x.dtype)
+            ev[4].record()
+            y = layer.local_fn(rows, ids, wts).contiguous()
+            ev[5].record()
+            back = torch.empty_like(y)
+            dist.all_to_all_single(back, y, group=layer.group)
+            ev[6].record()
+            ex.combine(back.view(world, T, H), idx, layer.num_experts, world)
+            ev[7].record()
+            torch.cuda.synchronize()
+            for i, n in enumerate(names):
+                sums[n] += ev[i].elapsed_time(ev[i + 1])
+    barrier()
+    return {n: max_over_ranks(v / steps) for n, v in sums.items()}
 
 
 # ---------------------------------------------------------------------------
