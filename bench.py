@@ -858,8 +858,10 @@ def glm_c4(args, dev, world, rank, barrier, max_over_ranks):
 
 def ep_phase_times(layer, x, steps, max_over_ranks, barrier) -> dict:
     """Where an expert-parallel decode step spends its time: the steps of
-    ``ep_moe_forward`` launched eagerly with CUDA events between them
-    (device time per phase, mean over steps, max over ranks)."""
+    ``ep_moe_forward`` launched eagerly with CUDA events between them, all
+    steps queued before one synchronisation so the GPU runs ahead of the
+    host (device time per phase, mean over steps, max over ranks; a phase
+    whose launch the host could not issue in time also counts the wait)."""
     import torch
     import torch.distributed as dist
     from hydranet_b200.ep import CudaExchange
@@ -871,9 +873,11 @@ def ep_phase_times(layer, x, steps, max_over_ranks, barrier) -> dict:
     sums = dict.fromkeys(names, 0.0)
     torch.cuda.synchronize()
     barrier()
+    all_ev = []
     with torch.no_grad():
         for _ in range(steps):
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+            all_ev.append(ev)
             ev[0].record()
             idx, w = layer.route(x)
             ev[1].record()
@@ -891,9 +895,10 @@ def ep_phase_times(layer, x, steps, max_over_ranks, barrier) -> dict:
             ev[6].record()
             ex.combine(back.view(world, T, H), idx, layer.num_experts, world)
             ev[7].record()
-            torch.cuda.synchronize()
-            for i, n in enumerate(names):
-                sums[n] += ev[i].elapsed_time(ev[i + 1])
+    torch.cuda.synchronize()
+    for ev in all_ev:
+        for i, n in enumerate(names):
+            sums[n] += ev[i].elapsed_time(ev[i + 1])
     barrier()
     return {n: max_over_ranks(v / steps) for n, v in sums.items()}
 
