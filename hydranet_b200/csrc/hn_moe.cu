@@ -36,7 +36,11 @@ constexpr int kChunk = 256;  // bytes per (token, k-group): 16 units of 16 B (12
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 32;
 constexpr int kPlanSmemEntries = 4096;  // routing entries the plan builder copies into shared memory
-constexpr int kPlanRankEntries = 1024;  // up to this many, assignment positions are counted directly
+// Routings of up to this many (token, slot) entries are planned by the prep
+// kernel's last CTA, which counts each assignment's rank directly; larger
+// ones by plan_kernel (one CTA per expert), whose cost does not grow with
+// experts x tokens.
+constexpr int kPlanRankEntries = 1024;
 
 enum { KIND_GATEUP = 0, KIND_DOWN = 1 };
 enum { EPI_COMBINE = 0, EPI_STORE = 1 };
@@ -537,43 +541,20 @@ __global__ void __launch_bounds__(256) route_prep_kernel(const RouteArgs a) {
   // positions past the planned assignments (left by skipped tokens) name
   // token 0, so a copy over all T*K positions stays in bounds
   for (int p = s_idx[0] + tid; p < TK; p += 256) a.plan.a_tok[p] = 0;
-  if (in_smem && TK <= kPlanRankEntries) {
-    // per-expert assignment order: by token, then by top-k slot -- the rank of
-    // assignment i among its expert's is the count of earlier ones with the
-    // same expert (a token listing an expert twice gets two slots)
-    for (int i = tid; i < TK; i += 256) {
-      const int e = pidx[i];
-      if (e < 0) continue;
-      int r = 0;
-      for (int j = 0; j < i; ++j) r += pidx[j] == e;
-      const int p = off[e] + r;
-      a.plan.pos[i] = p;
-      a.plan.a_tok[p] = i / a.K;
-      a.plan.a_tk[p] = i;
-      a.plan.a_w[p] = pwts[i];
-    }
-    return;
-  }
-  // per-expert assignment order: by token, then by top-k slot (ballot over 32
-  // tokens at a time); a token listing the same expert twice gets two slots
-  for (int e = warp; e < a.E; e += 8) {
-    int base = 0;
-    for (int t0 = 0; t0 < a.T; t0 += 32) {
-      const int tt = t0 + lane;
-      for (int k = 0; k < a.K; ++k) {
-        const int64_t at = (int64_t)tt * a.K + k;
-        const bool hit = tt < a.T && (in_smem ? pidx[at] : __ldcg(a.plan.idx + at)) == e;
-        const unsigned bal = __ballot_sync(0xffffffffu, hit);
-        if (hit) {
-          const int p = off[e] + base + __popc(bal & ((1u << lane) - 1u));
-          a.plan.pos[(int64_t)tt * a.K + k] = p;
-          a.plan.a_tok[p] = tt;
-          a.plan.a_tk[p] = (int)at;
-          a.plan.a_w[p] = in_smem ? pwts[at] : __ldcg(a.plan.wts + at);
-        }
-        base += __popc(bal);
-      }
-    }
+  // per-expert assignment order: by token, then by top-k slot -- the rank of
+  // assignment i among its expert's is the count of earlier ones with the
+  // same expert (a token listing an expert twice gets two slots); routings
+  // planned here hold at most kPlanRankEntries entries, all in shared memory
+  for (int i = tid; i < TK; i += 256) {
+    const int e = pidx[i];
+    if (e < 0) continue;
+    int r = 0;
+    for (int j = 0; j < i; ++j) r += pidx[j] == e;
+    const int p = off[e] + r;
+    a.plan.pos[i] = p;
+    a.plan.a_tok[p] = i / a.K;
+    a.plan.a_tk[p] = i;
+    a.plan.a_w[p] = pwts[i];
   }
 }
 
@@ -2220,7 +2201,8 @@ template <typename Tr>
 static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   const int64_t TK = (int64_t)ra.T * ra.K;
   RouteArgs r = ra;
-  size_t sm = (size_t)(ra.H + 2 * ra.E) * 4 + (TK <= kPlanSmemEntries ? (size_t)TK * 8 : 0);
+  // the routing copy of the last CTA's planner (routings it plans)
+  size_t sm = (size_t)(ra.H + 2 * ra.E) * 4 + (TK <= kPlanRankEntries ? (size_t)TK * 8 : 0);
   sm = std::max(sm, (size_t)(2 * ra.E) * 4);
   sm = (sm + 15) & ~(size_t)15;
   r.wbuf_off = (int)sm;
@@ -2234,7 +2216,7 @@ static int launch_route(const RouteArgs& ra, cudaStream_t s) {
   HN_REQUIRE(sm <= 227 * 1024, "router: hidden size too large for the shared-memory plan");
   if (sm > 48 * 1024)
     HN_CUDA(cudaFuncSetAttribute(route_prep_kernel<Tr>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-  r.plan_here = TK <= kPlanSmemEntries;
+  r.plan_here = TK <= kPlanRankEntries;
   if (gemm && std::is_same<Tr, BF16>::value && ra.H % kRtK == 0) {
     static std::atomic<bool> attr_tc[64] = {};  // per device; setting it twice is harmless
     int dev = 0;
@@ -2574,7 +2556,7 @@ int hn_moe_layer_launches(int64_t T, int64_t H, int64_t F, int64_t E, int top_k)
   // router_logits_kernel (from kRouterGemmMinT tokens, when x and the router
   // rows are 16-byte aligned) or router_gemv_kernel (routers of more than 32 Ki weights)
   n += T >= kRouterGemmMinT || router_gemv_wanted(H, E);
-  n += big;         // plan_kernel
+  n += T * top_k > kPlanRankEntries;  // plan_kernel
   n += l.has_xs;    // stage_rows_kernel
   n += big;         // combine_kernel
   return n;

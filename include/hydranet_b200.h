@@ -166,8 +166,8 @@ HN_API size_t hn_moe_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, 
  * tokens (when x and the router rows are 16-byte aligned) or when the router
  * has more than 32 Ki weights (E * H > 32768, e.g. GLM-4.5's 128 x 4096), the
  * assignment-ordered token copy when experts get >= 12 assignments on average
- * on the tcgen05 engine, and the multi-CTA planner and the combine pass above
- * 4096 (token, slot) pairs. */
+ * on the tcgen05 engine, the multi-CTA planner above 1024 (token, slot)
+ * pairs and the combine pass above 4096. */
 HN_API int hn_moe_layer_launches(int64_t T, int64_t H, int64_t F, int64_t E, int top_k);
 
 /* TMA descriptors of an expert table (what the grouped ops stream weights

@@ -141,7 +141,7 @@ def test_moe_layer_launch_count_query():
     where the library adds kernels, at the GLM prefill shape, and for sizes
     the layer rejects."""
     lib = _lib.load()
-    want = {1: 3, 16: 3, 32: 3, 64: 4, 255: 4, 256: 5, 2048: 5, 2049: 7, 8192: 7}
+    want = {1: 3, 16: 3, 32: 3, 64: 4, 255: 4, 256: 5, 512: 5, 513: 6, 2048: 6, 2049: 7, 8192: 7}
     assert {T: lib.hn_moe_layer_launches(T, 4096, 14336, 8, 2) for T in want} == want
     # the engine choice does not change the count at decode sizes
     prev = lib.hn_set_decode_engine(_lib.HN_ENGINE_TCGEN05)
