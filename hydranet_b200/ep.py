@@ -167,12 +167,15 @@ def ep_moe_forward_chunked(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, 
 def cuda_local_fn(table, world: int = 1):
     """Step 3 on the GPU: the grouped kernel over the received rows with their
     top-k local ids and weights (-1 slots take no work; all -1 rows are
-    skipped).  About 1/world of the slots are this rank's, which sets the
-    kernel's token-segment width (``expected_assignments``)."""
+    skipped).  About 1/world of the slots are this rank's; the kernel's
+    token-segment width is chosen for half that (``expected_assignments``):
+    measured on one B200 at the GLM-4.5 2-, 4- and 8-rank decode shapes, the
+    narrower segments of the mma.sync engine were as fast or up to 12 %
+    faster than the widths the mean occupancy gives."""
     from .moe import moe_experts
 
     def fn(rows: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
-        expected = (rows.shape[0] * ids.shape[1] + world - 1) // max(world, 1)
+        expected = max(1, rows.shape[0] * ids.shape[1] // (2 * max(world, 1)))
         return moe_experts(rows, ids, weights, table, expected_assignments=expected)
 
     return fn
