@@ -860,8 +860,9 @@ def ep_phase_times(layer, x, steps, max_over_ranks, barrier) -> dict:
     """Where an expert-parallel decode step spends its time: the steps of
     ``ep_moe_forward`` launched eagerly with CUDA events between them, all
     steps queued before one synchronisation so the GPU runs ahead of the
-    host (device time per phase, mean over steps, max over ranks; a phase
-    whose launch the host could not issue in time also counts the wait)."""
+    host (device time per phase, median over steps -- a one-off stall of
+    one step does not count -- max over ranks; a phase whose launch the host
+    could not issue in time also counts the wait)."""
     import torch
     import torch.distributed as dist
     from hydranet_b200.ep import CudaExchange
@@ -870,7 +871,7 @@ def ep_phase_times(layer, x, steps, max_over_ranks, barrier) -> dict:
     world = dist.get_world_size(layer.group)
     T, H = x.shape
     names = ("route", "pack", "dispatch_all_to_all", "unpack", "local_experts", "return_all_to_all", "combine")
-    sums = dict.fromkeys(names, 0.0)
+    times = {n: [] for n in names}
     torch.cuda.synchronize()
     barrier()
     all_ev = []
@@ -898,9 +899,9 @@ def ep_phase_times(layer, x, steps, max_over_ranks, barrier) -> dict:
     torch.cuda.synchronize()
     for ev in all_ev:
         for i, n in enumerate(names):
-            sums[n] += ev[i].elapsed_time(ev[i + 1])
+            times[n].append(ev[i].elapsed_time(ev[i + 1]))
     barrier()
-    return {n: max_over_ranks(v / steps) for n, v in sums.items()}
+    return {n: max_over_ranks(statistics.median(v)) for n, v in times.items()}
 
 
 # ---------------------------------------------------------------------------
