@@ -856,6 +856,14 @@ def glm_c4(args, dev, world, rank, barrier, max_over_ranks):
     return res
 
 
+def ep_step_launches(world: int) -> int:
+    """Library kernels of one expert-parallel config-4 step: the router GEMV
+    and routing, pack, unpack, the local grouped call's prep, gate/up and
+    down (on the mma.sync engine at these shapes), the multi-CTA planner when
+    the received block holds more than 1024 slots, and the combine."""
+    return 8 + (world * G_T * G_K > 1024)
+
+
 def ep_phase_times(layer, x, steps, max_over_ranks, barrier) -> dict:
     """Where an expert-parallel decode step spends its time: the steps of
     ``ep_moe_forward`` launched eagerly with CUDA events between them, all
@@ -977,7 +985,7 @@ def main():
                            "cuda_graph": g["cuda_graph"],
                            "parallelism": f"ep{world} (experts sharded, NCCL all-to-all, one row per token and rank)"},
                 "roofline": {**g["roofline"], "traffic": None},
-                "e2e": g["e2e"], "gpu_launches": 8 * args.steps, "clocks": g["clocks"],
+                "e2e": g["e2e"], "gpu_launches": ep_step_launches(world) * args.steps, "clocks": g["clocks"],
                 "parity_rel_l2": g["parity_rel_l2"], "index_match": g["index_match"], "glm_c4": g,
                 "prefill_ep": pf, "cpu_baseline": None,
             }
